@@ -1,0 +1,409 @@
+"""Benchmark of the fused MoE MLP hot path on B200.
+
+Workload (default, N=1): the Mixtral-8x7B-shaped MoE layer — T=4096 tokens,
+H=4096, I=14336, E=8 experts, top-2, bf16, uniform softmax routing of
+N(0,1) logits, activations N(0,1), weights N(0,0.02) (seeded synthetic data).
+One step = one call of the top-k fused_moe_mlp (align -> gather -> gate_up
+GEMM + SwiGLU -> down GEMM + weighted combine -> bf16) over the resident batch.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config NAME]
+
+With N > 1 (torchrun) every rank runs the expert-parallel layer on its own
+T tokens (weak scaling): experts are sharded E/N per rank and tokens travel
+to their experts and back with NCCL all-to-all (mail_b200.ep).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+CONFIGS = {
+    "mixtral": dict(T=4096, H=4096, I=14336, E=8, k=2, routing="uniform-softmax", dtype="bf16", quant=False,
+                    desc="Mixtral-8x7B MoE layer"),
+    "tiny": dict(T=64, H=1024, I=512, E=8, k=2, routing="uniform-softmax", dtype="fp32", quant=False,
+                 desc="tiny fp32 MoE MLP"),
+    "qwen3-decode": dict(T=256, H=2048, I=768, E=128, k=8, routing="zipf1.2", dtype="bf16", quant=False,
+                         desc="Qwen3-30B-A3B decode (T=256)"),
+    "dsv3-w8a8": dict(T=8192, H=7168, I=2048, E=256, k=8, routing="sigmoid", dtype="bf16", quant=True,
+                      desc="DeepSeek-V3 prefill w8a8"),
+    "stress-w8a8": dict(T=65536, H=4096, I=1536, E=64, k=6, routing="hot25-zipf1.0", dtype="bf16", quant=True,
+                        desc="long-prefill load-imbalance stress w8a8"),
+}
+STAGES = 7  # MOE_STAGE_* boundaries recorded per step
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return dict(hbm=float(p["hbm_gbs"]), bf16=float(p["bf16_tflops"]),
+                    bf16_sus=float(p["bf16_tflops_sustained"]), source="measured")
+    except Exception:
+        return dict(hbm=6650.0, bf16=1590.0, bf16_sus=1400.0, source="fallback")
+
+
+def load_traffic(config: str):
+    path = os.path.join(ROOT, "profiles", "traffic.json")
+    try:
+        with open(path) as f:
+            return json.load(f).get(config)
+    except Exception:
+        return None
+
+
+class ClockSampler:
+    """Samples nvidia-smi clocks/throttle reasons while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,utilization.gpu,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.file = None
+
+    def start(self):
+        try:
+            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.gpu)], stdout=self.file, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.file.flush()
+        self.file.seek(0)
+        rows = [r.split(",") for r in self.file.read().strip().splitlines() if r.strip()]
+        self.file.close()
+        os.unlink(self.file.name)
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            try:
+                sm.append(float(r[1]))
+                smax.append(float(r[2]))
+                for n, v in zip(names, r[6:10]):
+                    if v.strip().lower() == "active":
+                        reasons.add(n)
+            except (ValueError, IndexError):
+                continue
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(smax), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# --------------------------------------------------------------------------- inputs
+
+
+def make_inputs(cfg, rank: int, device):
+    import torch
+
+    from oracle import moe_oracle as O  # routing of the synthetic inputs only (setup, untimed)
+
+    T, H, I, E, k = cfg["T"], cfg["H"], cfg["I"], cfg["E"], cfg["k"]
+    dt = {"bf16": torch.bfloat16, "fp32": torch.float32, "fp16": torch.float16}[cfg["dtype"]]
+    g = torch.Generator(device=device).manual_seed(1234 + rank)
+    x = torch.randn(T, H, device=device, generator=g).to(dt)
+    ids, wts = O.synthetic_routing(cfg["routing"], T, E, k, seed=rank)
+    return x, torch.from_numpy(ids).to(device), torch.from_numpy(wts).to(device), dt
+
+
+def make_weights(cfg, experts, device, dt):
+    """Weights of the given experts, logical (E, K, N) views over K-major storage."""
+    import torch
+
+    import mail_b200 as mb
+
+    H, I = cfg["H"], cfg["I"]
+    g = torch.Generator(device=device).manual_seed(99)
+    w13 = torch.empty(len(experts), 2 * I, H, device=device, dtype=dt)
+    w2 = torch.empty(len(experts), H, I, device=device, dtype=dt)
+    for i, e in enumerate(experts):
+        g.manual_seed(1000 + e)
+        w13[i] = (torch.randn(2 * I, H, device=device, generator=g) * 0.02).to(dt)
+        w2[i] = (torch.randn(H, I, device=device, generator=g) * 0.02).to(dt)
+    w13, w2 = w13.transpose(1, 2), w2.transpose(1, 2)
+    scales = None
+    if cfg["quant"]:
+        w13, w2, scales = mb.quantize_weights_int8(w13, w2)
+    return w13, w2, scales
+
+
+# --------------------------------------------------------------------------- reference arm / cpu baseline
+
+
+def cpu_reference_run(cfg, steps: int, warmup: int, budget_s: float = 20.0):
+    """Times the oracle port of the reference's torch MoE path (per-expert fp32
+    loop, fixed_kernel.py:232-249, extended with the top-k combine) on the
+    host cores over a bounded token sample of the workload: the sample size is
+    chosen from a quick sgemm calibration so one step takes about
+    budget_s / steps seconds, and only the experts the sample touches get
+    (host-generated) weights."""
+    try:
+        from threadpoolctl import threadpool_info
+        threads = max([i.get("num_threads", 1) for i in threadpool_info()] or [1])
+    except Exception:
+        threads = os.cpu_count() or 1
+
+    from oracle import moe_oracle as O
+
+    T, H, I, E, k = cfg["T"], cfg["H"], cfg["I"], cfg["E"], cfg["k"]
+    rng = np.random.default_rng(0)
+    a = rng.standard_normal((256, H), dtype=np.float32)
+    b = rng.standard_normal((H, 2048), dtype=np.float32)
+    a @ b
+    t0 = time.perf_counter()
+    for _ in range(3):
+        a @ b
+    gflops = 3 * 2 * 256 * H * 2048 / (time.perf_counter() - t0) / 1e9
+    per_step = max(budget_s / max(steps + warmup, 1), 0.25)
+    flops_per_token = 6.0 * k * H * I
+    n = int(max(1, min(T, per_step * gflops * 1e9 / flops_per_token)))
+    ids_all, wts_all = O.synthetic_routing(cfg["routing"], T, E, k, seed=0)
+    ids, wts = ids_all[:n], wts_all[:n]
+    x = rng.standard_normal((n, H), dtype=np.float32)
+    touched = sorted(set(int(e) for e in ids.reshape(-1) if 0 <= e < E))
+
+    class Shared:
+        """E experts whose weights alternate between `nw` host arrays: one
+        expert's weights (H x 3I floats) exceed any host cache, so the
+        per-expert loop still streams every expert's weights from DRAM, while
+        the host materialises only nw of them."""
+
+        def __init__(self, arrays, n):
+            self.arrays, self.shape = arrays, (n,) + arrays[0].shape
+
+        def __getitem__(self, e):
+            return self.arrays[e % len(self.arrays)]
+
+    nw = 2
+    w13 = [rng.standard_normal((H, 2 * I), dtype=np.float32) * np.float32(0.02) for _ in range(nw)]
+    w2 = [rng.standard_normal((I, H), dtype=np.float32) * np.float32(0.02) for _ in range(nw)]
+    ids_l = ids
+    if cfg["quant"]:
+        q = [O.quantize_weight_per_channel(w.T) for w in w13]
+        q2 = [O.quantize_weight_per_channel(w.T) for w in w2]
+        q13, s13 = Shared([a for a, _ in q], E), Shared([b for _, b in q], E)
+        q2, s2 = Shared([a for a, _ in q2], E), Shared([b for _, b in q2], E)
+    w13, w2 = Shared(w13, E), Shared(w2, E)
+
+    def run():
+        t1 = time.perf_counter()
+        if cfg["quant"]:
+            O.moe_mlp_w8a8(x, q13, s13, q2, s2, wts, ids_l)
+        else:
+            O.moe_mlp_topk(x, w13, w2, wts, ids_l)
+        return time.perf_counter() - t1
+
+    for _ in range(warmup):
+        run()
+    times = [run() for _ in range(steps)]
+    t = sum(times) / len(times)
+    return dict(value=n / t, unit="tokens/s", cores=int(threads), tokens=n, seconds_per_step=t,
+                sample=f"{n} of {T} tokens per step (same H/I/E/k and routing; {len(touched)} experts touched), "
+                       f"{'w8a8 ' if cfg['quant'] else ''}fp32 numpy per-expert loop, {threads} BLAS threads")
+
+
+# --------------------------------------------------------------------------- our arm
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", default="mixtral", choices=sorted(CONFIGS))
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    cfg = CONFIGS[args.config]
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    T, H, I, E, k = cfg["T"], cfg["H"], cfg["I"], cfg["E"], cfg["k"]
+    dtype_name = "int8" if cfg["quant"] else cfg["dtype"]
+    config_json = {"workload": cfg["desc"], "tokens_per_gpu": T, "hidden": H, "inter": I, "experts": E,
+                   "top_k": k, "routing": cfg["routing"], "dtype": cfg["dtype"] + ("+w8a8" if cfg["quant"] else ""),
+                   "parallelism": f"ep{world}" if world > 1 else "single",
+                   "l2": "weights (%.2f GB) exceed the 126 MB L2, streamed every step" %
+                         (E * 3 * H * I * (1 if cfg["quant"] else (4 if cfg["dtype"] == "fp32" else 2)) / 1e9)}
+
+    if args.impl == "reference":
+        if rank != 0:
+            return 0
+        ref = cpu_reference_run(cfg, args.steps, args.warmup)
+        line = {"metric": "fused MoE MLP tokens/s", "value": ref["value"], "unit": "tokens/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ref["seconds_per_step"] * 1e3,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+                "data": "synthetic", "config": config_json, "impl": "reference",
+                "cpu_baseline": {"value": ref["value"], "unit": "tokens/s", "cores": ref["cores"], "kind": "port",
+                                 "sample": ref["sample"]},
+                "e2e": {"value": ref["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return 0
+
+    import torch
+    import torch.distributed as dist
+
+    import mail_b200 as mb
+    from mail_b200 import _lib
+
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+    lib = _lib.load()
+
+    x, ids, wts, dt = make_inputs(cfg, rank, device)
+    if world > 1:
+        from mail_b200 import ep as mep
+        assert E % world == 0, "experts must divide evenly over ranks"
+        local = list(range(rank * E // world, (rank + 1) * E // world))
+        w13, w2, scales = make_weights(cfg, local, device, dt)
+        layer = mep.ExpertParallelMoE(w13, w2, E, scales=scales)
+
+        def step(xx, ii, ww):
+            return layer(xx, ww, ii)
+    else:
+        w13, w2, scales = make_weights(cfg, list(range(E)), device, dt)
+
+        def step(xx, ii, ww):
+            return mb.fused_moe_mlp(xx, w13, w2, ww, ii, scales=scales)
+
+    stream = torch.cuda.current_stream(device)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+
+    # ---- warm-up
+    for _ in range(args.warmup):
+        step(x, ids, wts)
+    torch.cuda.synchronize()
+
+    # ---- timed region (device-resident inputs), per-stage events every step
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(STAGES)] for _ in range(args.steps)]
+    handles = [(torch.cuda.Event(enable_timing=True)) for _ in range(2)]
+    import ctypes
+    ev_arrays = [(ctypes.c_void_p * STAGES)(*[e.cuda_event for e in row]) for row in ev]
+    sampler = ClockSampler(local_rank)
+    sampler.start()
+    time.sleep(0.3)
+    barrier()
+    torch.cuda.synchronize()
+    launches0 = lib.moe_launch_count()
+    handles[0].record(stream)
+    for i in range(args.steps):
+        lib.moe_set_stage_events(ev_arrays[i], STAGES)
+        step(x, ids, wts)
+    lib.moe_set_stage_events(None, 0)
+    handles[1].record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    clocks = sampler.stop()
+    launches = lib.moe_launch_count() - launches0
+    ms = handles[0].elapsed_time(handles[1]) / args.steps
+
+    def stage_ms(a, b):
+        return statistics.mean(row[a].elapsed_time(row[b]) for row in ev)
+
+    st_ms = {"route": stage_ms(0, 1), "gather": stage_ms(1, 2), "gemm1": stage_ms(2, 3), "pre_gemm2": stage_ms(3, 4),
+             "gemm2": stage_ms(4, 5), "finalize": stage_ms(5, 6)}
+    if world > 1:
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+
+    # ---- end to end through the public API: pinned host inputs in, result out
+    x_h = x.cpu().pin_memory()
+    ids_h = ids.cpu().pin_memory()
+    wts_h = wts.cpu().pin_memory()
+    y_h = torch.empty((T, H), dtype=dt).pin_memory()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for _ in range(2):
+        y = step(x_h.to(device, non_blocking=True), ids_h.to(device, non_blocking=True),
+                 wts_h.to(device, non_blocking=True))
+        y_h.copy_(y, non_blocking=True)
+    torch.cuda.synchronize()
+    barrier()
+    e0.record(stream)
+    for _ in range(args.steps):
+        y = step(x_h.to(device, non_blocking=True), ids_h.to(device, non_blocking=True),
+                 wts_h.to(device, non_blocking=True))
+        y_h.copy_(y, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    h2d = x_h.numel() * x_h.element_size() + ids_h.numel() * 4 + wts_h.numel() * 4
+    d2h = y_h.numel() * y_h.element_size()
+
+    # ---- roofline of the dominant kernel (gate_up GEMM + SwiGLU)
+    peaks = load_peaks()
+    S_local = int(T * k)  # slots per rank (uniform routing keeps the per-rank load ~ T*k)
+    flops_gemm1 = 2.0 * S_local * H * 2 * I
+    gemm1_s = st_ms["gemm1"] / 1e3
+    peak_tc = peaks["bf16_sus"] * (2.0 if cfg["quant"] else 1.0)
+    roofline = {"kernel": "moe_gemm_kernel<SWIGLU> (gate_up GEMM + SwiGLU)", "bound": "tensor",
+                "achieved": flops_gemm1 / gemm1_s / 1e12, "peak": peak_tc, "unit": "TFLOP/s",
+                "frac": flops_gemm1 / gemm1_s / 1e12 / peak_tc,
+                "peak_source": f"{peaks['source']} bf16 sustained" + (" x2 (int8, spec ratio)" if cfg["quant"] else ""),
+                "traffic": load_traffic(args.config),
+                "flops_per_launch": flops_gemm1, "ms_per_launch": st_ms["gemm1"]}
+    flops_step = 6.0 * S_local * H * I
+    value = world * T / (ms / 1e3)
+
+    line = {"metric": "fused MoE MLP tokens/s", "value": value, "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": dtype_name, "data": "synthetic", "config": config_json,
+            "tflops_per_gpu": flops_step / (ms / 1e3) / 1e12,
+            "frac_of_tensor_peak": flops_step / (ms / 1e3) / 1e12 / peak_tc,
+            "stage_ms": st_ms, "roofline": roofline,
+            "e2e": {"value": world * T / (e2e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": int(h2d),
+                    "d2h_bytes_per_step": int(d2h), "ms_per_step": e2e_ms},
+            "gpu_launches": int(launches), "clocks": clocks}
+
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        ref = cpu_reference_run(cfg, steps=3, warmup=1, budget_s=20.0)
+        line["cpu_baseline"] = {"value": ref["value"], "unit": "tokens/s", "cores": ref["cores"], "kind": "port",
+                                "sample": ref["sample"]}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier(device_ids=[local_rank])
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,234 @@
+/*
+ * moe_b200.h — C ABI of the B200-native (sm_100a) fused MoE MLP.
+ *
+ * The op is the expert MLP of an sglang-style MoE layer:
+ *
+ *     out = grouped_matmul(x, w13) -> silu(gate) * up -> grouped_matmul(., w2)
+ *
+ * Reference interface this library replaces (CrDem/mail, Python + Triton):
+ *   - fused_moe_mlp(x, w13, w2, group_sizes, BLOCK_M, ...)  fused_moe_mlp_triton.py:121-160
+ *   - build_tile_schedule(group_sizes, num_tokens, BLOCK_M)  fused_moe_mlp_triton.py:91-119
+ *   - the sglang call site fused_moe_mlp(hidden_states, w13_weight, w2_weight,
+ *     expert_tokens)                                           unquant_diff.txt:13-18
+ * The top-k entry point (moe_fused_experts) implements the north-star call
+ * fused_moe_mlp(hidden_states, w13, w2, topk_weights, topk_ids, [scales]); the
+ * reference has no routing/align/quant/combine code, so those stages follow the
+ * semantics documented beside each declaration.
+ *
+ * Conventions
+ *   - All pointers are device pointers unless stated otherwise; sizes are
+ *     element counts. Nothing here allocates device memory: callers pass a
+ *     workspace sized by the matching *_workspace_size() query.
+ *   - Every call is asynchronous on `stream` (a cudaStream_t, NULL = legacy
+ *     default stream) and never synchronises the device.
+ *   - Return value: MOE_OK or a moe_status_t; moe_last_error() returns a
+ *     thread-local message for the last failing call of this thread.
+ *   - Weight layout ("(E, K, N)" logical, K-major physical): w13 is stored as
+ *     [E, 2I, H] row-major (row n of expert e holds the H weights of output
+ *     column n; rows [0, I) = gate, [I, 2I) = up) which is the reference's
+ *     logical w13[E, H, 2I] viewed through transpose(1, 2) (kernel_bench.py:229-235).
+ *     w2 is stored as [E, H, I] row-major (the reference's logical w2[E, I, H]).
+ *   - Device-side failures (a pipeline wait that exceeded its time limit) are
+ *     latched in a device flag read by moe_get_device_error().
+ */
+#ifndef MOE_B200_H_
+#define MOE_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define MOE_API __attribute__((visibility("default")))
+#else
+#define MOE_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  MOE_OK = 0,
+  MOE_ERR_INVALID_ARG = 1,  /* bad shape / dtype / pointer / alignment */
+  MOE_ERR_UNSUPPORTED = 2,  /* valid request this build does not implement */
+  MOE_ERR_CUDA = 3,         /* a CUDA runtime or driver call failed */
+  MOE_ERR_WORKSPACE = 4,    /* workspace too small */
+  MOE_ERR_DEVICE = 5        /* device-side error flag was set (timeout) */
+} moe_status_t;
+
+typedef enum {
+  MOE_F32 = 0,
+  MOE_F16 = 1,
+  MOE_BF16 = 2,
+  MOE_I8 = 3,
+  MOE_I32 = 4,
+  MOE_I64 = 5
+} moe_dtype_t;
+
+/* GEMM2 epilogue modes (moe_gemm2). */
+typedef enum {
+  MOE_EPI_STORE_ROWS = 0,   /* out[row] = acc, rows in schedule order (pre-routed form) */
+  MOE_EPI_COMBINE_ADD = 1,  /* out_f32[slot / top_k] += row_weight[slot] * acc (top-k combine) */
+  MOE_EPI_SCATTER_ROWS = 2  /* out[slot] = acc (unpermute; expert-parallel return path) */
+} moe_epilogue_t;
+
+/* Library version (major * 10000 + minor * 100 + patch). */
+MOE_API int moe_version(void);
+/* Message of the last failing call on this host thread ("" if none). */
+MOE_API const char* moe_last_error(void);
+/* Copies the device error flag (0 = none, else a code identifying the stalled
+ * pipeline role) into *host_code and clears it. Synchronises `stream`. */
+MOE_API int moe_get_device_error(int* host_code, void* stream);
+
+/* Number of CUDA kernels this library has launched in this process
+ * (monotonic, all threads). */
+MOE_API int64_t moe_launch_count(void);
+
+/* Stage boundaries at which the all-in-one entry points record profiling
+ * events (moe_set_stage_events). */
+typedef enum {
+  MOE_STAGE_ENTRY = 0,
+  MOE_STAGE_ROUTED = 1,   /* tile schedule / align done */
+  MOE_STAGE_GATHERED = 2, /* permuting gather (+ int8 quant) done */
+  MOE_STAGE_GEMM1 = 3,    /* gate_up GEMM + SwiGLU done */
+  MOE_STAGE_PRE_GEMM2 = 4,/* int8 quant of h + output clear done */
+  MOE_STAGE_GEMM2 = 5,    /* down GEMM + combine done */
+  MOE_STAGE_DONE = 6,     /* output conversion done */
+  MOE_NUM_STAGES = 7
+} moe_stage_t;
+
+/* Profiling hook (this host thread only): while `events` is non-NULL,
+ * moe_fused_mlp and moe_fused_experts record events[i] (cudaEvent_t) on their
+ * stream at stage boundary i < num_events. Pass NULL to disable. */
+MOE_API int moe_set_stage_events(void* const* events, int num_events);
+
+/* --------------------------------------------------------------------------
+ * Tile schedule — replaces build_tile_schedule (fused_moe_mlp_triton.py:91-119).
+ * For grid = ceil(num_tokens / block_m) + num_experts tiles (the reference's
+ * static upper bound) writes, per tile i:
+ *   tile_expert[i]    = searchsorted(cumsum(ceil(gs / block_m)), i, right=True),
+ *                       clamped to num_experts - 1
+ *   tile_row_start[i] = offsets[e] + (i - tiles_cumsum[e]) * block_m (0 if invalid)
+ *   tile_row_count[i] = clamp(offsets[e + 1] - row_start, 0, block_m) (0 if invalid)
+ * as int64, bit-identical to the reference. group_sizes is int32 or int64.
+ * `tile_table` (optional, may be NULL) receives the compact int32 table the
+ * GEMM entry points consume; its size is moe_tile_table_ints(E, grid).
+ * -------------------------------------------------------------------------- */
+MOE_API int64_t moe_tile_grid(int64_t num_tokens, int num_experts, int block_m);
+MOE_API int64_t moe_tile_table_ints(int num_experts, int64_t max_tiles);
+MOE_API int moe_tile_schedule(const void* group_sizes, int gs_dtype, int num_experts, int64_t num_tokens, int block_m,
+                      int64_t* tile_expert, int64_t* tile_row_start, int64_t* tile_row_count,
+                      int32_t* tile_table, void* stream);
+
+/* --------------------------------------------------------------------------
+ * Routing align (no reference counterpart; upstream of fused_moe_mlp, the
+ * contract of "tokens grouped contiguously by expert, expert 0 first",
+ * independent_test.py:24-31). Stable counting sort of the num_tokens*top_k
+ * slots (slot = t * top_k + j) by expert id, each expert's segment padded to
+ * a multiple of block_m rows:
+ *   sorted_slots[p]  slot id at padded row p, or -1 for padding rows
+ *   slot_pos[slot]   padded row of the slot, -1 if its id is outside [0, E)
+ *   group_sizes[e]   number of slots routed to expert e (int32)
+ *   padded_offsets[e] first padded row of expert e; [E] = total padded rows
+ *   tile_table       compact schedule consumed by the GEMMs
+ * Ids outside [0, num_experts) are dropped (counted in tile_table[2]).
+ * sorted_slots needs moe_align_capacity() entries.
+ * -------------------------------------------------------------------------- */
+MOE_API int64_t moe_align_capacity(int64_t num_slots, int num_experts, int block_m);
+MOE_API size_t moe_align_workspace_size(int64_t num_tokens, int top_k, int num_experts, int block_m);
+MOE_API int moe_align(const int32_t* topk_ids, int64_t num_tokens, int top_k, int num_experts, int block_m,
+              int32_t* sorted_slots, int32_t* slot_pos, int32_t* group_sizes, int32_t* padded_offsets,
+              int32_t* tile_table, void* workspace, size_t workspace_bytes, void* stream);
+
+/* --------------------------------------------------------------------------
+ * Row gather and per-token int8 quant (no reference counterpart).
+ * moe_gather_rows: dst[p] = src[sorted_slots[p] / top_k] for p < rows
+ * (zero rows where sorted_slots[p] < 0). If dst_dtype == MOE_I8 the row is
+ * quantised on the fly: s = absmax / 127, q = clamp(rint(x / s), -127, 127)
+ * (round-half-even; s = 0 and q = 0 for an all-zero row), scale written to
+ * dst_scale[p]. `rows_dev` (optional) points at a device int bounding the
+ * rows processed (e.g. tile_table + 1); `rows` is the static upper bound.
+ * moe_quant_rows: the same quantisation applied row-by-row in place order.
+ * -------------------------------------------------------------------------- */
+MOE_API int moe_gather_rows(const void* src, int src_dtype, int64_t cols, const int32_t* sorted_slots, int top_k,
+                    int64_t rows, const int32_t* rows_dev, void* dst, int dst_dtype, float* dst_scale,
+                    void* stream);
+MOE_API int moe_quant_rows(const void* src, int src_dtype, int64_t rows, int64_t cols, const int32_t* rows_dev,
+                   int8_t* dst, float* dst_scale, void* stream);
+
+/* --------------------------------------------------------------------------
+ * Grouped GEMMs (tcgen05 / TMEM, TMA-fed, persistent, warp-specialised).
+ * Replaces _grouped_gemm1_swiglu_kernel (partially_fused_moe_mlp_triton.py:59-114)
+ * and the GEMM1 half of _fused_moe_mlp_kernel (fused_moe_mlp_triton.py:35-66):
+ *   h[r, n] = silu(g) * u,  g = a[r] . w13[e, n],  u = a[r] . w13[e, I + n]
+ * with fp32 (int32 for int8) accumulation; w8a8 dequant (a_scale[r] *
+ * w13_scale[e, n]) is applied to g and u before the SwiGLU. h is written in
+ * h_dtype (the reference's weight dtype; bf16 for int8 inputs).
+ * a: [a_rows, H]; w13: [E, 2I, H]; h: [a_rows, I]. dtypes: BF16, F16, F32
+ * (tf32 tensor cores), I8 (a and w13 both int8, scales required).
+ * -------------------------------------------------------------------------- */
+MOE_API int moe_gemm1_swiglu(const void* a, int dtype, int64_t a_rows, int64_t hidden, const void* w13,
+                     int num_experts, int64_t inter, const float* a_scale, const float* w13_scale,
+                     const int32_t* tile_table, int64_t max_tiles, void* h, int h_dtype, void* stream);
+
+/* Replaces _grouped_gemm2_kernel (partially_fused_moe_mlp_triton.py:116-162)
+ * and the GEMM2 half of _fused_moe_mlp_kernel (fused_moe_mlp_triton.py:68-88):
+ *   acc[r, c] = h[r] . w2[e, c]   (w2: [E, H, I], h: [h_rows, I])
+ * dequantised by h_scale[r] * w2_scale[e, c] for int8, then per `epilogue`:
+ *   MOE_EPI_STORE_ROWS   out[r, c] = acc                       (out_dtype)
+ *   MOE_EPI_COMBINE_ADD  out[row_map[r] / top_k, c] += row_weight[row_map[r]] * acc
+ *                        (out is fp32, atomically accumulated; rows with
+ *                        row_map < 0 skipped) — the top-k weighted unpermute
+ *                        and combine of the MoE layer
+ *   MOE_EPI_SCATTER_ROWS out[row_map[r], c] = acc (x row_weight[row_map[r]] if
+ *                        row_weight != NULL), out_dtype
+ * -------------------------------------------------------------------------- */
+MOE_API int moe_gemm2(const void* h, int dtype, int64_t h_rows, int64_t inter, const void* w2, int num_experts,
+              int64_t hidden, const float* h_scale, const float* w2_scale, const int32_t* tile_table,
+              int64_t max_tiles, int epilogue, const int32_t* row_map, const float* row_weight, int top_k,
+              void* out, int out_dtype, int64_t out_rows, void* stream);
+
+/* y[t, c] = sum_j topk_weights[t, j] * o[slot_pos[t*k + j], c] (fp32 sum,
+ * skipped where slot_pos < 0), written in y_dtype. Deterministic combine used
+ * by the expert-parallel path. */
+MOE_API int moe_combine_rows(const void* o, int o_dtype, int64_t hidden, const int32_t* slot_pos,
+                     const float* topk_weights, int64_t num_tokens, int top_k, void* y, int y_dtype,
+                     void* stream);
+
+/* dst[i] = (dst_dtype) src_f32[i] for i < n. */
+MOE_API int moe_convert_f32(const float* src, int64_t n, void* dst, int dst_dtype, void* stream);
+
+/* --------------------------------------------------------------------------
+ * All-in-one entry points.
+ *
+ * moe_fused_mlp — drop-in for fused_moe_mlp(x, w13, w2, group_sizes)
+ * (fused_moe_mlp_triton.py:121-160; call site unquant_diff.txt:13-18): x is
+ * [num_tokens, H] already grouped by expert, group_sizes [E] (int32/int64)
+ * counts, out [num_tokens, H] in x's dtype (rows no group covers are zero).
+ * dtype in {BF16, F16, F32}; block_m must be 128.
+ *
+ * moe_fused_experts — the top-k form fused_moe_mlp(hidden_states, w13, w2,
+ * topk_weights, topk_ids, [scales]): align -> gather (+int8 quant) -> GEMM1 +
+ * SwiGLU -> (int8 quant of h) -> GEMM2 + weighted combine -> y [T, H] in
+ * x_dtype. w_dtype == MOE_I8 selects w8a8 with per-output-channel weight
+ * scales w13_scale [E, 2I] and w2_scale [E, H] (fp32) and dynamic per-token
+ * activation scales; otherwise w_dtype must equal x_dtype.
+ * -------------------------------------------------------------------------- */
+MOE_API size_t moe_fused_mlp_workspace_size(int64_t num_tokens, int64_t hidden, int64_t inter, int num_experts,
+                                    int dtype, int block_m);
+MOE_API int moe_fused_mlp(const void* x, int dtype, int64_t num_tokens, int64_t hidden, const void* w13,
+                  const void* w2, int num_experts, int64_t inter, const void* group_sizes, int gs_dtype,
+                  int block_m, void* out, void* workspace, size_t workspace_bytes, void* stream);
+
+MOE_API size_t moe_fused_experts_workspace_size(int64_t num_tokens, int64_t hidden, int64_t inter, int num_experts,
+                                        int top_k, int x_dtype, int w_dtype);
+MOE_API int moe_fused_experts(const void* x, int x_dtype, int64_t num_tokens, int64_t hidden, const void* w13,
+                      const void* w2, int w_dtype, int num_experts, int64_t inter, const float* topk_weights,
+                      const int32_t* topk_ids, int top_k, const float* w13_scale, const float* w2_scale,
+                      void* y, void* workspace, size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MOE_B200_H_ */

@@ -1,0 +1,97 @@
+// Internal helpers shared by the MoE translation units: status/error
+// reporting, dtype sizes, the compact tile table, and the device error flag.
+#pragma once
+#include <cstdarg>
+#include <cstdint>
+#include <cstdio>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include "../../include/moe_b200.h"
+
+namespace moe {
+
+constexpr int kBlockM = 128;  // rows per M tile (UMMA M)
+
+// Records a message for moe_last_error() and returns `code`.
+int set_error(int code, const char* fmt, ...);
+
+#define MOE_CHECK_ARG(cond, ...)                                   \
+  do {                                                             \
+    if (!(cond)) return ::moe::set_error(MOE_ERR_INVALID_ARG, __VA_ARGS__); \
+  } while (0)
+
+#define MOE_CUDA_TRY(expr)                                                                       \
+  do {                                                                                           \
+    cudaError_t e_ = (expr);                                                                     \
+    if (e_ != cudaSuccess)                                                                       \
+      return ::moe::set_error(MOE_ERR_CUDA, "%s failed: %s (%s:%d)", #expr, cudaGetErrorString(e_), \
+                              __FILE__, __LINE__);                                               \
+  } while (0)
+
+// Counts one kernel launch (moe_launch_count).
+void note_launch();
+
+#define MOE_LAUNCH_CHECK(name)                                                                   \
+  do {                                                                                           \
+    cudaError_t e_ = cudaGetLastError();                                                         \
+    if (e_ != cudaSuccess)                                                                       \
+      return ::moe::set_error(MOE_ERR_CUDA, "launch of %s failed: %s", name, cudaGetErrorString(e_)); \
+    ::moe::note_launch();                                                                        \
+  } while (0)
+
+#define MOE_TRY(expr)            \
+  do {                           \
+    int s_ = (expr);             \
+    if (s_ != MOE_OK) return s_; \
+  } while (0)
+
+inline int dtype_size(int dt) {
+  switch (dt) {
+    case MOE_F32: return 4;
+    case MOE_F16: return 2;
+    case MOE_BF16: return 2;
+    case MOE_I8: return 1;
+    case MOE_I32: return 4;
+    case MOE_I64: return 8;
+    default: return 0;
+  }
+}
+
+inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// Compact int32 tile table written by the schedule/align kernels and read by
+// the GEMMs:
+//   [0] number of valid M tiles        [1] rows covered (padded rows for align)
+//   [2] dropped slots (align)          [3] reserved
+//   [4 .. 4+E]          tile_cumsum[E+1] (tiles of expert e are [cum[e], cum[e+1]))
+//   [5+E .. 5+E+T)      row_start[T]
+//   [5+E+T .. 5+E+2T)   row_count[T]           (T = max_tiles)
+struct TileTable {
+  static constexpr int kHeader = 4;
+  __host__ __device__ static int64_t ints(int E, int64_t max_tiles) { return kHeader + (E + 1) + 2 * max_tiles; }
+  __host__ __device__ static int64_t cum_off() { return kHeader; }
+  __host__ __device__ static int64_t start_off(int E) { return kHeader + E + 1; }
+  __host__ __device__ static int64_t count_off(int E, int64_t max_tiles) { return kHeader + E + 1 + max_tiles; }
+};
+
+// Device error codes latched by the GEMM kernels (first error wins):
+// 1 = TMA producer wait, 2 = MMA issuer wait, 3 = epilogue wait, 4 = drain wait.
+inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+inline int num_sms() {
+  static int cache[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  if (cache[dev] == 0) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    cache[dev] = n > 0 ? n : 148;
+  }
+  return cache[dev];
+}
+
+}  // namespace moe

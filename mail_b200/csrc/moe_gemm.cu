@@ -1,0 +1,578 @@
+// Grouped MoE GEMMs on the 5th-generation tensor cores (tcgen05 + TMEM).
+//
+// One persistent, warp-specialised kernel template serves both GEMMs of the
+// expert MLP:
+//   GEMM1 (SWIGLU=true):  h = silu(a . w_gate) * (a . w_up)   (+ w8a8 dequant)
+//   GEMM2 (SWIGLU=false): out = h . w2 with three epilogues (row store,
+//                         weighted scatter-add combine, row scatter)
+// Reference kernels replaced: _grouped_gemm1_swiglu_kernel /
+// _grouped_gemm2_kernel (partially_fused_moe_mlp_triton.py:59-162) and the two
+// halves of _fused_moe_mlp_kernel (fused_moe_mlp_triton.py:35-88).
+//
+// CTA layout (192 threads, one CTA per SM):
+//   warp 0      TMA producer: A tile (128 rows x 128 B) + B tile (256 rows x
+//               128 B) per stage, 128B-swizzled, 4-stage ring in shared memory
+//   warp 1      TMEM allocator + single-thread tcgen05.mma issuer
+//               (M=128, N=256, K=32 bytes per instruction) into one of two
+//               256-column fp32/int32 accumulators in tensor memory
+//   warps 2..5  epilogue: tcgen05.ld of the accumulator (warp w reads TMEM
+//               lanes 32*(w%4)..+31), fused SwiGLU / dequant / combine, stores
+// The two accumulators let the epilogue of tile i overlap the MMAs of tile
+// i+1. Tiles are visited expert-major (all tiles of expert e, in bands of 16
+// M-tiles x all N-tiles), so CTAs running at the same time share weight
+// tiles through L2 and each expert's weights stream from HBM about once.
+#include <cuda.h>
+
+#include "common.cuh"
+#include "ptx.cuh"
+
+namespace moe {
+
+__device__ int g_moe_device_error = 0;
+
+namespace {
+
+constexpr int BM = 128;
+constexpr int BN = 256;
+constexpr int STAGES = 4;
+constexpr int ROW_BYTES = 128;             // K bytes per stage (one 128B swizzle atom)
+constexpr int A_BYTES = BM * ROW_BYTES;    // 16 KiB
+constexpr int B_BYTES = BN * ROW_BYTES;    // 32 KiB
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int NUM_THREADS = 192;
+constexpr int GROUP_M = 16;
+constexpr int TMEM_COLS = 512;             // 2 accumulators x 256 columns
+constexpr int BAR_BYTES = 256;             // barriers + tmem slot + abort flag
+
+__device__ __forceinline__ void raise_device_error(int code) { atomicCAS(&g_moe_device_error, 0, code); }
+
+struct Params {
+  int E;
+  int num_kb;             // K blocks of 128 bytes
+  int n_tiles;            // tiles along N
+  int n_valid;            // valid output columns (I for GEMM1, H for GEMM2)
+  int b_rows_per_expert;  // rows of B per expert (2I or H)
+  int inter;              // GEMM1: row offset of the up half within an expert
+  uint32_t idesc;         // tcgen05 instruction descriptor
+  const int32_t* table;
+  int max_tiles;
+  int64_t a_rows;
+  int epi;
+  void* out;
+  int out_dtype;
+  int64_t ldo;
+  int64_t out_rows;
+  const float* a_scale;
+  const float* b_scale;
+  const int32_t* row_map;
+  const float* row_weight;
+  int top_k;
+};
+
+// Tile t -> (m tile, n tile, expert) in expert-major, banded order.
+__device__ __forceinline__ void decode_tile(int t, const int32_t* s_cum, int E, int NT, int& m, int& n, int& e) {
+  int lo = 0, hi = E;  // invariant: s_cum[lo]*NT <= t < s_cum[hi]*NT
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (s_cum[mid] * NT <= t) lo = mid;
+    else hi = mid;
+  }
+  e = lo;
+  const int mt = s_cum[e + 1] - s_cum[e];
+  const int local = t - s_cum[e] * NT;
+  const int band = local / (GROUP_M * NT);
+  const int m0 = band * GROUP_M;
+  const int bsz = min(GROUP_M, mt - m0);
+  const int rem = local - band * GROUP_M * NT;
+  n = rem / bsz;
+  m = s_cum[e] + m0 + rem % bsz;
+}
+
+__device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.0f + __expf(-g)) * u; }
+
+// Stores 8 consecutive fp32 values as the output dtype (16- or 32-byte store).
+__device__ __forceinline__ void store8_out(void* base, int dtype, int64_t idx, const float* v) {
+  if (dtype == MOE_BF16) {
+    uint4 u;
+    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+    *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(base) + idx) = u;
+  } else if (dtype == MOE_F16) {
+    uint4 u;
+    __half2* h = reinterpret_cast<__half2*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) h[i] = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
+    *reinterpret_cast<uint4*>(static_cast<__half*>(base) + idx) = u;
+  } else {
+    float* f = static_cast<float*>(base) + idx;
+    *reinterpret_cast<float4*>(f) = make_float4(v[0], v[1], v[2], v[3]);
+    *reinterpret_cast<float4*>(f + 4) = make_float4(v[4], v[5], v[6], v[7]);
+  }
+}
+
+__device__ __forceinline__ void red_add4(float* addr, float a, float b, float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
+               : "memory");
+}
+
+template <int KIND>
+__device__ __forceinline__ float acc_value(uint32_t bits) {
+  if constexpr (KIND == 2) return static_cast<float>(static_cast<int32_t>(bits));
+  else return __uint_as_float(bits);
+}
+
+template <int KIND, bool SWIGLU>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    moe_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                    const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int32_t* s_cum = reinterpret_cast<int32_t*>(smem + STAGES * STAGE_BYTES + BAR_BYTES);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int E = p.E;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      ptx::mbar_init(&full[s], 1);
+      ptx::mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      ptx::mbar_init(&tfull[a], 1);
+      ptx::mbar_init(&tempty[a], 4 * 32);
+    }
+    ptx::mbar_init(drain, 1);
+    *abort_flag = 0;
+    ptx::fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    ptx::prefetch_tmap(&tmap_a);
+    ptx::prefetch_tmap(&tmap_b);
+  }
+  for (int i = threadIdx.x; i <= E; i += blockDim.x) s_cum[i] = p.table[TileTable::cum_off() + i];
+  if (warp == 1) {
+    ptx::tmem_alloc(tmem_slot, TMEM_COLS);
+    ptx::tmem_relinquish();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int NT = p.n_tiles;
+  const int total = s_cum[E] * NT;
+  const int32_t* row_start_tab = p.table + TileTable::start_off(E);
+  const int32_t* row_count_tab = p.table + TileTable::count_off(E, p.max_tiles);
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int last_par[STAGES];
+#pragma unroll
+      for (int s = 0; s < STAGES; ++s) last_par[s] = -1;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+        int m, n, e;
+        decode_tile(t, s_cum, E, NT, m, n, e);
+        const int row0 = row_start_tab[m];
+        const int brow = e * p.b_rows_per_expert + n * (SWIGLU ? BN / 2 : BN);
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          if (!ptx::mbar_wait(&empty[stage], phase ^ 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          ptx::mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
+          const int kx = kb * (ROW_BYTES / (KIND == 0 ? 2 : (KIND == 1 ? 4 : 1)));
+          ptx::tma_load_2d(sA + stage * A_BYTES, &tmap_a, &full[stage], kx, row0);
+          if constexpr (SWIGLU) {
+            ptx::tma_load_2d(sB + stage * B_BYTES, &tmap_b, &full[stage], kx, brow);
+            ptx::tma_load_2d(sB + stage * B_BYTES + B_BYTES / 2, &tmap_b, &full[stage], kx, brow + p.inter);
+          } else {
+            ptx::tma_load_2d(sB + stage * B_BYTES, &tmap_b, &full[stage], kx, brow);
+          }
+          last_par[stage] = (int)phase;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (!ok) {
+        raise_device_error(1);
+        *abort_flag = 1;
+        // let the copies already in flight land before the CTA exits
+        volatile int never = 0;
+        for (int s = 0; s < STAGES; ++s)
+          if (last_par[s] >= 0) ptx::mbar_wait(&full[s], (uint32_t)last_par[s], &never);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++it) {
+        const int acc = it & 1;
+        const uint32_t acc_par = (it >> 1) & 1;
+        if (!ptx::mbar_wait(&tempty[acc], acc_par ^ 1, abort_flag)) {
+          ok = false;
+          break;
+        }
+        ptx::tc_fence_after();
+        const uint32_t d = tmem_base + acc * BN;
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          if (!ptx::mbar_wait(&full[stage], phase, abort_flag)) {
+            ok = false;
+            break;
+          }
+          ptx::tc_fence_after();
+          const uint32_t a_addr = ptx::smem_u32(sA + stage * A_BYTES);
+          const uint32_t b_addr = ptx::smem_u32(sB + stage * B_BYTES);
+#pragma unroll
+          for (int k = 0; k < ROW_BYTES / 32; ++k) {
+            ptx::umma<KIND>(d, ptx::smem_desc_k128(a_addr + k * 32), ptx::smem_desc_k128(b_addr + k * 32), p.idesc,
+                            (kb > 0 || k > 0) ? 1u : 0u);
+          }
+          ptx::umma_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        ptx::umma_commit(&tfull[acc]);
+      }
+      if (!ok) {
+        raise_device_error(2);
+        *abort_flag = 1;
+      }
+      // all MMAs issued by this thread complete before TMEM is released
+      ptx::umma_commit(drain);
+      volatile int never = 0;
+      if (!ptx::mbar_wait(drain, 0, &never)) raise_device_error(4);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;          // TMEM lane quarter this warp may access
+    const int r = q * 32 + lane;     // row of the tile held by this thread
+    int it = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < total; t += gridDim.x, ++it) {
+      int m, n, e;
+      decode_tile(t, s_cum, E, NT, m, n, e);
+      const int acc = it & 1;
+      const uint32_t acc_par = (it >> 1) & 1;
+      bool w_ok = ptx::mbar_wait(&tfull[acc], acc_par, abort_flag);
+      if (!__all_sync(0xffffffffu, w_ok)) {
+        ok = false;
+        break;
+      }
+      ptx::tc_fence_after();
+      const int32_t rstart = row_start_tab[m];
+      const int32_t rcount = row_count_tab[m];
+      const int64_t grow = (int64_t)rstart + r;
+      const bool row_ok = (r < rcount) && (grow < p.a_rows);
+      const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
+      float sa = 1.f;
+      if constexpr (KIND == 2) sa = row_ok ? p.a_scale[grow] : 0.f;
+
+      if constexpr (SWIGLU) {
+        const int64_t wrow = (int64_t)e * p.b_rows_per_expert;
+#pragma unroll 1
+        for (int c = 0; c < (BN / 2) / 32; ++c) {
+          uint32_t g[32], u[32];
+          ptx::tmem_ld32(tbase + c * 32, g);
+          ptx::tmem_ld32(tbase + BN / 2 + c * 32, u);
+          ptx::tmem_ld_wait();
+          const int col0 = n * (BN / 2) + c * 32;
+          if (row_ok && col0 < p.n_valid) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const int cj = col0 + 8 * j;
+              if (cj < p.n_valid) {
+                float h[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                  float gv = acc_value<KIND>(g[8 * j + i]);
+                  float uv = acc_value<KIND>(u[8 * j + i]);
+                  if constexpr (KIND == 2) {
+                    gv = gv * sa * p.b_scale[wrow + cj + i];
+                    uv = uv * sa * p.b_scale[wrow + p.inter + cj + i];
+                  }
+                  h[i] = silu_mul(gv, uv);
+                }
+                store8_out(p.out, p.out_dtype, grow * p.ldo + cj, h);
+              }
+            }
+          }
+        }
+      } else {
+        int64_t dst_row = grow;
+        float wgt = 1.f;
+        bool do_store = row_ok;
+        if (p.epi != MOE_EPI_STORE_ROWS && row_ok) {
+          const int32_t slot = p.row_map[grow];
+          do_store = slot >= 0;
+          if (slot >= 0) {
+            dst_row = (p.epi == MOE_EPI_COMBINE_ADD) ? (int64_t)(slot / p.top_k) : (int64_t)slot;
+            if (p.row_weight) wgt = p.row_weight[slot];
+          }
+        }
+        if (dst_row >= p.out_rows) do_store = false;
+        const int64_t wrow = (int64_t)e * p.b_rows_per_expert;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t v[32];
+          ptx::tmem_ld32(tbase + c * 32, v);
+          ptx::tmem_ld_wait();
+          const int col0 = n * BN + c * 32;
+          if (do_store && col0 < p.n_valid) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const int cj = col0 + 8 * j;
+              if (cj < p.n_valid) {
+                float f[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                  float x = acc_value<KIND>(v[8 * j + i]);
+                  if constexpr (KIND == 2) x = x * sa * p.b_scale[wrow + cj + i];
+                  f[i] = x * wgt;
+                }
+                if (p.epi == MOE_EPI_COMBINE_ADD) {
+                  float* dst = static_cast<float*>(p.out) + dst_row * p.ldo + cj;
+                  red_add4(dst, f[0], f[1], f[2], f[3]);
+                  red_add4(dst + 4, f[4], f[5], f[6], f[7]);
+                } else {
+                  store8_out(p.out, p.out_dtype, dst_row * p.ldo + cj, f);
+                }
+              }
+            }
+          }
+        }
+      }
+      ptx::tc_fence_before();
+      ptx::mbar_arrive(&tempty[acc]);
+    }
+    if (!ok) {
+      if (lane == 0) raise_device_error(3);
+      *abort_flag = 1;
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------- host side
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+int get_encode(EncodeTiledFn* fn) {
+  static EncodeTiledFn cached = nullptr;
+  if (!cached) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q);
+    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !ptr)
+      return set_error(MOE_ERR_CUDA, "cuTensorMapEncodeTiled unavailable (%s)", cudaGetErrorString(e));
+    cached = reinterpret_cast<EncodeTiledFn>(ptr);
+  }
+  *fn = cached;
+  return MOE_OK;
+}
+
+int make_tmap(CUtensorMap* m, const void* ptr, int dtype, uint64_t inner, uint64_t rows, uint32_t box_rows) {
+  EncodeTiledFn enc;
+  MOE_TRY(get_encode(&enc));
+  const int es = dtype_size(dtype);
+  CUtensorMapDataType dt = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  if (dtype == MOE_F16) dt = CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  else if (dtype == MOE_F32) dt = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+  else if (dtype == MOE_I8) dt = CU_TENSOR_MAP_DATA_TYPE_UINT8;
+  cuuint64_t dims[2] = {inner, rows};
+  cuuint64_t strides[1] = {inner * es};
+  cuuint32_t box[2] = {(cuuint32_t)(ROW_BYTES / es), box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(m, dt, 2, const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(MOE_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d) for %llu x %llu dtype %d", (int)r,
+                     (unsigned long long)rows, (unsigned long long)inner, dtype);
+  return MOE_OK;
+}
+
+uint32_t make_idesc(int dtype) {
+  int c_fmt = 1, ab = 1;  // fp32 accumulate, bf16 operands
+  if (dtype == MOE_F16) ab = 0;
+  else if (dtype == MOE_F32) ab = 2;  // tf32
+  else if (dtype == MOE_I8) {
+    c_fmt = 2;  // s32 accumulate
+    ab = 1;     // signed int8
+  }
+  return ((uint32_t)c_fmt << 4) | ((uint32_t)ab << 7) | ((uint32_t)ab << 10) | ((uint32_t)(BN >> 3) << 17) |
+         ((uint32_t)(BM >> 4) << 24);
+}
+
+int kind_of(int dtype) { return dtype == MOE_F32 ? 1 : (dtype == MOE_I8 ? 2 : 0); }
+
+size_t gemm_smem_bytes(int E) { return 1024 + (size_t)STAGES * STAGE_BYTES + BAR_BYTES + (size_t)(E + 1) * 4; }
+
+template <int KIND, bool SWIGLU>
+int launch_kind(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, unsigned grid, cudaStream_t st) {
+  const size_t smem = gemm_smem_bytes(p.E);
+  auto kfn = moe_gemm_kernel<KIND, SWIGLU>;
+  MOE_CUDA_TRY(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  kfn<<<grid, NUM_THREADS, smem, st>>>(ta, tb, p);
+  MOE_LAUNCH_CHECK("moe_gemm_kernel");
+  return MOE_OK;
+}
+
+template <bool SWIGLU>
+int launch(int dtype, const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, cudaStream_t st) {
+  int64_t tiles_ub = (int64_t)p.max_tiles * p.n_tiles;
+  int64_t grid = num_sms();
+  if (tiles_ub < grid) grid = tiles_ub;
+  if (grid <= 0) return MOE_OK;
+  switch (kind_of(dtype)) {
+    case 0: return launch_kind<0, SWIGLU>(ta, tb, p, (unsigned)grid, st);
+    case 1: return launch_kind<1, SWIGLU>(ta, tb, p, (unsigned)grid, st);
+    default: return launch_kind<2, SWIGLU>(ta, tb, p, (unsigned)grid, st);
+  }
+}
+
+int check_gemm_common(const char* fn, int dtype, int64_t k, int E, const int32_t* table, int64_t max_tiles) {
+  MOE_CHECK_ARG(dtype == MOE_BF16 || dtype == MOE_F16 || dtype == MOE_F32 || dtype == MOE_I8,
+                "%s: unsupported dtype %d", fn, dtype);
+  const int es = dtype_size(dtype);
+  MOE_CHECK_ARG(k > 0 && (k * es) % 16 == 0, "%s: reduction length %lld x %d bytes must be a multiple of 16 bytes",
+                fn, (long long)k, es);
+  MOE_CHECK_ARG(E > 0 && E <= 4096, "%s: num_experts %d outside [1, 4096]", fn, E);
+  MOE_CHECK_ARG(table != nullptr, "%s: tile_table is NULL", fn);
+  MOE_CHECK_ARG(max_tiles >= 0 && max_tiles < (int64_t(1) << 24), "%s: max_tiles out of range", fn);
+  return MOE_OK;
+}
+
+}  // namespace
+}  // namespace moe
+
+using namespace moe;
+
+extern "C" int moe_get_device_error(int* host_code, void* stream) {
+  MOE_CHECK_ARG(host_code != nullptr, "moe_get_device_error: NULL output");
+  cudaStream_t st = as_stream(stream);
+  int zero = 0;
+  MOE_CUDA_TRY(cudaMemcpyFromSymbolAsync(host_code, g_moe_device_error, sizeof(int), 0, cudaMemcpyDeviceToHost, st));
+  MOE_CUDA_TRY(cudaMemcpyToSymbolAsync(g_moe_device_error, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, st));
+  MOE_CUDA_TRY(cudaStreamSynchronize(st));
+  return MOE_OK;
+}
+
+extern "C" int moe_gemm1_swiglu(const void* a, int dtype, int64_t a_rows, int64_t hidden, const void* w13,
+                                int num_experts, int64_t inter, const float* a_scale, const float* w13_scale,
+                                const int32_t* tile_table, int64_t max_tiles, void* h, int h_dtype, void* stream) {
+  MOE_TRY(check_gemm_common("moe_gemm1_swiglu", dtype, hidden, num_experts, tile_table, max_tiles));
+  MOE_CHECK_ARG(a && w13 && h, "moe_gemm1_swiglu: NULL pointer");
+  MOE_CHECK_ARG(inter > 0 && inter % 8 == 0, "moe_gemm1_swiglu: inter (%lld) must be a positive multiple of 8",
+                (long long)inter);
+  MOE_CHECK_ARG(a_rows >= 0 && a_rows < (int64_t(1) << 31), "moe_gemm1_swiglu: a_rows out of range");
+  MOE_CHECK_ARG((int64_t)num_experts * 2 * inter < (int64_t(1) << 31), "moe_gemm1_swiglu: weight rows overflow");
+  MOE_CHECK_ARG(h_dtype == MOE_BF16 || h_dtype == MOE_F16 || h_dtype == MOE_F32, "moe_gemm1_swiglu: bad h dtype");
+  if (dtype == MOE_I8) MOE_CHECK_ARG(a_scale && w13_scale, "moe_gemm1_swiglu: int8 needs a_scale and w13_scale");
+  MOE_CHECK_ARG((uintptr_t)a % 16 == 0 && (uintptr_t)w13 % 16 == 0 && (uintptr_t)h % 16 == 0,
+                "moe_gemm1_swiglu: pointers must be 16-byte aligned");
+  if (a_rows == 0 || max_tiles == 0) return MOE_OK;
+  CUtensorMap ta, tb;
+  MOE_TRY(make_tmap(&ta, a, dtype, hidden, a_rows, BM));
+  MOE_TRY(make_tmap(&tb, w13, dtype, hidden, (uint64_t)num_experts * 2 * inter, BN / 2));
+  Params p{};
+  p.E = num_experts;
+  p.num_kb = (int)ceil_div(hidden * dtype_size(dtype), ROW_BYTES);
+  p.n_tiles = (int)ceil_div(inter, BN / 2);
+  p.n_valid = (int)inter;
+  p.b_rows_per_expert = (int)(2 * inter);
+  p.inter = (int)inter;
+  p.idesc = make_idesc(dtype);
+  p.table = tile_table;
+  p.max_tiles = (int)max_tiles;
+  p.a_rows = a_rows;
+  p.epi = MOE_EPI_STORE_ROWS;
+  p.out = h;
+  p.out_dtype = h_dtype;
+  p.ldo = inter;
+  p.out_rows = a_rows;
+  p.a_scale = a_scale;
+  p.b_scale = w13_scale;
+  p.top_k = 1;
+  return launch<true>(dtype, ta, tb, p, as_stream(stream));
+}
+
+extern "C" int moe_gemm2(const void* h, int dtype, int64_t h_rows, int64_t inter, const void* w2, int num_experts,
+                         int64_t hidden, const float* h_scale, const float* w2_scale, const int32_t* tile_table,
+                         int64_t max_tiles, int epilogue, const int32_t* row_map, const float* row_weight,
+                         int top_k, void* out, int out_dtype, int64_t out_rows, void* stream) {
+  MOE_TRY(check_gemm_common("moe_gemm2", dtype, inter, num_experts, tile_table, max_tiles));
+  MOE_CHECK_ARG(h && w2 && out, "moe_gemm2: NULL pointer");
+  MOE_CHECK_ARG(hidden > 0 && hidden % 8 == 0, "moe_gemm2: hidden (%lld) must be a positive multiple of 8",
+                (long long)hidden);
+  MOE_CHECK_ARG(h_rows >= 0 && h_rows < (int64_t(1) << 31), "moe_gemm2: h_rows out of range");
+  MOE_CHECK_ARG((int64_t)num_experts * hidden < (int64_t(1) << 31), "moe_gemm2: weight rows overflow");
+  MOE_CHECK_ARG(epilogue == MOE_EPI_STORE_ROWS || epilogue == MOE_EPI_COMBINE_ADD || epilogue == MOE_EPI_SCATTER_ROWS,
+                "moe_gemm2: bad epilogue %d", epilogue);
+  if (epilogue == MOE_EPI_COMBINE_ADD) {
+    MOE_CHECK_ARG(out_dtype == MOE_F32, "moe_gemm2: the combine epilogue accumulates into fp32");
+    MOE_CHECK_ARG(row_map && row_weight && top_k > 0, "moe_gemm2: combine needs row_map, row_weight, top_k");
+  } else {
+    MOE_CHECK_ARG(out_dtype == MOE_BF16 || out_dtype == MOE_F16 || out_dtype == MOE_F32, "moe_gemm2: bad out dtype");
+  }
+  if (epilogue == MOE_EPI_SCATTER_ROWS) MOE_CHECK_ARG(row_map != nullptr, "moe_gemm2: scatter needs row_map");
+  if (dtype == MOE_I8) MOE_CHECK_ARG(h_scale && w2_scale, "moe_gemm2: int8 needs h_scale and w2_scale");
+  MOE_CHECK_ARG((uintptr_t)h % 16 == 0 && (uintptr_t)w2 % 16 == 0 && (uintptr_t)out % 16 == 0,
+                "moe_gemm2: pointers must be 16-byte aligned");
+  if (h_rows == 0 || max_tiles == 0) return MOE_OK;
+  CUtensorMap ta, tb;
+  MOE_TRY(make_tmap(&ta, h, dtype, inter, h_rows, BM));
+  MOE_TRY(make_tmap(&tb, w2, dtype, inter, (uint64_t)num_experts * hidden, BN));
+  Params p{};
+  p.E = num_experts;
+  p.num_kb = (int)ceil_div(inter * dtype_size(dtype), ROW_BYTES);
+  p.n_tiles = (int)ceil_div(hidden, BN);
+  p.n_valid = (int)hidden;
+  p.b_rows_per_expert = (int)hidden;
+  p.inter = (int)inter;
+  p.idesc = make_idesc(dtype);
+  p.table = tile_table;
+  p.max_tiles = (int)max_tiles;
+  p.a_rows = h_rows;
+  p.epi = epilogue;
+  p.out = out;
+  p.out_dtype = out_dtype;
+  p.ldo = hidden;
+  p.out_rows = out_rows;
+  p.a_scale = h_scale;
+  p.b_scale = w2_scale;
+  p.row_map = row_map;
+  p.row_weight = row_weight;
+  p.top_k = top_k > 0 ? top_k : 1;
+  return launch<false>(dtype, ta, tb, p, as_stream(stream));
+}

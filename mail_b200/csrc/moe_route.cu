@@ -1,0 +1,353 @@
+// Tile schedule and routing align kernels.
+//
+//  * tile_schedule_kernel restates build_tile_schedule
+//    (fused_moe_mlp_triton.py:91-119) on the device: one CTA scans the group
+//    sizes and every thread resolves tiles with a binary search, so the
+//    reference's eight small torch launches become one.
+//  * align_* kernels implement the stable, block-padded counting sort of the
+//    top-k slots by expert that the reference's callers get from an external
+//    routing op (fused moe mlp triton.py:11-13): per-chunk warp histograms
+//    (__match_any_sync), a per-expert scan over chunks, a per-expert scan
+//    with padding to BLOCK_M, and a stable scatter.
+#include "common.cuh"
+
+namespace moe {
+namespace {
+
+constexpr int kScanThreads = 1024;
+constexpr int kChunk = 256;  // slots per align chunk (one warp, 8 rounds)
+
+// Inclusive scan across a CTA of kScanThreads threads.
+template <typename T>
+__device__ T block_inclusive_scan(T v, T* warp_sums) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    T n = __shfl_up_sync(0xffffffffu, v, o);
+    if (lane >= o) v += n;
+  }
+  if (lane == 31) warp_sums[warp] = v;
+  __syncthreads();
+  if (warp == 0) {
+    T w = (lane < (int)(blockDim.x >> 5)) ? warp_sums[lane] : T(0);
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      T n = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += n;
+    }
+    warp_sums[lane] = w;
+  }
+  __syncthreads();
+  if (warp > 0) v += warp_sums[warp - 1];
+  __syncthreads();
+  return v;
+}
+
+// In-place inclusive scan of a[0..n) held in shared memory (one CTA).
+template <typename T>
+__device__ void smem_inclusive_scan(T* a, int n, T* warp_sums) {
+  const int per = (n + blockDim.x - 1) / blockDim.x;
+  const int lo = min(n, (int)threadIdx.x * per), hi = min(n, lo + per);
+  T local = 0;
+  for (int i = lo; i < hi; ++i) local += a[i];
+  T incl = block_inclusive_scan<T>(local, warp_sums);
+  T run = incl - local;
+  for (int i = lo; i < hi; ++i) {
+    run += a[i];
+    a[i] = run;
+  }
+  __syncthreads();
+}
+
+// ---------------------------------------------------------------------------
+// build_tile_schedule (fused_moe_mlp_triton.py:91-119), bit-exact.
+__global__ void __launch_bounds__(kScanThreads) tile_schedule_kernel(
+    const void* __restrict__ gs_ptr, int gs_is64, int E, int BM, int64_t grid, int64_t* __restrict__ tile_expert,
+    int64_t* __restrict__ tile_row_start, int64_t* __restrict__ tile_row_count, int32_t* __restrict__ table) {
+  extern __shared__ int64_t sh[];
+  int64_t* offsets = sh;          // [E+1]  offsets[e] = sum gs[<e]
+  int64_t* tcum = sh + (E + 1);   // [E+1]  tiles_cumsum
+  __shared__ int64_t warp_sums[32];
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    int64_t g = gs_is64 ? reinterpret_cast<const int64_t*>(gs_ptr)[e]
+                        : (int64_t) reinterpret_cast<const int32_t*>(gs_ptr)[e];
+    if (g < 0) g = 0;  // negative counts are treated as empty groups
+    offsets[e + 1] = g;
+    tcum[e + 1] = (g + BM - 1) / BM;
+  }
+  if (threadIdx.x == 0) {
+    offsets[0] = 0;
+    tcum[0] = 0;
+  }
+  __syncthreads();
+  smem_inclusive_scan<int64_t>(offsets + 1, E, warp_sums);
+  smem_inclusive_scan<int64_t>(tcum + 1, E, warp_sums);
+
+  const int64_t total_tiles = tcum[E];
+  for (int64_t i = threadIdx.x; i < grid; i += blockDim.x) {
+    // searchsorted(tcum[1:], i, right=True): number of e with tcum[e+1] <= i.
+    int lo = 0, hi = E;  // answer in [0, E]
+    while (lo < hi) {
+      int mid = (lo + hi) >> 1;
+      if (tcum[mid + 1] <= i) lo = mid + 1;
+      else hi = mid;
+    }
+    const bool valid = lo < E;
+    const int e = valid ? lo : E - 1;
+    const int64_t local = i - tcum[e];
+    const int64_t start = valid ? offsets[e] + local * BM : 0;
+    int64_t count = offsets[e + 1] - start;
+    count = count < 0 ? 0 : (count > BM ? BM : count);
+    if (!valid) count = 0;
+    if (tile_expert) tile_expert[i] = e;
+    if (tile_row_start) tile_row_start[i] = start;
+    if (tile_row_count) tile_row_count[i] = count;
+    if (table && valid) {
+      table[TileTable::start_off(E) + i] = (int32_t)start;
+      table[TileTable::count_off(E, grid) + i] = (int32_t)count;
+    }
+  }
+  if (table) {
+    for (int e = threadIdx.x; e <= E; e += blockDim.x) table[TileTable::cum_off() + e] = (int32_t)tcum[e];
+    if (threadIdx.x == 0) {
+      table[0] = (int32_t)total_tiles;
+      table[1] = (int32_t)offsets[E];
+      table[2] = 0;
+      table[3] = 0;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Align, pass 1: per-chunk histogram (key E collects ids outside [0, E)).
+__global__ void align_count_kernel(const int32_t* __restrict__ ids, int64_t S, int E,
+                                   int32_t* __restrict__ chunk_hist) {
+  extern __shared__ int32_t hist[];  // [E+1]
+  const int lane = threadIdx.x;
+  for (int e = lane; e <= E; e += 32) hist[e] = 0;
+  __syncwarp();
+  const int64_t base = (int64_t)blockIdx.x * kChunk;
+#pragma unroll 1
+  for (int r = 0; r < kChunk / 32; ++r) {
+    const int64_t s = base + r * 32 + lane;
+    int key = -1;
+    if (s < S) {
+      const int id = ids[s];
+      key = (id >= 0 && id < E) ? id : E;
+    }
+    const unsigned m = __match_any_sync(0xffffffffu, key);
+    if (key >= 0 && lane == __ffs(m) - 1) hist[key] += __popc(m);
+    __syncwarp();
+  }
+  int32_t* out = chunk_hist + (int64_t)blockIdx.x * (E + 1);
+  for (int e = lane; e <= E; e += 32) out[e] = hist[e];
+}
+
+// Align, pass 2: exclusive scan of each expert column over chunks.
+__global__ void __launch_bounds__(kScanThreads) align_colscan_kernel(const int32_t* __restrict__ chunk_hist,
+                                                                     int num_chunks, int E,
+                                                                     int32_t* __restrict__ chunk_base,
+                                                                     int32_t* __restrict__ totals) {
+  __shared__ int32_t warp_sums[32];
+  const int e = blockIdx.x;  // 0..E (E = dropped column)
+  int32_t carry = 0;
+  for (int c0 = 0; c0 < num_chunks; c0 += blockDim.x) {
+    const int c = c0 + threadIdx.x;
+    const int32_t v = (c < num_chunks) ? chunk_hist[(int64_t)c * (E + 1) + e] : 0;
+    const int32_t incl = block_inclusive_scan<int32_t>(v, warp_sums);
+    if (c < num_chunks) chunk_base[(int64_t)c * (E + 1) + e] = carry + incl - v;
+    __shared__ int32_t last;
+    if (threadIdx.x == blockDim.x - 1) last = incl;
+    __syncthreads();
+    carry += last;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) totals[e] = carry;
+}
+
+// Align, pass 3: padded expert offsets, group sizes, tile table, pad fill.
+__global__ void __launch_bounds__(kScanThreads) align_finalize_kernel(
+    const int32_t* __restrict__ totals, int E, int BM, int64_t max_tiles, int32_t* __restrict__ group_sizes,
+    int32_t* __restrict__ padded_offsets, int32_t* __restrict__ table, int32_t* __restrict__ sorted_slots) {
+  extern __shared__ int32_t sm[];
+  int32_t* poff = sm;            // [E+1] padded offsets (exclusive)
+  int32_t* tcum = sm + (E + 1);  // [E+1] tile cumsum (exclusive)
+  __shared__ int32_t warp_sums[32];
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    const int32_t c = totals[e];
+    const int32_t t = (c + BM - 1) / BM;
+    poff[e + 1] = t * BM;
+    tcum[e + 1] = t;
+    group_sizes[e] = c;
+  }
+  if (threadIdx.x == 0) {
+    poff[0] = 0;
+    tcum[0] = 0;
+  }
+  __syncthreads();
+  smem_inclusive_scan<int32_t>(poff + 1, E, warp_sums);
+  smem_inclusive_scan<int32_t>(tcum + 1, E, warp_sums);
+  const int32_t ntiles = tcum[E];
+  for (int e = threadIdx.x; e <= E; e += blockDim.x) {
+    padded_offsets[e] = poff[e];
+    table[TileTable::cum_off() + e] = tcum[e];
+  }
+  if (threadIdx.x == 0) {
+    table[0] = ntiles;
+    table[1] = poff[E];
+    table[2] = totals[E];
+    table[3] = 0;
+  }
+  for (int i = threadIdx.x; i < ntiles && i < max_tiles; i += blockDim.x) {
+    int lo = 0, hi = E - 1;  // expert e with tcum[e] <= i < tcum[e+1]
+    while (lo < hi) {
+      int mid = (lo + hi + 1) >> 1;
+      if (tcum[mid] <= i) lo = mid;
+      else hi = mid - 1;
+    }
+    const int e = lo;
+    const int j = i - tcum[e];
+    const int32_t start = poff[e] + j * BM;
+    const int32_t cnt = min(BM, totals[e] - j * BM);
+    table[TileTable::start_off(E) + i] = start;
+    table[TileTable::count_off(E, max_tiles) + i] = cnt;
+    for (int r = cnt; r < BM; ++r) sorted_slots[start + r] = -1;
+  }
+}
+
+// Align, pass 4: stable scatter of slots into their padded rows.
+__global__ void align_scatter_kernel(const int32_t* __restrict__ ids, int64_t S, int E,
+                                     const int32_t* __restrict__ chunk_base,
+                                     const int32_t* __restrict__ padded_offsets,
+                                     int32_t* __restrict__ sorted_slots, int32_t* __restrict__ slot_pos) {
+  extern __shared__ int32_t run[];  // [E]
+  const int lane = threadIdx.x;
+  const int32_t* cb = chunk_base + (int64_t)blockIdx.x * (E + 1);
+  for (int e = lane; e < E; e += 32) run[e] = padded_offsets[e] + cb[e];
+  __syncwarp();
+  const int64_t base = (int64_t)blockIdx.x * kChunk;
+  const unsigned lt_mask = (1u << lane) - 1u;
+#pragma unroll 1
+  for (int r = 0; r < kChunk / 32; ++r) {
+    const int64_t s = base + r * 32 + lane;
+    int key = -1;
+    if (s < S) {
+      const int id = ids[s];
+      key = (id >= 0 && id < E) ? id : E;
+    }
+    const unsigned m = __match_any_sync(0xffffffffu, key);
+    if (key >= 0 && key < E) {
+      const int32_t pos = run[key] + __popc(m & lt_mask);
+      sorted_slots[pos] = (int32_t)s;
+      slot_pos[s] = pos;
+    } else if (key == E) {
+      slot_pos[s] = -1;
+    }
+    __syncwarp();
+    if (key >= 0 && key < E && lane == __ffs(m) - 1) run[key] += __popc(m);
+    __syncwarp();
+  }
+}
+
+}  // namespace
+}  // namespace moe
+
+using namespace moe;
+
+extern "C" int64_t moe_tile_grid(int64_t num_tokens, int num_experts, int block_m) {
+  if (block_m <= 0 || num_tokens < 0 || num_experts <= 0) return -1;
+  return ceil_div(num_tokens, block_m) + num_experts;
+}
+
+extern "C" int64_t moe_tile_table_ints(int num_experts, int64_t max_tiles) {
+  return TileTable::ints(num_experts, max_tiles);
+}
+
+extern "C" int moe_tile_schedule(const void* group_sizes, int gs_dtype, int num_experts, int64_t num_tokens,
+                                 int block_m, int64_t* tile_expert, int64_t* tile_row_start,
+                                 int64_t* tile_row_count, int32_t* tile_table, void* stream) {
+  MOE_CHECK_ARG(group_sizes != nullptr, "moe_tile_schedule: group_sizes is NULL");
+  MOE_CHECK_ARG(gs_dtype == MOE_I32 || gs_dtype == MOE_I64, "moe_tile_schedule: group_sizes must be int32/int64");
+  MOE_CHECK_ARG(num_experts > 0 && num_experts <= 4096, "moe_tile_schedule: num_experts %d outside [1, 4096]",
+                num_experts);
+  MOE_CHECK_ARG(block_m > 0, "moe_tile_schedule: block_m must be positive");
+  MOE_CHECK_ARG(num_tokens >= 0 && num_tokens < (int64_t(1) << 31), "moe_tile_schedule: num_tokens out of range");
+  const int64_t grid = moe_tile_grid(num_tokens, num_experts, block_m);
+  const size_t smem = 2 * (num_experts + 1) * sizeof(int64_t);
+  if (smem > 48 * 1024)
+    MOE_CUDA_TRY(cudaFuncSetAttribute(tile_schedule_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  tile_schedule_kernel<<<1, kScanThreads, smem, as_stream(stream)>>>(group_sizes, gs_dtype == MOE_I64, num_experts,
+                                                                     block_m, grid, tile_expert, tile_row_start,
+                                                                     tile_row_count, tile_table);
+  MOE_LAUNCH_CHECK("tile_schedule_kernel");
+  return MOE_OK;
+}
+
+namespace {
+struct AlignWs {
+  int64_t chunks;
+  size_t hist_off, base_off, totals_off, bytes;
+};
+AlignWs align_ws(int64_t S, int E) {
+  AlignWs w;
+  w.chunks = ceil_div(S, kChunk);
+  const size_t col = (size_t)(E + 1) * sizeof(int32_t);
+  w.hist_off = 0;
+  w.base_off = align_up(w.chunks * col, 256);
+  w.totals_off = w.base_off + align_up(w.chunks * col, 256);
+  w.bytes = w.totals_off + align_up(col, 256);
+  return w;
+}
+}  // namespace
+
+extern "C" int64_t moe_align_capacity(int64_t num_slots, int num_experts, int block_m) {
+  if (num_slots < 0 || num_experts <= 0 || block_m <= 0) return -1;
+  // every expert's segment is padded by at most block_m - 1 rows; round the
+  // total up to whole tiles so TMA boxes of block_m rows stay in bounds.
+  int64_t cap = num_slots + (int64_t)num_experts * (block_m - 1);
+  return ceil_div(cap, block_m) * block_m;
+}
+
+extern "C" size_t moe_align_workspace_size(int64_t num_tokens, int top_k, int num_experts, int block_m) {
+  (void)block_m;
+  if (num_tokens < 0 || top_k <= 0 || num_experts <= 0) return 0;
+  return align_ws(num_tokens * top_k, num_experts).bytes;
+}
+
+extern "C" int moe_align(const int32_t* topk_ids, int64_t num_tokens, int top_k, int num_experts, int block_m,
+                         int32_t* sorted_slots, int32_t* slot_pos, int32_t* group_sizes, int32_t* padded_offsets,
+                         int32_t* tile_table, void* workspace, size_t workspace_bytes, void* stream) {
+  MOE_CHECK_ARG(num_tokens >= 0 && top_k > 0, "moe_align: bad num_tokens/top_k");
+  MOE_CHECK_ARG(num_experts > 0 && num_experts <= 4096, "moe_align: num_experts %d outside [1, 4096]",
+                num_experts);
+  MOE_CHECK_ARG(block_m > 0 && block_m <= 1024, "moe_align: block_m %d outside [1, 1024]", block_m);
+  const int64_t S = num_tokens * top_k;
+  MOE_CHECK_ARG(S < (int64_t(1) << 30), "moe_align: too many slots");
+  MOE_CHECK_ARG(S == 0 || (topk_ids && slot_pos), "moe_align: NULL ids/slot_pos");
+  MOE_CHECK_ARG(sorted_slots && group_sizes && padded_offsets && tile_table, "moe_align: NULL output");
+  const AlignWs w = align_ws(S, num_experts);
+  if (workspace_bytes < w.bytes || (w.bytes && !workspace))
+    return set_error(MOE_ERR_WORKSPACE, "moe_align: workspace %zu < %zu bytes", workspace_bytes, w.bytes);
+  char* ws = static_cast<char*>(workspace);
+  int32_t* hist = reinterpret_cast<int32_t*>(ws + w.hist_off);
+  int32_t* base = reinterpret_cast<int32_t*>(ws + w.base_off);
+  int32_t* totals = reinterpret_cast<int32_t*>(ws + w.totals_off);
+  cudaStream_t st = as_stream(stream);
+  const int64_t max_tiles = moe_align_capacity(S, num_experts, block_m) / block_m;
+  const size_t hsmem = (num_experts + 1) * sizeof(int32_t);
+  if (w.chunks > 0) {
+    align_count_kernel<<<(unsigned)w.chunks, 32, hsmem, st>>>(topk_ids, S, num_experts, hist);
+    MOE_LAUNCH_CHECK("align_count_kernel");
+  }
+  align_colscan_kernel<<<num_experts + 1, kScanThreads, 0, st>>>(hist, (int)w.chunks, num_experts, base, totals);
+  MOE_LAUNCH_CHECK("align_colscan_kernel");
+  align_finalize_kernel<<<1, kScanThreads, 2 * hsmem, st>>>(totals, num_experts, block_m, max_tiles, group_sizes,
+                                                            padded_offsets, tile_table, sorted_slots);
+  MOE_LAUNCH_CHECK("align_finalize_kernel");
+  if (w.chunks > 0) {
+    align_scatter_kernel<<<(unsigned)w.chunks, 32, hsmem, st>>>(topk_ids, S, num_experts, base, padded_offsets,
+                                                                sorted_slots, slot_pos);
+    MOE_LAUNCH_CHECK("align_scatter_kernel");
+  }
+  return MOE_OK;
+}

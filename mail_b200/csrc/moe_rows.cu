@@ -1,0 +1,280 @@
+// Row-wise HBM-bound kernels around the grouped GEMMs: the permuting gather
+// (optionally fused with per-token int8 quantisation), the deterministic
+// weighted combine, and the fp32 -> output-dtype conversion.
+//
+// All of them move whole rows with 16-byte vector accesses, one warp per row,
+// grid-stride over rows with the grid sized as a multiple of the SM count.
+#include "common.cuh"
+
+namespace moe {
+namespace {
+
+template <typename T>
+struct Vec8;  // 8 elements of T
+template <>
+struct Vec8<__nv_bfloat16> {
+  using type = uint4;
+};
+template <>
+struct Vec8<__half> {
+  using type = uint4;
+};
+template <>
+struct Vec8<int8_t> {
+  using type = uint2;
+};
+
+__device__ __forceinline__ void load8(const __nv_bfloat16* p, float (&v)[8]) {
+  uint4 u = *reinterpret_cast<const uint4*>(p);
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float2 f = __bfloat1622float2(h[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+__device__ __forceinline__ void load8(const __half* p, float (&v)[8]) {
+  uint4 u = *reinterpret_cast<const uint4*>(p);
+  const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float2 f = __half22float2(h[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+__device__ __forceinline__ void load8(const float* p, float (&v)[8]) {
+  float4 a = *reinterpret_cast<const float4*>(p);
+  float4 b = *reinterpret_cast<const float4*>(p + 4);
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+  v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+__device__ __forceinline__ void store8(__nv_bfloat16* p, const float (&v)[8]) {
+  uint4 u;
+  __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+  *reinterpret_cast<uint4*>(p) = u;
+}
+__device__ __forceinline__ void store8(__half* p, const float (&v)[8]) {
+  uint4 u;
+  __half2* h = reinterpret_cast<__half2*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) h[i] = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
+  *reinterpret_cast<uint4*>(p) = u;
+}
+__device__ __forceinline__ void store8(float* p, const float (&v)[8]) {
+  *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+  *reinterpret_cast<float4*>(p + 4) = make_float4(v[4], v[5], v[6], v[7]);
+}
+
+// Copies 8 elements of T (16 bytes for 16-bit T, 32 bytes for fp32).
+template <typename T>
+__device__ __forceinline__ void copy8(const T* s, T* d) {
+  if constexpr (sizeof(T) == 4) {
+    *reinterpret_cast<float4*>(d) = *reinterpret_cast<const float4*>(s);
+    *reinterpret_cast<float4*>(d + 4) = *reinterpret_cast<const float4*>(s + 4);
+  } else {
+    *reinterpret_cast<uint4*>(d) = *reinterpret_cast<const uint4*>(s);
+  }
+}
+template <typename T>
+__device__ __forceinline__ void zero8(T* d) {
+  if constexpr (sizeof(T) == 4) {
+    *reinterpret_cast<float4*>(d) = make_float4(0.f, 0.f, 0.f, 0.f);
+    *reinterpret_cast<float4*>(d + 4) = make_float4(0.f, 0.f, 0.f, 0.f);
+  } else if constexpr (sizeof(T) == 2) {
+    *reinterpret_cast<uint4*>(d) = make_uint4(0, 0, 0, 0);
+  } else {
+    *reinterpret_cast<uint2*>(d) = make_uint2(0, 0);
+  }
+}
+
+// Per-token symmetric int8 quantisation of 8 values with a row scale:
+// q = clamp(rint(x / s), -127, 127), 0 when the row is all zeros.
+__device__ __forceinline__ uint2 quant8(const float (&v)[8], float scale) {
+  uint32_t w[2] = {0u, 0u};
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    int q = 0;
+    if (scale > 0.f) {
+      q = __float2int_rn(__fdiv_rn(v[i], scale));
+      q = max(-127, min(127, q));
+    }
+    w[i >> 2] |= (uint32_t)(q & 0xff) << (8 * (i & 3));
+  }
+  return make_uint2(w[0], w[1]);
+}
+
+template <typename Tin, typename Tout>
+__global__ void __launch_bounds__(256) gather_rows_kernel(const Tin* __restrict__ src, int64_t cols,
+                                                          const int32_t* __restrict__ slots, int top_k,
+                                                          int64_t rows, const int32_t* __restrict__ rows_dev,
+                                                          Tout* __restrict__ dst, float* __restrict__ dst_scale) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  int64_t limit = rows;
+  if (rows_dev) limit = min(limit, (int64_t)*rows_dev);
+  for (int64_t p = warp; p < limit; p += nwarps) {
+    const int64_t slot = slots ? (int64_t)slots[p] : p;
+    Tout* d = dst + p * cols;
+    if (slot < 0) {
+      for (int64_t c = lane * 8; c < cols; c += 256) zero8(d + c);
+      if constexpr (sizeof(Tout) == 1)
+        if (lane == 0 && dst_scale) dst_scale[p] = 0.f;
+      continue;
+    }
+    const Tin* s = src + (slot / top_k) * cols;
+    if constexpr (sizeof(Tout) == 1) {
+      float amax = 0.f;
+      for (int64_t c = lane * 8; c < cols; c += 256) {
+        float v[8];
+        load8(s + c, v);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+      const float scale = __fdiv_rn(amax, 127.0f);
+      for (int64_t c = lane * 8; c < cols; c += 256) {
+        float v[8];
+        load8(s + c, v);
+        *reinterpret_cast<uint2*>(d + c) = quant8(v, scale);
+      }
+      if (lane == 0 && dst_scale) dst_scale[p] = scale;
+    } else {
+      for (int64_t c = lane * 8; c < cols; c += 256) copy8(s + c, d + c);
+    }
+  }
+}
+
+template <typename To, typename Tacc>
+__global__ void __launch_bounds__(256) combine_rows_kernel(const To* __restrict__ o, int64_t hidden,
+                                                           const int32_t* __restrict__ slot_pos,
+                                                           const float* __restrict__ w, int64_t T, int k,
+                                                           Tacc* __restrict__ y) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t t = warp; t < T; t += nwarps) {
+    for (int64_t c = lane * 8; c < hidden; c += 256) {
+      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      for (int j = 0; j < k; ++j) {
+        const int32_t pos = slot_pos[t * k + j];
+        if (pos < 0) continue;
+        const float wj = w[t * k + j];
+        float v[8];
+        load8(o + (int64_t)pos * hidden + c, v);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[i] = fmaf(wj, v[i], acc[i]);
+      }
+      store8(y + t * hidden + c, acc);
+    }
+  }
+}
+
+template <typename Tout>
+__global__ void __launch_bounds__(256) convert_f32_kernel(const float* __restrict__ src, int64_t n8,
+                                                          Tout* __restrict__ dst) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += (int64_t)gridDim.x * blockDim.x) {
+    float v[8];
+    load8(src + i * 8, v);
+    store8(dst + i * 8, v);
+  }
+}
+
+unsigned row_grid(int64_t rows) {
+  const int64_t per_block = 8;  // warps per 256-thread block
+  int64_t blocks = ceil_div(rows, per_block);
+  const int64_t cap = (int64_t)num_sms() * 16;
+  if (blocks > cap) blocks = cap;
+  return (unsigned)(blocks < 1 ? 1 : blocks);
+}
+
+}  // namespace
+}  // namespace moe
+
+using namespace moe;
+
+extern "C" int moe_gather_rows(const void* src, int src_dtype, int64_t cols, const int32_t* sorted_slots,
+                               int top_k, int64_t rows, const int32_t* rows_dev, void* dst, int dst_dtype,
+                               float* dst_scale, void* stream) {
+  MOE_CHECK_ARG(src && dst, "moe_gather_rows: NULL src/dst");
+  MOE_CHECK_ARG(cols > 0 && cols % 8 == 0, "moe_gather_rows: cols (%lld) must be a positive multiple of 8",
+                (long long)cols);
+  MOE_CHECK_ARG(top_k > 0 && rows >= 0, "moe_gather_rows: bad top_k/rows");
+  MOE_CHECK_ARG(((uintptr_t)src % 16 == 0) && ((uintptr_t)dst % 16 == 0), "moe_gather_rows: pointers must be 16-byte aligned");
+  if (rows == 0) return MOE_OK;
+  cudaStream_t st = as_stream(stream);
+  const unsigned grid = row_grid(rows);
+#define GATHER(TI, TO)                                                                                     \
+  gather_rows_kernel<TI, TO><<<grid, 256, 0, st>>>(static_cast<const TI*>(src), cols, sorted_slots, top_k, \
+                                                   rows, rows_dev, static_cast<TO*>(dst), dst_scale)
+  if (dst_dtype == src_dtype) {
+    if (src_dtype == MOE_BF16) GATHER(__nv_bfloat16, __nv_bfloat16);
+    else if (src_dtype == MOE_F16) GATHER(__half, __half);
+    else if (src_dtype == MOE_F32) GATHER(float, float);
+    else return set_error(MOE_ERR_UNSUPPORTED, "moe_gather_rows: dtype %d not supported", src_dtype);
+  } else if (dst_dtype == MOE_I8) {
+    MOE_CHECK_ARG(dst_scale != nullptr, "moe_gather_rows: int8 output needs dst_scale");
+    if (src_dtype == MOE_BF16) GATHER(__nv_bfloat16, int8_t);
+    else if (src_dtype == MOE_F16) GATHER(__half, int8_t);
+    else if (src_dtype == MOE_F32) GATHER(float, int8_t);
+    else return set_error(MOE_ERR_UNSUPPORTED, "moe_gather_rows: dtype %d not supported", src_dtype);
+  } else {
+    return set_error(MOE_ERR_UNSUPPORTED, "moe_gather_rows: %d -> %d not supported", src_dtype, dst_dtype);
+  }
+#undef GATHER
+  MOE_LAUNCH_CHECK("gather_rows_kernel");
+  return MOE_OK;
+}
+
+extern "C" int moe_quant_rows(const void* src, int src_dtype, int64_t rows, int64_t cols, const int32_t* rows_dev,
+                              int8_t* dst, float* dst_scale, void* stream) {
+  return moe_gather_rows(src, src_dtype, cols, nullptr, 1, rows, rows_dev, dst, MOE_I8, dst_scale, stream);
+}
+
+extern "C" int moe_combine_rows(const void* o, int o_dtype, int64_t hidden, const int32_t* slot_pos,
+                                const float* topk_weights, int64_t num_tokens, int top_k, void* y, int y_dtype,
+                                void* stream) {
+  MOE_CHECK_ARG(o && slot_pos && topk_weights && y, "moe_combine_rows: NULL pointer");
+  MOE_CHECK_ARG(hidden > 0 && hidden % 8 == 0, "moe_combine_rows: hidden must be a positive multiple of 8");
+  MOE_CHECK_ARG(num_tokens >= 0 && top_k > 0, "moe_combine_rows: bad num_tokens/top_k");
+  if (num_tokens == 0) return MOE_OK;
+  cudaStream_t st = as_stream(stream);
+  const unsigned grid = row_grid(num_tokens);
+#define COMBINE(TO, TY)                                                                                    \
+  combine_rows_kernel<TO, TY><<<grid, 256, 0, st>>>(static_cast<const TO*>(o), hidden, slot_pos, topk_weights, \
+                                                    num_tokens, top_k, static_cast<TY*>(y))
+  if (o_dtype == MOE_BF16 && y_dtype == MOE_BF16) COMBINE(__nv_bfloat16, __nv_bfloat16);
+  else if (o_dtype == MOE_F16 && y_dtype == MOE_F16) COMBINE(__half, __half);
+  else if (o_dtype == MOE_F32 && y_dtype == MOE_F32) COMBINE(float, float);
+  else if (o_dtype == MOE_BF16 && y_dtype == MOE_F32) COMBINE(__nv_bfloat16, float);
+  else return set_error(MOE_ERR_UNSUPPORTED, "moe_combine_rows: %d -> %d not supported", o_dtype, y_dtype);
+#undef COMBINE
+  MOE_LAUNCH_CHECK("combine_rows_kernel");
+  return MOE_OK;
+}
+
+extern "C" int moe_convert_f32(const float* src, int64_t n, void* dst, int dst_dtype, void* stream) {
+  MOE_CHECK_ARG(src && dst, "moe_convert_f32: NULL pointer");
+  MOE_CHECK_ARG(n >= 0 && n % 8 == 0, "moe_convert_f32: n must be a multiple of 8");
+  if (n == 0) return MOE_OK;
+  cudaStream_t st = as_stream(stream);
+  const int64_t n8 = n / 8;
+  int64_t blocks = ceil_div(n8, 256);
+  const int64_t cap = (int64_t)num_sms() * 8;
+  if (blocks > cap) blocks = cap;
+  if (dst_dtype == MOE_BF16)
+    convert_f32_kernel<__nv_bfloat16><<<(unsigned)blocks, 256, 0, st>>>(src, n8, static_cast<__nv_bfloat16*>(dst));
+  else if (dst_dtype == MOE_F16)
+    convert_f32_kernel<__half><<<(unsigned)blocks, 256, 0, st>>>(src, n8, static_cast<__half*>(dst));
+  else if (dst_dtype == MOE_F32)
+    convert_f32_kernel<float><<<(unsigned)blocks, 256, 0, st>>>(src, n8, static_cast<float*>(dst));
+  else
+    return set_error(MOE_ERR_UNSUPPORTED, "moe_convert_f32: dtype %d not supported", dst_dtype);
+  MOE_LAUNCH_CHECK("convert_f32_kernel");
+  return MOE_OK;
+}

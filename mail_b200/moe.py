@@ -1,0 +1,260 @@
+"""Host-side mirror of the reference's fused_moe_mlp interface.
+
+`fused_moe_mlp` keeps the reference's call signature
+(fused_moe_mlp_triton.py:121-130, called from sglang at unquant_diff.txt:13-18)
+and adds the north-star top-k form:
+
+    fused_moe_mlp(x, w13, w2, group_sizes)                      # pre-routed rows
+    fused_moe_mlp(hidden_states, w13, w2, topk_weights, topk_ids, scales=None)
+
+Weights use the reference's logical "(E, K, N)" layout: w13[E, H, 2I] (gate =
+first I columns) and w2[E, I, H]. The sm_100a kernels read them K-major, i.e.
+physically [E, 2I, H] / [E, H, I] — exactly what transpose(1, 2) of nn.Linear
+weights gives (kernel_bench.py:229-235) — so such views are used without a
+copy; any other stride pattern is made K-major with one copy per call (use
+`prepack_weights` once at load time instead).
+
+Every op runs the CUDA kernels of libmoe_b200.so through its C ABI on the
+current torch stream. There is no CPU or PyTorch fallback: a missing library
+or a non-CUDA tensor raises.
+"""
+from __future__ import annotations
+
+import warnings
+
+import torch
+
+from . import _lib
+
+_DT = {torch.float32: _lib.F32, torch.float16: _lib.F16, torch.bfloat16: _lib.BF16, torch.int8: _lib.I8,
+       torch.int32: _lib.I32, torch.int64: _lib.I64}
+BLOCK_M = 128  # M tile of the tcgen05 kernels
+
+
+def _code(t: torch.Tensor) -> int:
+    try:
+        return _DT[t.dtype]
+    except KeyError:
+        raise TypeError(f"unsupported dtype {t.dtype}") from None
+
+
+def _stream(dev: torch.device) -> int:
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _require_cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise ValueError("mail_b200 ops run on CUDA tensors only (no CPU fallback)")
+
+
+def _workspace(nbytes: int, dev) -> torch.Tensor:
+    return torch.empty(max(int(nbytes), 1), dtype=torch.uint8, device=dev)
+
+
+_warned_copy = False
+
+
+def kmajor(w: torch.Tensor) -> torch.Tensor:
+    """Logical (E, K, N) weight -> contiguous K-major [E, N, K] storage."""
+    global _warned_copy
+    wt = w.transpose(1, 2)
+    if wt.is_contiguous():
+        return wt
+    if not _warned_copy:
+        warnings.warn("fused_moe_mlp: weights are not K-major; copying them on every call "
+                      "(call prepack_weights once at load time)", stacklevel=3)
+        _warned_copy = True
+    return wt.contiguous()
+
+
+def prepack_weights(w13: torch.Tensor, w2: torch.Tensor):
+    """Returns (w13, w2) logical views whose storage is K-major, copying once
+    if needed; pass the results to fused_moe_mlp."""
+    return (w13.transpose(1, 2).contiguous().transpose(1, 2), w2.transpose(1, 2).contiguous().transpose(1, 2))
+
+
+def weights_from_linear(w13_linear: torch.Tensor, w2_linear: torch.Tensor):
+    """nn.Linear-layout weights (w13 [E, 2I, H], w2 [E, H, I]) -> logical
+    (E, K, N) views with no copy (kernel_bench.py:229-235)."""
+    return w13_linear.transpose(1, 2), w2_linear.transpose(1, 2)
+
+
+# ---------------------------------------------------------------------------
+# Building blocks (each one C-ABI call)
+
+
+def build_tile_schedule(group_sizes: torch.Tensor, num_tokens: int, BLOCK_M: int = BLOCK_M):
+    """Device restatement of build_tile_schedule (fused_moe_mlp_triton.py:91-119).
+
+    Returns (tile_expert, tile_row_start, tile_row_count) int64 tensors on
+    group_sizes' device and the static grid size cdiv(num_tokens, BLOCK_M) + E.
+    """
+    _require_cuda(group_sizes)
+    gs = group_sizes.contiguous()
+    if gs.dtype not in (torch.int32, torch.int64):
+        gs = gs.to(torch.int64)
+    E = gs.numel()
+    grid = int(_lib.query("moe_tile_grid", int(num_tokens), E, int(BLOCK_M)))
+    if grid < 0:
+        raise ValueError("build_tile_schedule: bad arguments")
+    dev = gs.device
+    te = torch.empty(grid, dtype=torch.int64, device=dev)
+    ts = torch.empty(grid, dtype=torch.int64, device=dev)
+    tc = torch.empty(grid, dtype=torch.int64, device=dev)
+    _lib.call("moe_tile_schedule", gs.data_ptr(), _code(gs), E, int(num_tokens), int(BLOCK_M), te.data_ptr(),
+              ts.data_ptr(), tc.data_ptr(), None, _stream(dev))
+    return te, ts, tc, grid
+
+
+def moe_align(topk_ids: torch.Tensor, num_experts: int, block_m: int = BLOCK_M) -> dict:
+    """Stable block-padded sort of the T*k slots by expert (see moe_b200.h).
+
+    Returns dict(sorted_slots, slot_pos, group_sizes, padded_offsets,
+    tile_table, capacity, max_tiles).
+    """
+    _require_cuda(topk_ids)
+    ids = topk_ids.to(torch.int32).contiguous()
+    T, k = ids.shape
+    S = T * k
+    dev = ids.device
+    cap = int(_lib.query("moe_align_capacity", S, num_experts, block_m))
+    max_tiles = cap // block_m
+    sorted_slots = torch.empty(max(cap, 1), dtype=torch.int32, device=dev)
+    slot_pos = torch.empty(max(S, 1), dtype=torch.int32, device=dev)
+    gs = torch.empty(num_experts, dtype=torch.int32, device=dev)
+    poff = torch.empty(num_experts + 1, dtype=torch.int32, device=dev)
+    table = torch.empty(int(_lib.query("moe_tile_table_ints", num_experts, max_tiles)), dtype=torch.int32,
+                        device=dev)
+    ws = _workspace(_lib.query("moe_align_workspace_size", T, k, num_experts, block_m), dev)
+    _lib.call("moe_align", ids.data_ptr(), T, k, num_experts, block_m, sorted_slots.data_ptr(), slot_pos.data_ptr(),
+              gs.data_ptr(), poff.data_ptr(), table.data_ptr(), ws.data_ptr(), ws.numel(), _stream(dev))
+    return dict(sorted_slots=sorted_slots, slot_pos=slot_pos[:S], group_sizes=gs, padded_offsets=poff,
+                tile_table=table, capacity=cap, max_tiles=max_tiles)
+
+
+def quant_int8_rows(x: torch.Tensor):
+    """Per-row int8: s = absmax / 127, q = clamp(rint(x / s), -127, 127)."""
+    _require_cuda(x)
+    x = x.contiguous()
+    R, C = x.shape
+    q = torch.empty((R, C), dtype=torch.int8, device=x.device)
+    s = torch.empty(max(R, 1), dtype=torch.float32, device=x.device)
+    _lib.call("moe_quant_rows", x.data_ptr(), _code(x), R, C, None, q.data_ptr(), s.data_ptr(), _stream(x.device))
+    return q, s[:R]
+
+
+def gather_rows(src: torch.Tensor, sorted_slots: torch.Tensor, top_k: int, rows: int, out_dtype=None,
+                rows_dev: torch.Tensor | None = None):
+    """dst[p] = src[sorted_slots[p] // top_k] (zero rows for negative slots);
+    out_dtype=torch.int8 quantises each row (returns (q, scale))."""
+    _require_cuda(src, sorted_slots)
+    src = src.contiguous()
+    out_dtype = out_dtype or src.dtype
+    dst = torch.empty((rows, src.shape[1]), dtype=out_dtype, device=src.device)
+    scale = torch.empty(max(rows, 1), dtype=torch.float32, device=src.device) if out_dtype == torch.int8 else None
+    _lib.call("moe_gather_rows", src.data_ptr(), _code(src), src.shape[1], sorted_slots.data_ptr(), top_k, rows,
+              _ptr(rows_dev), dst.data_ptr(), _code(dst), _ptr(scale), _stream(src.device))
+    return (dst, scale[:rows]) if scale is not None else dst
+
+
+def quantize_weights_int8(w13: torch.Tensor, w2: torch.Tensor):
+    """Load-time w8a8 weight prep (not on the hot path): logical (E, K, N)
+    weights -> int8 logical views with K-major storage and per-output-channel
+    fp32 scales = absmax / 127 (round-half-even). Returns
+    (w13_q, w2_q, (w13_scale [E, 2I], w2_scale [E, H]))."""
+    def q(w):
+        wk = w.transpose(1, 2).float()                    # [E, N, K]
+        s = wk.abs().amax(dim=2) / 127.0                  # [E, N]
+        qq = torch.where(s[..., None] > 0, torch.round(wk / s[..., None]), torch.zeros_like(wk))
+        return qq.clamp_(-127, 127).to(torch.int8).contiguous().transpose(1, 2), s.contiguous()
+    a, sa = q(w13)
+    b, sb = q(w2)
+    return a, b, (sa, sb)
+
+
+# ---------------------------------------------------------------------------
+# The op
+
+
+def fused_moe_mlp(x: torch.Tensor, w13: torch.Tensor, w2: torch.Tensor, group_sizes_or_topk_weights: torch.Tensor,
+                  topk_ids: torch.Tensor | None = None, scales=None, BLOCK_M: int = 128, BLOCK_N: int = 128,
+                  BLOCK_N2: int = 256, BLOCK_K: int = 256) -> torch.Tensor:
+    """Fused expert MLP: grouped GEMM(x, w13) -> silu(gate) * up -> grouped GEMM(., w2).
+
+    Pre-routed form (topk_ids is None) — drop-in for the reference
+    (fused_moe_mlp_triton.py:121-160): x [S, H] grouped by expert,
+    group_sizes [E]; returns [S, H] in x.dtype (rows beyond sum(group_sizes)
+    are zero). dtypes: bf16, fp16, fp32 (fp32 runs on tf32 tensor cores).
+
+    Top-k form: x [T, H], topk_weights [T, k] (fp32), topk_ids [T, k]; returns
+    y [T, H] = sum_j topk_weights[t, j] * MLP_{topk_ids[t, j]}(x[t]) in x.dtype.
+    int8 w13/w2 select w8a8 with scales=(w13_scale [E, 2I], w2_scale [E, H])
+    and dynamic per-token activation quantisation.
+
+    BLOCK_* are accepted for signature compatibility; the sm_100a kernels use
+    fixed 128 x 256 tiles and results do not depend on them.
+    """
+    del BLOCK_M, BLOCK_N, BLOCK_N2, BLOCK_K
+    _require_cuda(x, w13, w2, group_sizes_or_topk_weights, topk_ids)
+    if x.dim() != 2 or w13.dim() != 3 or w2.dim() != 3:
+        raise ValueError("fused_moe_mlp: expected x [T, H], w13 [E, H, 2I], w2 [E, I, H]")
+    T, H = x.shape
+    E, Hw, two_i = w13.shape
+    inter = two_i // 2
+    if Hw != H or two_i != 2 * inter or tuple(w2.shape) != (E, inter, H):
+        raise ValueError(f"fused_moe_mlp: shape mismatch x{tuple(x.shape)} w13{tuple(w13.shape)} "
+                         f"w2{tuple(w2.shape)} (expected w13 [E, H, 2I], w2 [E, I, H])")
+    x = x.contiguous()
+    w13k, w2k = kmajor(w13), kmajor(w2)
+    dev = x.device
+    st = _stream(dev)
+    if topk_ids is None:
+        gs = group_sizes_or_topk_weights
+        if gs.numel() != E:
+            raise ValueError("fused_moe_mlp: group_sizes must have E entries")
+        if gs.dtype not in (torch.int32, torch.int64):
+            gs = gs.to(torch.int64)
+        gs = gs.contiguous()
+        if w13.dtype != x.dtype or w2.dtype != x.dtype:
+            raise TypeError("fused_moe_mlp: x, w13 and w2 must share a dtype")
+        out = torch.empty((T, H), dtype=x.dtype, device=dev)
+        ws = _workspace(_lib.query("moe_fused_mlp_workspace_size", T, H, inter, E, _code(x), 128), dev)
+        _lib.call("moe_fused_mlp", x.data_ptr(), _code(x), T, H, w13k.data_ptr(), w2k.data_ptr(), E, inter,
+                  gs.data_ptr(), _code(gs), 128, out.data_ptr(), ws.data_ptr(), ws.numel(), st)
+        return out
+
+    topk_weights = group_sizes_or_topk_weights.to(torch.float32).contiguous()
+    ids = topk_ids.to(torch.int32).contiguous()
+    if topk_weights.shape != ids.shape or ids.dim() != 2 or ids.shape[0] != T:
+        raise ValueError("fused_moe_mlp: topk_weights/topk_ids must both be [T, k]")
+    k = ids.shape[1]
+    w_code = _code(w13)
+    s13 = s2 = None
+    if w13.dtype == torch.int8:
+        if scales is None:
+            raise ValueError("fused_moe_mlp: int8 weights need scales=(w13_scale, w2_scale)")
+        s13, s2 = (s.to(torch.float32).contiguous() for s in scales)
+        if tuple(s13.shape) != (E, 2 * inter) or tuple(s2.shape) != (E, H):
+            raise ValueError("fused_moe_mlp: scales must be w13_scale [E, 2I] and w2_scale [E, H]")
+    elif w13.dtype != x.dtype or w2.dtype != x.dtype:
+        raise TypeError("fused_moe_mlp: weights must share x's dtype or be int8")
+    y = torch.empty((T, H), dtype=x.dtype, device=dev)
+    ws = _workspace(_lib.query("moe_fused_experts_workspace_size", T, H, inter, E, k, _code(x), w_code), dev)
+    _lib.call("moe_fused_experts", x.data_ptr(), _code(x), T, H, w13k.data_ptr(), w2k.data_ptr(), w_code, E, inter,
+              topk_weights.data_ptr(), ids.data_ptr(), k, _ptr(s13), _ptr(s2), y.data_ptr(), ws.data_ptr(),
+              ws.numel(), st)
+    return y
+
+
+def device_error(device=None) -> int:
+    """Reads and clears the kernels' device error flag (synchronises)."""
+    import ctypes
+    dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    code = ctypes.c_int(0)
+    _lib.call("moe_get_device_error", ctypes.addressof(code), _stream(dev))
+    return code.value

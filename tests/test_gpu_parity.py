@@ -1,0 +1,291 @@
+"""GPU parity: the sm_100a kernels (through the C ABI) against the oracle and
+the reference's golden vectors.
+
+Bars: integer/index work (tile schedule, align, int8 quant) bit-exact;
+floating-point outputs within max-abs-rel error 1e-2 of an fp32 reference
+(max |y - ref| / max |ref|), the north-star tolerance for bf16 outputs.
+"""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import mail_b200 as mb
+from mail_b200 import _lib
+from oracle import moe_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
+TOL = 1e-2  # max-abs-rel error bound for bf16/fp16/tf32 outputs
+
+
+def max_abs_rel(y, ref):
+    y = np.asarray(y, np.float64)
+    ref = np.asarray(ref, np.float64)
+    return float(np.abs(y - ref).max() / max(np.abs(ref).max(), 1e-30))
+
+
+def npf(t):
+    return t.detach().float().cpu().numpy()
+
+
+def dev():
+    return torch.device("cuda", 0)
+
+
+def assert_no_device_error():
+    assert mb.device_error(dev()) == 0
+
+
+# --------------------------------------------------------------------------- tile schedule
+
+
+def schedule_cases():
+    t = np.load(os.path.join(GOLDEN, "tile_schedule.npz"))
+    names = sorted({k.split("/")[0] for k in t.files})
+    return [(n, bm) for n in names for bm in (16, 32, 64, 128, 256)]
+
+
+@pytest.mark.parametrize("name,bm", schedule_cases())
+def test_tile_schedule_matches_reference_bit_exact(name, bm):
+    t = np.load(os.path.join(GOLDEN, "tile_schedule.npz"))
+    gs = t[f"{name}/group_sizes"]
+    for dt in (torch.int64, torch.int32):
+        g = torch.tensor(gs, dtype=dt, device=dev())
+        te, ts, tc, grid = mb.build_tile_schedule(g, int(gs.sum()), bm)
+        assert grid == int(t[f"{name}/bm{bm}/grid"])
+        np.testing.assert_array_equal(te.cpu().numpy(), t[f"{name}/bm{bm}/expert"])
+        np.testing.assert_array_equal(ts.cpu().numpy(), t[f"{name}/bm{bm}/row_start"])
+        np.testing.assert_array_equal(tc.cpu().numpy(), t[f"{name}/bm{bm}/row_count"])
+        exact = int(t[f"{name}/bm{bm}/exact_grid"])
+        np.testing.assert_array_equal(ts.cpu().numpy()[:exact], t[f"{name}/bm{bm}/exact_row_start"])
+
+
+# --------------------------------------------------------------------------- align
+
+
+ALIGN_CASES = [
+    ("uniform", 64, 2, 8), ("uniform", 4096, 2, 8), ("uniform", 1, 8, 128), ("zipf", 257, 8, 128),
+    ("uniform", 8192, 8, 256), ("hot", 5000, 6, 64), ("invalid", 300, 4, 16), ("one_expert", 1000, 1, 32),
+]
+
+
+def make_ids(kind, T, k, E, seed=0):
+    rng = np.random.default_rng(seed)
+    if kind == "uniform":
+        return np.argsort(rng.random((T, E)), axis=1)[:, :k].astype(np.int32)
+    if kind == "zipf":
+        return O.synthetic_routing("zipf1.2", T, E, k, seed)[0]
+    if kind == "hot":
+        return O.synthetic_routing("hot25-zipf1.0", T, E, k, seed)[0]
+    if kind == "invalid":
+        return rng.integers(-2, E + 3, size=(T, k)).astype(np.int32)
+    if kind == "one_expert":
+        return np.full((T, k), E - 1, np.int32)
+    raise ValueError(kind)
+
+
+@pytest.mark.parametrize("kind,T,k,E", ALIGN_CASES)
+def test_align_bit_exact(kind, T, k, E):
+    ids = make_ids(kind, T, k, E)
+    ref = O.align(ids, E, 128)
+    got = mb.moe_align(torch.from_numpy(ids).to(dev()), E, 128)
+    table = got["tile_table"].cpu().numpy()
+    n = ref["num_tiles"]
+    total = int(ref["padded_offsets"][-1])
+    assert table[0] == n and table[1] == total and table[2] == ref["dropped"]
+    np.testing.assert_array_equal(got["group_sizes"].cpu().numpy(), ref["group_sizes"])
+    np.testing.assert_array_equal(got["padded_offsets"].cpu().numpy(), ref["padded_offsets"])
+    np.testing.assert_array_equal(got["sorted_slots"].cpu().numpy()[:total], ref["sorted_slots"])
+    np.testing.assert_array_equal(got["slot_pos"].cpu().numpy(), ref["slot_pos"])
+    mt = got["max_tiles"]
+    np.testing.assert_array_equal(table[4:4 + E + 1], ref["tile_cumsum"])
+    np.testing.assert_array_equal(table[5 + E:5 + E + n], ref["tile_row_start"])
+    np.testing.assert_array_equal(table[5 + E + mt:5 + E + mt + n], ref["tile_row_count"])
+
+
+# --------------------------------------------------------------------------- quant / gather
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+def test_quant_int8_rows_bit_exact(dtype):
+    rng = np.random.default_rng(4)
+    x = rng.standard_normal((300, 1024), dtype=np.float32) * rng.uniform(0.01, 10, size=(300, 1)).astype(np.float32)
+    x[7] = 0.0
+    x[11, :5] = [0.5, -0.5, 1.5, 2.5, 127.0]
+    xt = torch.from_numpy(x).to(dev(), dtype)
+    q, s = mb.quant_int8_rows(xt)
+    q_ref, s_ref = O.quant_int8_rows(npf(xt))
+    np.testing.assert_array_equal(s.cpu().numpy(), s_ref)
+    np.testing.assert_array_equal(q.cpu().numpy(), q_ref)
+
+
+def test_gather_rows_bit_exact():
+    rng = np.random.default_rng(5)
+    T, k, H, E = 100, 3, 256, 7
+    x = torch.from_numpy(rng.standard_normal((T, H), dtype=np.float32)).to(dev(), torch.bfloat16)
+    ids = make_ids("uniform", T, k, E)
+    a = mb.moe_align(torch.from_numpy(ids).to(dev()), E, 128)
+    rows = a["capacity"]
+    xp = mb.gather_rows(x, a["sorted_slots"], k, rows, rows_dev=a["tile_table"][1:2])
+    ref = O.align(ids, E, 128)
+    total = int(ref["padded_offsets"][-1])
+    xs = ref["sorted_slots"]
+    expect = np.where(xs[:, None] >= 0, npf(x)[np.maximum(xs, 0) // k], 0.0)
+    np.testing.assert_array_equal(npf(xp[:total]), expect)
+    qp, sp = mb.gather_rows(x, a["sorted_slots"], k, rows, out_dtype=torch.int8, rows_dev=a["tile_table"][1:2])
+    q_ref, s_ref = O.quant_int8_rows(expect)
+    np.testing.assert_array_equal(qp[:total].cpu().numpy(), q_ref)
+    np.testing.assert_array_equal(sp[:total].cpu().numpy(), s_ref)
+
+
+# --------------------------------------------------------------------------- pre-routed form
+
+
+@pytest.mark.parametrize("case", ["mlp_selfcheck_f32", "mlp_selftest_f16", "mlp_ragged_f32"])
+@pytest.mark.parametrize("dtype", [None, torch.bfloat16])
+def test_pre_routed_matches_reference_golden(case, dtype):
+    d = np.load(os.path.join(GOLDEN, case + ".npz"))
+    dt = dtype or {np.float16: torch.float16, np.float32: torch.float32}[d["x"].dtype.type]
+    x = torch.from_numpy(d["x"]).to(dev(), dt)
+    # reference layout: logical (E, K, N) view over nn.Linear-style storage
+    w13 = torch.from_numpy(d["w13"]).to(dev(), dt).transpose(1, 2).contiguous().transpose(1, 2)
+    w2 = torch.from_numpy(d["w2"]).to(dev(), dt).transpose(1, 2).contiguous().transpose(1, 2)
+    gs = torch.from_numpy(d["group_sizes"]).to(dev())
+    out = mb.fused_moe_mlp(x, w13, w2, gs)
+    assert out.dtype == dt and out.shape == x.shape
+    if dtype is None:
+        ref = d["ref_golden_loop"]  # the reference's own fp32 golden loop
+    else:
+        ref = O.moe_mlp_grouped(npf(x), npf(w13), npf(w2), d["group_sizes"])
+    err = max_abs_rel(npf(out), ref)
+    assert err < TOL, err
+    assert_no_device_error()
+
+
+def test_pre_routed_non_kmajor_weights_and_tail_rows():
+    rng = np.random.default_rng(9)
+    E, H, I = 3, 256, 384
+    gs = np.array([100, 0, 77])
+    T = int(gs.sum()) + 20  # 20 rows no group covers -> zero (reference zero-inits its output)
+    x = torch.from_numpy(rng.standard_normal((T, H), dtype=np.float32)).to(dev(), torch.bfloat16)
+    w13 = (torch.randn(E, H, 2 * I, device=dev()) * 0.05).to(torch.bfloat16)  # N-contiguous: copied
+    w2 = (torch.randn(E, I, H, device=dev()) * 0.05).to(torch.bfloat16)
+    out = mb.fused_moe_mlp(x, w13, w2, torch.from_numpy(gs).to(dev()))
+    ref = O.moe_mlp_grouped(npf(x), npf(w13), npf(w2), gs)
+    assert max_abs_rel(npf(out), ref) < TOL
+    assert (npf(out)[int(gs.sum()):] == 0).all()
+
+
+# --------------------------------------------------------------------------- top-k form
+
+
+def topk_case(T, H, I, E, k, routing, dtype, seed=0, w_std=0.02):
+    rng = np.random.default_rng(seed)
+    x = torch.from_numpy(rng.standard_normal((T, H), dtype=np.float32)).to(dev(), dtype)
+    w13 = torch.from_numpy((rng.standard_normal((E, 2 * I, H), dtype=np.float32) * w_std)).to(dev(), dtype)
+    w2 = torch.from_numpy((rng.standard_normal((E, H, I), dtype=np.float32) * w_std)).to(dev(), dtype)
+    ids, wts = O.synthetic_routing(routing, T, E, k, seed)
+    return x, w13.transpose(1, 2), w2.transpose(1, 2), ids, wts
+
+
+def run_topk(x, w13, w2, ids, wts, scales=None):
+    return mb.fused_moe_mlp(x, w13, w2, torch.from_numpy(wts).to(dev()), torch.from_numpy(ids).to(dev()),
+                            scales=scales)
+
+
+@pytest.mark.parametrize("T,H,I,E,k,routing,dtype", [
+    (64, 1024, 512, 8, 2, "uniform-softmax", torch.float32),    # config 1: tiny fp32 (tf32 tensor cores)
+    (64, 1024, 512, 8, 2, "uniform-softmax", torch.bfloat16),
+    (300, 512, 384, 16, 4, "sigmoid", torch.float16),
+    (1, 2048, 768, 128, 8, "zipf1.2", torch.bfloat16),          # config 3 decode shapes
+    (32, 2048, 768, 128, 8, "zipf1.2", torch.bfloat16),
+    (256, 2048, 768, 128, 8, "zipf1.2", torch.bfloat16),
+    (777, 256, 136, 6, 3, "uniform-softmax", torch.bfloat16),   # ragged I (not a multiple of 128)
+])
+def test_topk_matches_oracle(T, H, I, E, k, routing, dtype):
+    x, w13, w2, ids, wts = topk_case(T, H, I, E, k, routing, dtype)
+    y = run_topk(x, w13, w2, ids, wts)
+    assert y.dtype == dtype and y.shape == (T, H)
+    rnd = None if dtype == torch.float32 else (O.round_bf16 if dtype == torch.bfloat16 else O.round_fp16)
+    ref = O.moe_mlp_topk(npf(x), npf(w13), npf(w2), wts, ids, round_hidden=rnd)
+    err = max_abs_rel(npf(y), ref)
+    assert err < TOL, err
+    assert_no_device_error()
+
+
+def test_topk_drops_out_of_range_ids():
+    x, w13, w2, ids, wts = topk_case(128, 256, 128, 4, 2, "uniform-softmax", torch.bfloat16)
+    ids = ids.copy()
+    ids[::3, 1] = -1      # expert-parallel style "not mine"
+    ids[5, 0] = 99
+    y = run_topk(x, w13, w2, ids, wts)
+    ref = O.moe_mlp_topk(npf(x), npf(w13), npf(w2), wts, ids, round_hidden=O.round_bf16)
+    assert max_abs_rel(npf(y), ref) < TOL
+
+
+def test_w8a8_matches_oracle():
+    T, H, I, E, k = 256, 512, 256, 16, 4
+    x, w13, w2, ids, wts = topk_case(T, H, I, E, k, "sigmoid", torch.bfloat16, seed=3)
+    w13q, w2q, scales = mb.quantize_weights_int8(w13, w2)
+    q13, s13 = O.quantize_weight_per_channel(np.swapaxes(npf(w13), 1, 2))
+    np.testing.assert_array_equal(w13q.transpose(1, 2).cpu().numpy(), q13)
+    np.testing.assert_array_equal(scales[0].cpu().numpy(), s13)
+    q2, s2 = O.quantize_weight_per_channel(np.swapaxes(npf(w2), 1, 2))
+    y = run_topk(x, w13q, w2q, ids, wts, scales=scales)
+    ref = O.moe_mlp_w8a8(npf(x), q13, s13, q2, s2, wts, ids, round_hidden=O.round_bf16)
+    err = max_abs_rel(npf(y), ref)
+    assert err < TOL, err
+    # and against the unquantised fp32 MLP (quantisation error only)
+    ref_f = O.moe_mlp_topk(npf(x), npf(w13), npf(w2), wts, ids)
+    assert max_abs_rel(npf(y), ref_f) < 5e-2
+    assert_no_device_error()
+
+
+# --------------------------------------------------------------------------- full size (Mixtral layer)
+
+
+def test_mixtral_full_size_sampled_and_properties():
+    """T=4096, H=4096, I=14336, E=8, top-2, bf16: sampled tokens against an fp32
+    torch reference of the same op, plus size-independent properties."""
+    T, H, I, E, k = 4096, 4096, 14336, 8, 2
+    g = torch.Generator(device=dev()).manual_seed(0)
+    x = torch.randn(T, H, device=dev(), generator=g).to(torch.bfloat16)
+    w13 = (torch.randn(E, 2 * I, H, device=dev(), generator=g) * 0.02).to(torch.bfloat16)
+    w2 = (torch.randn(E, H, I, device=dev(), generator=g) * 0.02).to(torch.bfloat16)
+    ids, wts = O.synthetic_routing("uniform-softmax", T, E, k, 0)
+    ids_t, wts_t = torch.from_numpy(ids).to(dev()), torch.from_numpy(wts).to(dev())
+    y = mb.fused_moe_mlp(x, w13.transpose(1, 2), w2.transpose(1, 2), wts_t, ids_t)
+    torch.cuda.synchronize()
+    rng = np.random.default_rng(1)
+    sample = rng.choice(T, size=24, replace=False)
+    ref = torch.zeros(len(sample), H, device=dev())
+    for i, t in enumerate(sample):
+        for j in range(k):
+            e = int(ids[t, j])
+            gu = x[t].float() @ w13[e].float().t()
+            h = torch.nn.functional.silu(gu[:I]) * gu[I:]
+            h = h.to(torch.bfloat16).float()
+            ref[i] += float(wts[t, j]) * (h @ w2[e].float().t())
+    err = max_abs_rel(npf(y[torch.from_numpy(sample).to(dev())]), npf(ref))
+    assert err < TOL, err
+    # linearity in the routing weights
+    y2 = mb.fused_moe_mlp(x, w13.transpose(1, 2), w2.transpose(1, 2), wts_t * 2, ids_t)
+    assert max_abs_rel(npf(y2), 2 * npf(y)) < 1e-2
+    # token permutation equivariance
+    perm = torch.randperm(T, device=dev(), generator=g)
+    y3 = mb.fused_moe_mlp(x[perm], w13.transpose(1, 2), w2.transpose(1, 2), wts_t[perm], ids_t[perm])
+    assert max_abs_rel(npf(y3), npf(y[perm])) < 1e-2
+    assert torch.isfinite(y).all()
+    assert_no_device_error()
+
+
+def test_launch_counter_counts_kernels():
+    x, w13, w2, ids, wts = topk_case(64, 256, 128, 4, 2, "uniform-softmax", torch.bfloat16)
+    lib = _lib.load()
+    before = lib.moe_launch_count()
+    run_topk(x, w13, w2, ids, wts)
+    # align (4) + gather + gemm1 + gemm2 + convert
+    assert lib.moe_launch_count() - before == 8
