@@ -163,15 +163,16 @@ def gather_rows(src: torch.Tensor, sorted_slots: torch.Tensor, top_k: int, rows:
 
 
 def quantize_weights_int8(w13: torch.Tensor, w2: torch.Tensor):
-    """Load-time w8a8 weight prep (not on the hot path): logical (E, K, N)
-    weights -> int8 logical views with K-major storage and per-output-channel
-    fp32 scales = absmax / 127 (round-half-even). Returns
+    """Load-time w8a8 weight prep: logical (E, K, N) weights -> int8 logical
+    views with K-major storage and per-output-channel fp32 scales
+    s = absmax / 127, q = clamp(rint(w / s), -127, 127) — the per-row int8
+    kernel applied to the K-major rows. Returns
     (w13_q, w2_q, (w13_scale [E, 2I], w2_scale [E, H]))."""
     def q(w):
-        wk = w.transpose(1, 2).float()                    # [E, N, K]
-        s = wk.abs().amax(dim=2) / 127.0                  # [E, N]
-        qq = torch.where(s[..., None] > 0, torch.round(wk / s[..., None]), torch.zeros_like(wk))
-        return qq.clamp_(-127, 127).to(torch.int8).contiguous().transpose(1, 2), s.contiguous()
+        wk = kmajor(w)                                  # [E, N, K] contiguous
+        E, N, K = wk.shape
+        qq, s = quant_int8_rows(wk.reshape(E * N, K))
+        return qq.view(E, N, K).transpose(1, 2), s.view(E, N)
     a, sa = q(w13)
     b, sb = q(w2)
     return a, b, (sa, sb)
