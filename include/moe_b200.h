@@ -140,6 +140,26 @@ MOE_API int moe_align(const int32_t* topk_ids, int64_t num_tokens, int top_k, in
               int32_t* sorted_slots, int32_t* slot_pos, int32_t* group_sizes, int32_t* padded_offsets,
               int32_t* tile_table, void* workspace, size_t workspace_bytes, void* stream);
 
+/* moe_align without a workspace argument, for callers that cannot allocate
+ * device memory at all — for example a plugin that a host engine hands only
+ * its input and output buffers, or a serving process whose memory pool is
+ * fully reserved at start-up so no cudaMalloc may happen afterwards. It has
+ * no counterpart in the reference. Outputs and their meaning are exactly
+ * those of moe_align; it allocates nothing and calls no cudaMalloc/cudaFree.
+ * Its scratch is a file-scope device array of MOE_ALIGN_STATIC_SCRATCH_BYTES
+ * (1 MiB) that every GPU which loads this library holds until the process
+ * exits; requests whose scratch (moe_align_workspace_size) exceeds it fail
+ * with MOE_ERR_INVALID_ARG (e.g. 65536 tokens x top-8 over 256 experts needs
+ * about 0.5 MiB and fits). The first call on each device looks up the
+ * array's device address with that device current; make that first call
+ * before any stream capture. All calls share the one array and it keeps the
+ * last call's contents: calls that overlap on the GPU (other streams, other
+ * host threads) race with each other and must be serialised by the caller. */
+#define MOE_ALIGN_STATIC_SCRATCH_BYTES (1u << 20)
+MOE_API int moe_align_static(const int32_t* topk_ids, int64_t num_tokens, int top_k, int num_experts, int block_m,
+                             int32_t* sorted_slots, int32_t* slot_pos, int32_t* group_sizes,
+                             int32_t* padded_offsets, int32_t* tile_table, void* stream);
+
 /* --------------------------------------------------------------------------
  * Row gather and per-token int8 quant (no reference counterpart).
  * moe_gather_rows: dst[p] = src[sorted_slots[p] / top_k] for p < rows

@@ -36,6 +36,7 @@ SIGNATURES = {
     "moe_align_capacity": (_i64, [_i64, _i, _i]),
     "moe_align_workspace_size": (_sz, [_i64, _i, _i, _i]),
     "moe_align": (_i, [_p, _i64, _i, _i, _i, _p, _p, _p, _p, _p, _p, _sz, _p]),
+    "moe_align_static": (_i, [_p, _i64, _i, _i, _i, _p, _p, _p, _p, _p, _p]),
     "moe_gather_rows": (_i, [_p, _i, _i64, _p, _i, _i64, _p, _p, _i, _p, _p]),
     "moe_quant_rows": (_i, [_p, _i, _i64, _i64, _p, _p, _p, _p]),
     "moe_gemm1_swiglu": (_i, [_p, _i, _i64, _i64, _p, _i, _i64, _p, _p, _p, _i64, _p, _i, _p]),

@@ -9,6 +9,8 @@
 //    routing op (fused moe mlp triton.py:11-13): per-chunk warp histograms
 //    (__match_any_sync), a per-expert scan over chunks, a per-expert scan
 //    with padding to BLOCK_M, and a stable scatter.
+#include <mutex>
+
 #include "common.cuh"
 
 namespace moe {
@@ -329,6 +331,80 @@ extern "C" int moe_align(const int32_t* topk_ids, int64_t num_tokens, int top_k,
   if (workspace_bytes < w.bytes || (w.bytes && !workspace))
     return set_error(MOE_ERR_WORKSPACE, "moe_align: workspace %zu < %zu bytes", workspace_bytes, w.bytes);
   char* ws = static_cast<char*>(workspace);
+  int32_t* hist = reinterpret_cast<int32_t*>(ws + w.hist_off);
+  int32_t* base = reinterpret_cast<int32_t*>(ws + w.base_off);
+  int32_t* totals = reinterpret_cast<int32_t*>(ws + w.totals_off);
+  cudaStream_t st = as_stream(stream);
+  const int64_t max_tiles = moe_align_capacity(S, num_experts, block_m) / block_m;
+  const size_t hsmem = (num_experts + 1) * sizeof(int32_t);
+  if (w.chunks > 0) {
+    align_count_kernel<<<(unsigned)w.chunks, 32, hsmem, st>>>(topk_ids, S, num_experts, hist);
+    MOE_LAUNCH_CHECK("align_count_kernel");
+  }
+  align_colscan_kernel<<<num_experts + 1, kScanThreads, 0, st>>>(hist, (int)w.chunks, num_experts, base, totals);
+  MOE_LAUNCH_CHECK("align_colscan_kernel");
+  align_finalize_kernel<<<1, kScanThreads, 2 * hsmem, st>>>(totals, num_experts, block_m, max_tiles, group_sizes,
+                                                            padded_offsets, tile_table, sorted_slots);
+  MOE_LAUNCH_CHECK("align_finalize_kernel");
+  if (w.chunks > 0) {
+    align_scatter_kernel<<<(unsigned)w.chunks, 32, hsmem, st>>>(topk_ids, S, num_experts, base, padded_offsets,
+                                                                sorted_slots, slot_pos);
+    MOE_LAUNCH_CHECK("align_scatter_kernel");
+  }
+  return MOE_OK;
+}
+
+// ---------------------------------------------------------------------------
+// moe_align_static: the same four align kernels with their scratch in a
+// file-scope device array instead of a caller workspace, for callers that
+// cannot allocate device memory. Nothing in the scratch has to start at zero:
+// every histogram, base and total the kernels read is written earlier in the
+// same call. Calls that overlap on the GPU share (and race on) the array.
+namespace {
+static __device__ __align__(256) unsigned char g_align_scratch[MOE_ALIGN_STATIC_SCRATCH_BYTES];
+
+std::mutex g_align_scratch_mu;
+void* g_align_scratch_ptr[64] = {nullptr};
+
+// Device address of g_align_scratch on the current device. In host code the
+// symbol is only a host-side stand-in, so the address is looked up once per
+// device, with that device current, and cached.
+int align_scratch_address(void** out) {
+  int dev = 0;
+  MOE_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return set_error(MOE_ERR_UNSUPPORTED, "moe_align_static: device %d >= 64", dev);
+  std::lock_guard<std::mutex> lock(g_align_scratch_mu);
+  if (!g_align_scratch_ptr[dev]) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_align_scratch);
+    if (e != cudaSuccess || !p)
+      return set_error(MOE_ERR_CUDA, "moe_align_static: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
+    g_align_scratch_ptr[dev] = p;
+  }
+  *out = g_align_scratch_ptr[dev];
+  return MOE_OK;
+}
+}  // namespace
+
+extern "C" int moe_align_static(const int32_t* topk_ids, int64_t num_tokens, int top_k, int num_experts,
+                                int block_m, int32_t* sorted_slots, int32_t* slot_pos, int32_t* group_sizes,
+                                int32_t* padded_offsets, int32_t* tile_table, void* stream) {
+  MOE_CHECK_ARG(num_tokens >= 0 && top_k > 0, "moe_align_static: bad num_tokens/top_k");
+  MOE_CHECK_ARG(num_experts > 0 && num_experts <= 4096, "moe_align_static: num_experts %d outside [1, 4096]",
+                num_experts);
+  MOE_CHECK_ARG(block_m > 0 && block_m <= 1024, "moe_align_static: block_m %d outside [1, 1024]", block_m);
+  const int64_t S = num_tokens * top_k;
+  MOE_CHECK_ARG(S < (int64_t(1) << 30), "moe_align_static: too many slots");
+  MOE_CHECK_ARG(S == 0 || (topk_ids && slot_pos), "moe_align_static: NULL ids/slot_pos");
+  MOE_CHECK_ARG(sorted_slots && group_sizes && padded_offsets && tile_table, "moe_align_static: NULL output");
+  const AlignWs w = align_ws(S, num_experts);
+  MOE_CHECK_ARG(w.bytes <= MOE_ALIGN_STATIC_SCRATCH_BYTES,
+                "moe_align_static: %lld slots over %d experts need %zu bytes of scratch, more than the static "
+                "%u-byte array; use moe_align with a workspace",
+                (long long)S, num_experts, w.bytes, (unsigned)MOE_ALIGN_STATIC_SCRATCH_BYTES);
+  void* scratch = nullptr;
+  MOE_TRY(align_scratch_address(&scratch));
+  char* ws = static_cast<char*>(scratch);
   int32_t* hist = reinterpret_cast<int32_t*>(ws + w.hist_off);
   int32_t* base = reinterpret_cast<int32_t*>(ws + w.base_off);
   int32_t* totals = reinterpret_cast<int32_t*>(ws + w.totals_off);
