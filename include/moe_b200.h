@@ -164,8 +164,8 @@ MOE_API int moe_align_static(const int32_t* topk_ids, int64_t num_tokens, int to
  * Row gather and per-token int8 quant (no reference counterpart).
  * moe_gather_rows: dst[p] = src[sorted_slots[p] / top_k] for p < rows
  * (zero rows where sorted_slots[p] < 0). If dst_dtype == MOE_I8 the row is
- * quantised on the fly: s = absmax / 127, q = clamp(rint(x / s), -127, 127)
- * (round-half-even; s = 0 and q = 0 for an all-zero row), scale written to
+ * quantised on the fly: s = absmax / 127, q = clamp(rint(x * (127 / absmax)),
+ * -127, 127) (fp32, round-half-even; s = 0 and q = 0 for an all-zero row), s written to
  * dst_scale[p]. `rows_dev` (optional) points at a device int bounding the
  * rows processed (e.g. tile_table + 1); `rows` is the static upper bound.
  * moe_quant_rows: the same quantisation applied row-by-row in place order.
@@ -230,7 +230,9 @@ MOE_API int moe_convert_f32(const float* src, int64_t n, void* dst, int dst_dtyp
  * moe_fused_experts — the top-k form fused_moe_mlp(hidden_states, w13, w2,
  * topk_weights, topk_ids, [scales]): align -> gather (+int8 quant) -> GEMM1 +
  * SwiGLU -> (int8 quant of h) -> GEMM2 + weighted combine -> y [T, H] in
- * x_dtype. w_dtype == MOE_I8 selects w8a8 with per-output-channel weight
+ * x_dtype. The combine is fused into GEMM2's epilogue (fp32 atomics) while
+ * the T x H fp32 accumulator fits in L2 (<= 80 MiB); larger outputs store
+ * GEMM2 rows and sum them per token with moe_combine_rows. w_dtype == MOE_I8 selects w8a8 with per-output-channel weight
  * scales w13_scale [E, 2I] and w2_scale [E, H] (fp32) and dynamic per-token
  * activation scales; otherwise w_dtype must equal x_dtype.
  * -------------------------------------------------------------------------- */
@@ -246,6 +248,19 @@ MOE_API int moe_fused_experts(const void* x, int x_dtype, int64_t num_tokens, in
                       const void* w2, int w_dtype, int num_experts, int64_t inter, const float* topk_weights,
                       const int32_t* topk_ids, int top_k, const float* w13_scale, const float* w2_scale,
                       void* y, void* workspace, size_t workspace_bytes, void* stream);
+
+/* moe_fused_expert_rows — the expert MLP applied row by row, with no routing
+ * weights and no combine: out[r] = MLP_{expert_ids[r]}(x[r]) for r < rows,
+ * in x_dtype (rows whose id is outside [0, E) are left unwritten). This is
+ * the local pass of expert parallelism, where each received row carries one
+ * local expert id and its result travels back unweighted. No reference
+ * counterpart. */
+MOE_API size_t moe_fused_expert_rows_workspace_size(int64_t rows, int64_t hidden, int64_t inter, int num_experts,
+                                                    int x_dtype, int w_dtype);
+MOE_API int moe_fused_expert_rows(const void* x, int x_dtype, int64_t rows, int64_t hidden, const void* w13,
+                                  const void* w2, int w_dtype, int num_experts, int64_t inter,
+                                  const int32_t* expert_ids, const float* w13_scale, const float* w2_scale,
+                                  void* out, void* workspace, size_t workspace_bytes, void* stream);
 
 #ifdef __cplusplus
 }

@@ -6,6 +6,7 @@ from .moe import (
     BLOCK_M,
     build_tile_schedule,
     device_error,
+    fused_expert_rows,
     fused_moe_mlp,
     gather_rows,
     kmajor,
@@ -17,7 +18,7 @@ from .moe import (
 )
 
 __all__ = [
-    "BLOCK_M", "MoeError", "build_tile_schedule", "device_error", "fused_moe_mlp", "gather_rows", "kmajor",
+    "BLOCK_M", "MoeError", "build_tile_schedule", "device_error", "fused_expert_rows", "fused_moe_mlp", "gather_rows", "kmajor",
     "load_library", "moe_align", "prepack_weights", "quant_int8_rows", "quantize_weights_int8",
     "weights_from_linear",
 ]

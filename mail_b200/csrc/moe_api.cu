@@ -64,12 +64,30 @@ FusedMlpWs fused_mlp_ws(int64_t T, int64_t I, int E, int dtype, int block_m) {
   return w;
 }
 
+// Output handling of the top-k expert pass.
+enum class ExpertsOut {
+  kCombineAtomic,  // GEMM2 epilogue scatter-adds w * row into an fp32 [T, H] accumulator
+  kCombineRows,    // GEMM2 stores rows [cap, H]; moe_combine_rows sums the k rows per token
+  kScatterRows     // k = 1, unit weight: GEMM2 writes row r of the output directly
+};
+
+// The fused atomic combine pays off while its fp32 accumulator stays
+// resident in the 126 MB L2 next to the other traffic; above this size the
+// read-modify-writes reach HBM and a row store + separate combine is cheaper.
+constexpr size_t kAtomicCombineMaxBytes = size_t(80) << 20;
+
+ExpertsOut combine_mode(int64_t T, int64_t H) {
+  return (size_t)T * H * sizeof(float) <= kAtomicCombineMaxBytes ? ExpertsOut::kCombineAtomic
+                                                                  : ExpertsOut::kCombineRows;
+}
+
 struct FusedExpertsWs {
   int64_t S, cap, max_tiles;
   size_t align_bytes;
-  size_t align, sorted, slot_pos, gs, poff, table, xp, xs, h, hq, hs, y32, bytes;
+  size_t align, sorted, slot_pos, gs, poff, table, xp, xs, h, hq, hs, y32, o, bytes;
 };
-FusedExpertsWs fused_experts_ws(int64_t T, int64_t H, int64_t I, int E, int k, int x_dtype, int w_dtype) {
+FusedExpertsWs fused_experts_ws(int64_t T, int64_t H, int64_t I, int E, int k, int x_dtype, int w_dtype,
+                                ExpertsOut mode) {
   FusedExpertsWs w;
   w.S = T * k;
   w.cap = moe_align_capacity(w.S, E, kBlockM);
@@ -89,9 +107,112 @@ FusedExpertsWs fused_experts_ws(int64_t T, int64_t H, int64_t I, int E, int k, i
   w.h = c.take((size_t)w.cap * I * dtype_size(h_dtype));
   w.hq = c.take(q ? (size_t)w.cap * I : 0);
   w.hs = c.take(q ? w.cap * sizeof(float) : 0);
-  w.y32 = c.take(x_dtype == MOE_F32 ? 0 : (size_t)T * H * sizeof(float));
+  const bool atomic_acc = mode == ExpertsOut::kCombineAtomic && x_dtype != MOE_F32;
+  w.y32 = c.take(atomic_acc ? (size_t)T * H * sizeof(float) : 0);
+  w.o = c.take(mode == ExpertsOut::kCombineRows ? (size_t)w.cap * H * dtype_size(x_dtype) : 0);
   w.bytes = c.off;
   return w;
+}
+
+struct ExpertsArgs {
+  const void* x;
+  int x_dtype;
+  int64_t T, H;
+  const void* w13;
+  const void* w2;
+  int w_dtype, E;
+  int64_t I;
+  const float* topk_weights;  // NULL for kScatterRows
+  const int32_t* topk_ids;
+  int k;
+  const float* w13_scale;
+  const float* w2_scale;
+  void* y;
+  void* workspace;
+  size_t workspace_bytes;
+  void* stream;
+  ExpertsOut mode;
+  const char* name;
+};
+
+int check_experts(const ExpertsArgs& a) {
+  MOE_CHECK_ARG(a.x_dtype == MOE_BF16 || a.x_dtype == MOE_F16 || a.x_dtype == MOE_F32,
+                "%s: x dtype must be bf16, fp16 or fp32", a.name);
+  MOE_CHECK_ARG(a.w_dtype == a.x_dtype || a.w_dtype == MOE_I8,
+                "%s: weights must share x's dtype or be int8 (w8a8)", a.name);
+  MOE_CHECK_ARG(!(a.w_dtype == MOE_I8 && a.x_dtype == MOE_F32), "%s: w8a8 takes bf16/fp16 activations", a.name);
+  if (a.w_dtype == MOE_I8) MOE_CHECK_ARG(a.w13_scale && a.w2_scale, "%s: int8 weights need scales", a.name);
+  MOE_CHECK_ARG(a.T >= 0 && a.H > 0 && a.I > 0 && a.E > 0 && a.k > 0, "%s: bad sizes", a.name);
+  MOE_CHECK_ARG(a.y != nullptr, "%s: output is NULL", a.name);
+  return MOE_OK;
+}
+
+// align -> gather (+int8 quant) -> GEMM1 + SwiGLU -> (int8 quant of h) ->
+// GEMM2 with the output handling of a.mode.
+int run_experts(const ExpertsArgs& a) {
+  if (a.T == 0) return MOE_OK;
+  MOE_CHECK_ARG(a.x && a.w13 && a.w2 && a.topk_ids && (a.topk_weights || a.mode == ExpertsOut::kScatterRows),
+                "%s: NULL input", a.name);
+  const FusedExpertsWs w = fused_experts_ws(a.T, a.H, a.I, a.E, a.k, a.x_dtype, a.w_dtype, a.mode);
+  if (a.workspace_bytes < w.bytes || !a.workspace)
+    return set_error(MOE_ERR_WORKSPACE, "%s: workspace %zu < %zu bytes", a.name, a.workspace_bytes, w.bytes);
+  char* ws = static_cast<char*>(a.workspace);
+  int32_t* sorted = reinterpret_cast<int32_t*>(ws + w.sorted);
+  int32_t* slot_pos = reinterpret_cast<int32_t*>(ws + w.slot_pos);
+  int32_t* gs = reinterpret_cast<int32_t*>(ws + w.gs);
+  int32_t* poff = reinterpret_cast<int32_t*>(ws + w.poff);
+  int32_t* table = reinterpret_cast<int32_t*>(ws + w.table);
+  const bool q = (a.w_dtype == MOE_I8);
+  const int h_dtype = (a.x_dtype == MOE_F32) ? MOE_F32 : (q ? MOE_BF16 : a.x_dtype);
+  void* stream = a.stream;
+  cudaStream_t st = as_stream(stream);
+
+  MOE_TRY(record_stage(MOE_STAGE_ENTRY, st));
+  MOE_TRY(moe_align(a.topk_ids, a.T, a.k, a.E, kBlockM, sorted, slot_pos, gs, poff, table, ws + w.align,
+                    w.align_bytes, stream));
+  MOE_TRY(record_stage(MOE_STAGE_ROUTED, st));
+  const int32_t* rows_dev = table + 1;  // padded rows in use
+  void* xp = ws + w.xp;
+  float* xs = q ? reinterpret_cast<float*>(ws + w.xs) : nullptr;
+  MOE_TRY(moe_gather_rows(a.x, a.x_dtype, a.H, sorted, a.k, w.cap, rows_dev, xp, q ? MOE_I8 : a.x_dtype, xs,
+                          stream));
+  MOE_TRY(record_stage(MOE_STAGE_GATHERED, st));
+  void* h = ws + w.h;
+  MOE_TRY(moe_gemm1_swiglu(xp, q ? MOE_I8 : a.x_dtype, w.cap, a.H, a.w13, a.E, a.I, xs, a.w13_scale, table,
+                           w.max_tiles, h, h_dtype, stream));
+  MOE_TRY(record_stage(MOE_STAGE_GEMM1, st));
+  const void* a2 = h;
+  float* hs = nullptr;
+  if (q) {
+    int8_t* hq = reinterpret_cast<int8_t*>(ws + w.hq);
+    hs = reinterpret_cast<float*>(ws + w.hs);
+    MOE_TRY(moe_quant_rows(h, h_dtype, w.cap, a.I, rows_dev, hq, hs, stream));
+    a2 = hq;
+  }
+  const int g2_dtype = q ? MOE_I8 : h_dtype;
+  if (a.mode == ExpertsOut::kCombineAtomic) {
+    float* acc = (a.x_dtype == MOE_F32) ? static_cast<float*>(a.y) : reinterpret_cast<float*>(ws + w.y32);
+    MOE_CUDA_TRY(cudaMemsetAsync(acc, 0, (size_t)a.T * a.H * sizeof(float), st));
+    MOE_TRY(record_stage(MOE_STAGE_PRE_GEMM2, st));
+    MOE_TRY(moe_gemm2(a2, g2_dtype, w.cap, a.I, a.w2, a.E, a.H, hs, a.w2_scale, table, w.max_tiles,
+                      MOE_EPI_COMBINE_ADD, sorted, a.topk_weights, a.k, acc, MOE_F32, a.T, stream));
+    MOE_TRY(record_stage(MOE_STAGE_GEMM2, st));
+    if (a.x_dtype != MOE_F32) MOE_TRY(moe_convert_f32(acc, a.T * a.H, a.y, a.x_dtype, stream));
+  } else if (a.mode == ExpertsOut::kCombineRows) {
+    void* o = ws + w.o;
+    MOE_TRY(record_stage(MOE_STAGE_PRE_GEMM2, st));
+    MOE_TRY(moe_gemm2(a2, g2_dtype, w.cap, a.I, a.w2, a.E, a.H, hs, a.w2_scale, table, w.max_tiles,
+                      MOE_EPI_STORE_ROWS, nullptr, nullptr, 1, o, a.x_dtype, w.cap, stream));
+    MOE_TRY(record_stage(MOE_STAGE_GEMM2, st));
+    MOE_TRY(moe_combine_rows(o, a.x_dtype, a.H, slot_pos, a.topk_weights, a.T, a.k, a.y, a.x_dtype, stream));
+  } else {
+    MOE_TRY(record_stage(MOE_STAGE_PRE_GEMM2, st));
+    MOE_TRY(moe_gemm2(a2, g2_dtype, w.cap, a.I, a.w2, a.E, a.H, hs, a.w2_scale, table, w.max_tiles,
+                      MOE_EPI_SCATTER_ROWS, sorted, nullptr, 1, a.y, a.x_dtype, a.T, stream));
+    MOE_TRY(record_stage(MOE_STAGE_GEMM2, st));
+  }
+  MOE_TRY(record_stage(MOE_STAGE_DONE, st));
+  return MOE_OK;
 }
 
 }  // namespace
@@ -157,7 +278,9 @@ extern "C" size_t moe_fused_experts_workspace_size(int64_t num_tokens, int64_t h
                                                    int num_experts, int top_k, int x_dtype, int w_dtype) {
   if (num_tokens < 0 || hidden <= 0 || inter <= 0 || num_experts <= 0 || top_k <= 0) return 0;
   if (dtype_size(x_dtype) == 0 || dtype_size(w_dtype) == 0) return 0;
-  return fused_experts_ws(num_tokens, hidden, inter, num_experts, top_k, x_dtype, w_dtype).bytes;
+  return fused_experts_ws(num_tokens, hidden, inter, num_experts, top_k, x_dtype, w_dtype,
+                          combine_mode(num_tokens, hidden))
+      .bytes;
 }
 
 extern "C" int moe_fused_experts(const void* x, int x_dtype, int64_t num_tokens, int64_t hidden, const void* w13,
@@ -165,58 +288,27 @@ extern "C" int moe_fused_experts(const void* x, int x_dtype, int64_t num_tokens,
                                  const float* topk_weights, const int32_t* topk_ids, int top_k,
                                  const float* w13_scale, const float* w2_scale, void* y, void* workspace,
                                  size_t workspace_bytes, void* stream) {
-  MOE_CHECK_ARG(x_dtype == MOE_BF16 || x_dtype == MOE_F16 || x_dtype == MOE_F32,
-                "moe_fused_experts: x dtype must be bf16, fp16 or fp32");
-  MOE_CHECK_ARG(w_dtype == x_dtype || w_dtype == MOE_I8,
-                "moe_fused_experts: weights must share x's dtype or be int8 (w8a8)");
-  MOE_CHECK_ARG(!(w_dtype == MOE_I8 && x_dtype == MOE_F32), "moe_fused_experts: w8a8 takes bf16/fp16 activations");
-  if (w_dtype == MOE_I8) MOE_CHECK_ARG(w13_scale && w2_scale, "moe_fused_experts: int8 weights need scales");
-  MOE_CHECK_ARG(num_tokens >= 0 && hidden > 0 && inter > 0 && num_experts > 0 && top_k > 0,
-                "moe_fused_experts: bad sizes");
-  MOE_CHECK_ARG(y != nullptr, "moe_fused_experts: y is NULL");
-  if (num_tokens == 0) return MOE_OK;
-  MOE_CHECK_ARG(x && w13 && w2 && topk_weights && topk_ids, "moe_fused_experts: NULL input");
-  const FusedExpertsWs w = fused_experts_ws(num_tokens, hidden, inter, num_experts, top_k, x_dtype, w_dtype);
-  if (workspace_bytes < w.bytes || !workspace)
-    return set_error(MOE_ERR_WORKSPACE, "moe_fused_experts: workspace %zu < %zu bytes", workspace_bytes, w.bytes);
-  char* ws = static_cast<char*>(workspace);
-  int32_t* sorted = reinterpret_cast<int32_t*>(ws + w.sorted);
-  int32_t* slot_pos = reinterpret_cast<int32_t*>(ws + w.slot_pos);
-  int32_t* gs = reinterpret_cast<int32_t*>(ws + w.gs);
-  int32_t* poff = reinterpret_cast<int32_t*>(ws + w.poff);
-  int32_t* table = reinterpret_cast<int32_t*>(ws + w.table);
-  const bool q = (w_dtype == MOE_I8);
-  const int h_dtype = (x_dtype == MOE_F32) ? MOE_F32 : (q ? MOE_BF16 : x_dtype);
-  cudaStream_t st = as_stream(stream);
+  ExpertsArgs a{x, x_dtype, num_tokens, hidden, w13, w2, w_dtype, num_experts, inter, topk_weights, topk_ids,
+                top_k, w13_scale, w2_scale, y, workspace, workspace_bytes, stream,
+                combine_mode(num_tokens, hidden), "moe_fused_experts"};
+  MOE_TRY(check_experts(a));
+  return run_experts(a);
+}
 
-  MOE_TRY(record_stage(MOE_STAGE_ENTRY, st));
-  MOE_TRY(moe_align(topk_ids, num_tokens, top_k, num_experts, kBlockM, sorted, slot_pos, gs, poff, table,
-                    ws + w.align, w.align_bytes, stream));
-  MOE_TRY(record_stage(MOE_STAGE_ROUTED, st));
-  const int32_t* rows_dev = table + 1;  // padded rows in use
-  void* xp = ws + w.xp;
-  float* xs = q ? reinterpret_cast<float*>(ws + w.xs) : nullptr;
-  MOE_TRY(moe_gather_rows(x, x_dtype, hidden, sorted, top_k, w.cap, rows_dev, xp, q ? MOE_I8 : x_dtype, xs, stream));
-  MOE_TRY(record_stage(MOE_STAGE_GATHERED, st));
-  void* h = ws + w.h;
-  MOE_TRY(moe_gemm1_swiglu(xp, q ? MOE_I8 : x_dtype, w.cap, hidden, w13, num_experts, inter, xs, w13_scale, table,
-                           w.max_tiles, h, h_dtype, stream));
-  MOE_TRY(record_stage(MOE_STAGE_GEMM1, st));
-  const void* a2 = h;
-  float* hs = nullptr;
-  if (q) {
-    int8_t* hq = reinterpret_cast<int8_t*>(ws + w.hq);
-    hs = reinterpret_cast<float*>(ws + w.hs);
-    MOE_TRY(moe_quant_rows(h, h_dtype, w.cap, inter, rows_dev, hq, hs, stream));
-    a2 = hq;
-  }
-  float* acc = (x_dtype == MOE_F32) ? static_cast<float*>(y) : reinterpret_cast<float*>(ws + w.y32);
-  MOE_CUDA_TRY(cudaMemsetAsync(acc, 0, (size_t)num_tokens * hidden * sizeof(float), st));
-  MOE_TRY(record_stage(MOE_STAGE_PRE_GEMM2, st));
-  MOE_TRY(moe_gemm2(a2, q ? MOE_I8 : h_dtype, w.cap, inter, w2, num_experts, hidden, hs, w2_scale, table,
-                    w.max_tiles, MOE_EPI_COMBINE_ADD, sorted, topk_weights, top_k, acc, MOE_F32, num_tokens, stream));
-  MOE_TRY(record_stage(MOE_STAGE_GEMM2, st));
-  if (x_dtype != MOE_F32) MOE_TRY(moe_convert_f32(acc, num_tokens * hidden, y, x_dtype, stream));
-  MOE_TRY(record_stage(MOE_STAGE_DONE, st));
-  return MOE_OK;
+extern "C" size_t moe_fused_expert_rows_workspace_size(int64_t rows, int64_t hidden, int64_t inter, int num_experts,
+                                                       int x_dtype, int w_dtype) {
+  if (rows < 0 || hidden <= 0 || inter <= 0 || num_experts <= 0) return 0;
+  if (dtype_size(x_dtype) == 0 || dtype_size(w_dtype) == 0) return 0;
+  return fused_experts_ws(rows, hidden, inter, num_experts, 1, x_dtype, w_dtype, ExpertsOut::kScatterRows).bytes;
+}
+
+extern "C" int moe_fused_expert_rows(const void* x, int x_dtype, int64_t rows, int64_t hidden, const void* w13,
+                                     const void* w2, int w_dtype, int num_experts, int64_t inter,
+                                     const int32_t* expert_ids, const float* w13_scale, const float* w2_scale,
+                                     void* out, void* workspace, size_t workspace_bytes, void* stream) {
+  ExpertsArgs a{x, x_dtype, rows, hidden, w13, w2, w_dtype, num_experts, inter, nullptr, expert_ids,
+                1, w13_scale, w2_scale, out, workspace, workspace_bytes, stream,
+                ExpertsOut::kScatterRows, "moe_fused_expert_rows"};
+  MOE_TRY(check_experts(a));
+  return run_experts(a);
 }

@@ -9,21 +9,6 @@
 namespace moe {
 namespace {
 
-template <typename T>
-struct Vec8;  // 8 elements of T
-template <>
-struct Vec8<__nv_bfloat16> {
-  using type = uint4;
-};
-template <>
-struct Vec8<__half> {
-  using type = uint4;
-};
-template <>
-struct Vec8<int8_t> {
-  using type = uint2;
-};
-
 __device__ __forceinline__ void load8(const __nv_bfloat16* p, float (&v)[8]) {
   uint4 u = *reinterpret_cast<const uint4*>(p);
   const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
@@ -91,20 +76,24 @@ __device__ __forceinline__ void zero8(T* d) {
   }
 }
 
-// Per-token symmetric int8 quantisation of 8 values with a row scale:
-// q = clamp(rint(x / s), -127, 127), 0 when the row is all zeros.
-__device__ __forceinline__ uint2 quant8(const float (&v)[8], float scale) {
+// Per-token symmetric int8 quantisation of 8 values: q = clamp(rint(x * inv),
+// -127, 127) with inv = 127 / absmax (one correctly rounded division per row,
+// an exactly rounded multiply per element); inv = 0 for an all-zero row.
+__device__ __forceinline__ uint2 quant8(const float (&v)[8], float inv) {
   uint32_t w[2] = {0u, 0u};
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
-    int q = 0;
-    if (scale > 0.f) {
-      q = __float2int_rn(__fdiv_rn(v[i], scale));
-      q = max(-127, min(127, q));
-    }
+    int q = __float2int_rn(__fmul_rn(v[i], inv));
+    q = max(-127, min(127, q));
     w[i >> 2] |= (uint32_t)(q & 0xff) << (8 * (i & 3));
   }
   return make_uint2(w[0], w[1]);
+}
+
+// Row scale s = absmax / 127 and quantisation multiplier 127 / absmax.
+__device__ __forceinline__ void row_scales(float amax, float& scale, float& inv) {
+  scale = __fdiv_rn(amax, 127.0f);
+  inv = amax > 0.f ? __fdiv_rn(127.0f, amax) : 0.f;
 }
 
 template <typename Tin, typename Tout>
@@ -137,16 +126,76 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const Tin* __restrict_
       }
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-      const float scale = __fdiv_rn(amax, 127.0f);
+      float scale, inv;
+      row_scales(amax, scale, inv);
       for (int64_t c = lane * 8; c < cols; c += 256) {
         float v[8];
         load8(s + c, v);
-        *reinterpret_cast<uint2*>(d + c) = quant8(v, scale);
+        *reinterpret_cast<uint2*>(d + c) = quant8(v, inv);
       }
       if (lane == 0 && dst_scale) dst_scale[p] = scale;
     } else {
       for (int64_t c = lane * 8; c < cols; c += 256) copy8(s + c, d + c);
     }
+  }
+}
+
+// Gather + per-token int8 quantisation with one 128-thread CTA per row: each
+// thread keeps up to kQuantVecs 8-element vectors of the row in registers, so
+// the row is read from memory once with 8 independent 16-byte loads in flight
+// per thread, reduced to its absmax across the CTA, then quantised from
+// registers. Rows up to 128 * 8 * kQuantVecs columns.
+constexpr int kQuantVecs = 8;
+constexpr int kQuantThreads = 128;
+constexpr int64_t kQuantMaxCols = (int64_t)kQuantThreads * 8 * kQuantVecs;
+
+template <typename Tin>
+__global__ void __launch_bounds__(kQuantThreads) gather_quant_kernel(const Tin* __restrict__ src, int64_t cols,
+                                                                     const int32_t* __restrict__ slots, int top_k,
+                                                                     int64_t rows,
+                                                                     const int32_t* __restrict__ rows_dev,
+                                                                     int8_t* __restrict__ dst,
+                                                                     float* __restrict__ dst_scale) {
+  __shared__ float red[kQuantThreads / 32];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  int64_t limit = rows;
+  if (rows_dev) limit = min(limit, (int64_t)*rows_dev);
+  for (int64_t p = blockIdx.x; p < limit; p += gridDim.x) {
+    const int64_t slot = slots ? (int64_t)slots[p] : p;
+    int8_t* d = dst + p * cols;
+    if (slot < 0) {
+      for (int64_t c = (int64_t)tid * 8; c < cols; c += kQuantThreads * 8) zero8(d + c);
+      if (tid == 0 && dst_scale) dst_scale[p] = 0.f;
+      continue;
+    }
+    const Tin* s = src + (slot / top_k) * cols;
+    float v[kQuantVecs][8];
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < kQuantVecs; ++i) {
+      const int64_t c = ((int64_t)i * kQuantThreads + tid) * 8;
+      if (c < cols) {
+        load8(s + c, v[i]);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(v[i][j]));
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    if (lane == 0) red[warp] = amax;
+    __syncthreads();
+    amax = red[0];
+#pragma unroll
+    for (int w = 1; w < kQuantThreads / 32; ++w) amax = fmaxf(amax, red[w]);
+    __syncthreads();
+    float scale, inv;
+    row_scales(amax, scale, inv);
+#pragma unroll
+    for (int i = 0; i < kQuantVecs; ++i) {
+      const int64_t c = ((int64_t)i * kQuantThreads + tid) * 8;
+      if (c < cols) *reinterpret_cast<uint2*>(d + c) = quant8(v[i], inv);
+    }
+    if (tid == 0 && dst_scale) dst_scale[p] = scale;
   }
 }
 
@@ -219,6 +268,22 @@ extern "C" int moe_gather_rows(const void* src, int src_dtype, int64_t cols, con
     else return set_error(MOE_ERR_UNSUPPORTED, "moe_gather_rows: dtype %d not supported", src_dtype);
   } else if (dst_dtype == MOE_I8) {
     MOE_CHECK_ARG(dst_scale != nullptr, "moe_gather_rows: int8 output needs dst_scale");
+    if (cols <= kQuantMaxCols) {
+      int64_t blocks = rows;
+      const int64_t cap = (int64_t)num_sms() * 16;
+      if (blocks > cap) blocks = cap;
+#define GATHER_Q(TI)                                                                                          \
+  gather_quant_kernel<TI><<<(unsigned)blocks, kQuantThreads, 0, st>>>(static_cast<const TI*>(src), cols,     \
+                                                                     sorted_slots, top_k, rows, rows_dev,   \
+                                                                     static_cast<int8_t*>(dst), dst_scale)
+      if (src_dtype == MOE_BF16) GATHER_Q(__nv_bfloat16);
+      else if (src_dtype == MOE_F16) GATHER_Q(__half);
+      else if (src_dtype == MOE_F32) GATHER_Q(float);
+      else return set_error(MOE_ERR_UNSUPPORTED, "moe_gather_rows: dtype %d not supported", src_dtype);
+#undef GATHER_Q
+      MOE_LAUNCH_CHECK("gather_quant_kernel");
+      return MOE_OK;
+    }
     if (src_dtype == MOE_BF16) GATHER(__nv_bfloat16, int8_t);
     else if (src_dtype == MOE_F16) GATHER(__half, int8_t);
     else if (src_dtype == MOE_F32) GATHER(float, int8_t);

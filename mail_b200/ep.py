@@ -34,15 +34,14 @@ class CudaOps:
 
     def sort_slots(self, topk_ids: torch.Tensor, num_experts: int):
         a = _moe.moe_align(topk_ids, num_experts, block_m=1)
-        return a["sorted_slots"], a["slot_pos"], a["group_sizes"]
+        return a["sorted_slots"], a["slot_pos"], a["group_sizes"], a["tile_table"][1:2]
 
-    def gather(self, x: torch.Tensor, sorted_slots: torch.Tensor, top_k: int, rows: int) -> torch.Tensor:
-        return _moe.gather_rows(x, sorted_slots, top_k, rows)
+    def gather(self, x: torch.Tensor, sorted_slots: torch.Tensor, top_k: int, rows: int,
+               rows_dev: torch.Tensor | None = None) -> torch.Tensor:
+        return _moe.gather_rows(x, sorted_slots, top_k, rows, rows_dev=rows_dev)
 
     def expert_forward(self, x_rows, local_ids, w13, w2, scales):
-        R = x_rows.shape[0]
-        ones = torch.ones((R, 1), dtype=torch.float32, device=x_rows.device)
-        return _moe.fused_moe_mlp(x_rows, w13, w2, ones, local_ids.view(R, 1), scales=scales)
+        return _moe.fused_expert_rows(x_rows, w13, w2, local_ids, scales=scales)
 
     def combine(self, o_back, slot_pos, topk_weights, out_dtype):
         T, k = topk_weights.shape
@@ -79,22 +78,20 @@ class ExpertParallelMoE:
         self.w13, self.w2, self.scales = w13, w2, scales
         self.ops = ops or CudaOps()
 
-    def plan(self, topk_ids: torch.Tensor):
-        """Dispatch plan: sorted slots, slot positions, send/recv counts."""
-        sorted_slots, slot_pos, gs = self.ops.sort_slots(topk_ids, self.E)
-        per_dest = gs.to(torch.int64).view(self.world, self.E_local)
-        recv_expert = torch.empty_like(per_dest)
-        dist.all_to_all_single(recv_expert, per_dest, group=self.group)
-        counts = torch.stack([per_dest.sum(1), recv_expert.sum(1)]).cpu()  # host split sizes (one sync)
-        return dict(sorted_slots=sorted_slots, slot_pos=slot_pos, recv_expert=recv_expert,
-                    send=counts[0].tolist(), recv=counts[1].tolist())
-
     def __call__(self, x: torch.Tensor, topk_weights: torch.Tensor, topk_ids: torch.Tensor) -> torch.Tensor:
         T, H = x.shape
         k = topk_ids.shape[1]
-        p = self.plan(topk_ids)
+        sorted_slots, slot_pos, gs, n_valid_dev = self.ops.sort_slots(topk_ids, self.E)
+        per_dest = gs.to(torch.int64).view(self.world, self.E_local)
+        recv_expert = torch.empty_like(per_dest)
+        dist.all_to_all_single(recv_expert, per_dest, group=self.group)
+        # the send rows do not depend on what other ranks send: gather them
+        # (up to the device-side valid count) while the counts travel
+        x_send_all = self.ops.gather(x, sorted_slots, k, T * k, rows_dev=n_valid_dev)
+        counts = torch.stack([per_dest.sum(1), recv_expert.sum(1)]).cpu()  # host split sizes (one sync)
+        p = dict(send=counts[0].tolist(), recv=counts[1].tolist(), recv_expert=recv_expert, slot_pos=slot_pos)
         n_send, n_recv = sum(p["send"]), sum(p["recv"])
-        x_send = self.ops.gather(x, p["sorted_slots"], k, n_send)
+        x_send = x_send_all[:n_send]
         x_recv = x.new_empty((n_recv, H))
         dist.all_to_all_single(x_recv, x_send, p["recv"], p["send"], group=self.group)
         # received rows: grouped by source rank, then by local expert

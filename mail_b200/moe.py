@@ -138,7 +138,7 @@ def moe_align(topk_ids: torch.Tensor, num_experts: int, block_m: int = BLOCK_M) 
 
 
 def quant_int8_rows(x: torch.Tensor):
-    """Per-row int8: s = absmax / 127, q = clamp(rint(x / s), -127, 127)."""
+    """Per-row int8: s = absmax / 127, q = clamp(rint(x * (127 / absmax)), -127, 127)."""
     _require_cuda(x)
     x = x.contiguous()
     R, C = x.shape
@@ -165,7 +165,7 @@ def gather_rows(src: torch.Tensor, sorted_slots: torch.Tensor, top_k: int, rows:
 def quantize_weights_int8(w13: torch.Tensor, w2: torch.Tensor):
     """Load-time w8a8 weight prep: logical (E, K, N) weights -> int8 logical
     views with K-major storage and per-output-channel fp32 scales
-    s = absmax / 127, q = clamp(rint(w / s), -127, 127) — the per-row int8
+    s = absmax / 127, q = clamp(rint(w * (127 / absmax)), -127, 127) — the per-row int8
     kernel applied to the K-major rows. Returns
     (w13_q, w2_q, (w13_scale [E, 2I], w2_scale [E, H]))."""
     def q(w):
@@ -250,6 +250,35 @@ def fused_moe_mlp(x: torch.Tensor, w13: torch.Tensor, w2: torch.Tensor, group_si
               topk_weights.data_ptr(), ids.data_ptr(), k, _ptr(s13), _ptr(s2), y.data_ptr(), ws.data_ptr(),
               ws.numel(), st)
     return y
+
+
+def fused_expert_rows(x: torch.Tensor, w13: torch.Tensor, w2: torch.Tensor, expert_ids: torch.Tensor,
+                      scales=None) -> torch.Tensor:
+    """out[r] = MLP_{expert_ids[r]}(x[r]) — the expert MLP row by row with no
+    routing weights or combine (the local pass of expert parallelism).
+    Weights as in fused_moe_mlp; rows with ids outside [0, E) are left
+    unwritten (uninitialised)."""
+    _require_cuda(x, w13, w2, expert_ids)
+    R, H = x.shape
+    E, _, two_i = w13.shape
+    inter = two_i // 2
+    x = x.contiguous()
+    ids = expert_ids.to(torch.int32).contiguous().view(-1)
+    if ids.numel() != R:
+        raise ValueError("fused_expert_rows: one expert id per row")
+    w13k, w2k = kmajor(w13), kmajor(w2)
+    s13 = s2 = None
+    if w13.dtype == torch.int8:
+        if scales is None:
+            raise ValueError("fused_expert_rows: int8 weights need scales")
+        s13, s2 = (t.to(torch.float32).contiguous() for t in scales)
+    out = torch.empty((R, H), dtype=x.dtype, device=x.device)
+    ws = _workspace(_lib.query("moe_fused_expert_rows_workspace_size", R, H, inter, E, _code(x), _code(w13)),
+                    x.device)
+    _lib.call("moe_fused_expert_rows", x.data_ptr(), _code(x), R, H, w13k.data_ptr(), w2k.data_ptr(), _code(w13),
+              E, inter, ids.data_ptr(), _ptr(s13), _ptr(s2), out.data_ptr(), ws.data_ptr(), ws.numel(),
+              _stream(x.device))
+    return out
 
 
 def device_error(device=None) -> int:

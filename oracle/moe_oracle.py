@@ -174,27 +174,30 @@ def align(topk_ids, num_experts: int, block_m: int):
 # int8 (ABSENT in the reference)
 
 
-def quant_int8_rows(x):
-    """Per-row symmetric int8: s = absmax / 127 (fp32), q = clamp(rint(x / s),
+def _quant_rows_last_axis(x):
+    """Symmetric int8 along the last axis: s = absmax / 127 and
+    inv = 127 / absmax (both fp32, correctly rounded), q = clamp(rint(x * inv),
     -127, 127) with round-half-to-even; all-zero rows give s = 0, q = 0."""
     x = np.asarray(x, np.float32)
-    amax = np.abs(x).max(axis=1) if x.shape[1] else np.zeros(x.shape[0], np.float32)
-    s = (amax.astype(np.float32) / np.float32(127.0)).astype(np.float32)
+    amax = np.abs(x).max(axis=-1).astype(np.float32) if x.shape[-1] else np.zeros(x.shape[:-1], np.float32)
+    s = (amax / np.float32(127.0)).astype(np.float32)
     with np.errstate(divide="ignore", invalid="ignore"):
-        q = np.where(s[:, None] > 0, np.rint(x / s[:, None]), 0.0)
-    q = np.clip(q, -127, 127).astype(np.int8)
-    return q, s
+        inv = np.where(amax > 0, np.float32(127.0) / amax, np.float32(0.0)).astype(np.float32)
+    q = np.rint(x * inv[..., None]).astype(np.float32)
+    return np.clip(q, -127, 127).astype(np.int8), s
+
+
+def quant_int8_rows(x):
+    """Per-token (per-row) int8 activation quantisation; see
+    _quant_rows_last_axis for the exact arithmetic."""
+    return _quant_rows_last_axis(x)
 
 
 def quantize_weight_per_channel(w):
     """w [..., N, K] (K-major rows = output channels) -> int8 + fp32 scale
-    [..., N] with scale = absmax / 127 over each row (BASELINE config 4/5)."""
-    w = np.asarray(w, np.float32)
-    amax = np.abs(w).max(axis=-1)
-    s = (amax / np.float32(127.0)).astype(np.float32)
-    with np.errstate(divide="ignore", invalid="ignore"):
-        q = np.where(s[..., None] > 0, np.rint(w / s[..., None]), 0.0)
-    return np.clip(q, -127, 127).astype(np.int8), s
+    [..., N] = absmax / 127 over each row, same arithmetic as the per-token
+    activation quantisation."""
+    return _quant_rows_last_axis(w)
 
 
 # ---------------------------------------------------------------------------

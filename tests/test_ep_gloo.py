@@ -23,12 +23,16 @@ class OracleOps:
 
     def sort_slots(self, topk_ids, num_experts):
         a = O.align(topk_ids.numpy(), num_experts, 1)
+        n_valid = torch.tensor([int(a["padded_offsets"][-1])], dtype=torch.int32)
         return (torch.from_numpy(a["sorted_slots"]), torch.from_numpy(a["slot_pos"]),
-                torch.from_numpy(a["group_sizes"]))
+                torch.from_numpy(a["group_sizes"]), n_valid)
 
-    def gather(self, x, sorted_slots, top_k, rows):
-        s = sorted_slots[:rows].to(torch.int64)
-        return x[s // top_k].clone()
+    def gather(self, x, sorted_slots, top_k, rows, rows_dev=None):
+        n = min(rows, int(rows_dev[0])) if rows_dev is not None else rows
+        out = torch.zeros((rows, x.shape[1]), dtype=x.dtype)
+        s = sorted_slots[:n].to(torch.int64)
+        out[:n] = x[s // top_k]
+        return out
 
     def expert_forward(self, x_rows, local_ids, w13, w2, scales):
         ids = local_ids.numpy().reshape(-1, 1)

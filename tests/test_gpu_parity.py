@@ -282,6 +282,56 @@ def test_mixtral_full_size_sampled_and_properties():
     assert_no_device_error()
 
 
+@pytest.mark.parametrize("quant", [False, True])
+def test_large_output_uses_row_store_combine(quant):
+    """T x H fp32 accumulator above 80 MiB: GEMM2 stores rows and the
+    deterministic combine sums them (the path a DeepSeek-V3-sized batch takes)."""
+    T, H, I, E, k = 4096, 7168, 256, 32, 8   # 4096 x 7168 x 4 B = 117 MB
+    x, w13, w2, ids, wts = topk_case(T, H, I, E, k, "sigmoid", torch.bfloat16, seed=6)
+    scales = None
+    if quant:
+        w13, w2, scales = mb.quantize_weights_int8(w13, w2)
+    y = run_topk(x, w13, w2, ids, wts, scales=scales)
+    assert _lib.load().moe_fused_experts_workspace_size(T, H, I, E, k, _lib.BF16, _lib.I8 if quant else _lib.BF16) > 0
+    sample = np.random.default_rng(0).choice(T, size=64, replace=False)
+    if quant:
+        q13, s13 = (npf(w13.transpose(1, 2)).astype(np.int8), npf(scales[0]))
+        q2, s2 = (npf(w2.transpose(1, 2)).astype(np.int8), npf(scales[1]))
+        ref = O.moe_mlp_w8a8(npf(x)[sample], q13, s13, q2, s2, wts[sample], ids[sample], round_hidden=O.round_bf16)
+    else:
+        ref = O.moe_mlp_topk(npf(x)[sample], npf(w13), npf(w2), wts[sample], ids[sample], round_hidden=O.round_bf16)
+    err = max_abs_rel(npf(y)[sample], ref)
+    assert err < TOL, err
+    # deterministic path: bit-identical on a second call
+    y2 = run_topk(x, w13, w2, ids, wts, scales=scales)
+    assert torch.equal(y, y2)
+    assert_no_device_error()
+
+
+@pytest.mark.parametrize("dtype,quant", [(torch.bfloat16, False), (torch.bfloat16, True), (torch.float32, False)])
+def test_fused_expert_rows_matches_oracle(dtype, quant):
+    R, H, I, E = 333, 512, 384, 6
+    rng = np.random.default_rng(8)
+    x = torch.from_numpy(rng.standard_normal((R, H), dtype=np.float32)).to(dev(), dtype)
+    w13 = torch.from_numpy(rng.standard_normal((E, 2 * I, H), dtype=np.float32) * 0.03).to(dev(), dtype)
+    w2 = torch.from_numpy(rng.standard_normal((E, H, I), dtype=np.float32) * 0.03).to(dev(), dtype)
+    w13, w2 = w13.transpose(1, 2), w2.transpose(1, 2)
+    ids = rng.integers(0, E, size=(R, 1)).astype(np.int32)
+    ones = np.ones((R, 1), np.float32)
+    scales = None
+    if quant:
+        w13, w2, scales = mb.quantize_weights_int8(w13, w2)
+    out = mb.fused_expert_rows(x, w13, w2, torch.from_numpy(ids).to(dev()), scales=scales)
+    rnd = None if dtype == torch.float32 else O.round_bf16
+    if quant:
+        ref = O.moe_mlp_w8a8(npf(x), npf(w13.transpose(1, 2)).astype(np.int8), npf(scales[0]),
+                             npf(w2.transpose(1, 2)).astype(np.int8), npf(scales[1]), ones, ids, round_hidden=rnd)
+    else:
+        ref = O.moe_mlp_topk(npf(x), npf(w13), npf(w2), ones, ids, round_hidden=rnd)
+    assert max_abs_rel(npf(out), ref) < TOL
+    assert_no_device_error()
+
+
 def test_launch_counter_counts_kernels():
     x, w13, w2, ids, wts = topk_case(64, 256, 128, 4, 2, "uniform-softmax", torch.bfloat16)
     lib = _lib.load()
