@@ -56,10 +56,13 @@ def load_peaks():
 
 
 def load_traffic(config: str):
+    """DRAM bytes (read + write) per launch of the dominant kernel from a
+    committed ncu capture of this workload, or None."""
     path = os.path.join(ROOT, "profiles", "traffic.json")
     try:
         with open(path) as f:
-            return json.load(f).get(config)
+            entry = json.load(f).get(config)
+        return None if entry is None else float(entry["bytes"])
     except Exception:
         return None
 
@@ -238,6 +241,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="mixtral", choices=sorted(CONFIGS))
     ap.add_argument("--tokens", type=int, default=0, help="override tokens per GPU (profiling cases)")
+    ap.add_argument("--gemm", default="auto", choices=["auto", "pair", "single"],
+                    help="grouped GEMM variant: CTA pairs (cta_group::2), one CTA per tile, or chosen by size")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -253,7 +258,7 @@ def main():
     dtype_name = "int8" if cfg["quant"] else cfg["dtype"]
     config_json = {"workload": cfg["desc"], "tokens_per_gpu": T, "hidden": H, "inter": I, "experts": E,
                    "top_k": k, "routing": cfg["routing"], "dtype": cfg["dtype"] + ("+w8a8" if cfg["quant"] else ""),
-                   "parallelism": f"ep{world}" if world > 1 else "single",
+                   "parallelism": f"ep{world}" if world > 1 else "single", "gemm": args.gemm,
                    "l2": "weights (%.2f GB) exceed the 126 MB L2, streamed every step" %
                          (E * 3 * H * I * (1 if cfg["quant"] else (4 if cfg["dtype"] == "fp32" else 2)) / 1e9)}
 
@@ -284,6 +289,7 @@ def main():
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
     lib = _lib.load()
+    lib.moe_set_option(_lib.OPT_GEMM_CTA_PAIR, {"pair": 1, "single": 0, "auto": 2}[args.gemm])
 
     x, ids, wts, dt = make_inputs(cfg, rank, device)
     if world > 1:
@@ -392,7 +398,7 @@ def main():
                 "frac": flops_gemm1 / gemm1_s / 1e12 / peak_tc,
                 "peak_source": f"{peaks['source']} bf16 {'sustained' if sustained else 'burst'}"
                                + (" x2 (int8, spec ratio)" if cfg["quant"] else ""),
-                "traffic": load_traffic(args.config),
+                "traffic": load_traffic(args.config) if not args.tokens else None, "traffic_unit": "bytes",
                 "flops_per_launch": flops_gemm1, "ms_per_launch": st_ms["gemm1"]}
     flops_step = 6.0 * S_local * H * I
     value = world * T / (ms / 1e3)

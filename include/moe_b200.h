@@ -80,6 +80,16 @@ MOE_API const char* moe_last_error(void);
  * pipeline role) into *host_code and clears it. Synchronises `stream`. */
 MOE_API int moe_get_device_error(int* host_code, void* stream);
 
+/* Process-wide tuning options (moe_set_option / moe_get_option). */
+typedef enum {
+  MOE_OPT_GEMM_CTA_PAIR = 1 /* 1: grouped GEMMs run one tcgen05 MMA across a pair of CTAs on neighbouring
+                               SMs (cta_group::2, 256-row tiles); 0: one CTA per 128-row tile; 2 (default):
+                               pairs when the experts average at least 4 M tiles of 128 rows */
+} moe_option_t;
+MOE_API int moe_set_option(int option, int value);
+/* Current value of an option, or -1 for an unknown option. */
+MOE_API int moe_get_option(int option);
+
 /* Number of CUDA kernels this library has launched in this process
  * (monotonic, all threads). */
 MOE_API int64_t moe_launch_count(void);

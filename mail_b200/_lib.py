@@ -15,6 +15,7 @@ LIB_PATH = os.path.join(_HERE, "libmoe_b200.so")
 # dtype / status / epilogue codes (moe_b200.h)
 F32, F16, BF16, I8, I32, I64 = 0, 1, 2, 3, 4, 5
 EPI_STORE_ROWS, EPI_COMBINE_ADD, EPI_SCATTER_ROWS = 0, 1, 2
+OPT_GEMM_CTA_PAIR = 1
 STATUS = {0: "MOE_OK", 1: "MOE_ERR_INVALID_ARG", 2: "MOE_ERR_UNSUPPORTED", 3: "MOE_ERR_CUDA",
           4: "MOE_ERR_WORKSPACE", 5: "MOE_ERR_DEVICE"}
 
@@ -29,6 +30,8 @@ SIGNATURES = {
     "moe_last_error": (ctypes.c_char_p, []),
     "moe_get_device_error": (_i, [_p, _p]),
     "moe_launch_count": (_i64, []),
+    "moe_set_option": (_i, [_i, _i]),
+    "moe_get_option": (_i, [_i]),
     "moe_set_stage_events": (_i, [_p, _i]),
     "moe_tile_grid": (_i64, [_i64, _i, _i]),
     "moe_tile_table_ints": (_i64, [_i, _i64]),

@@ -23,6 +23,9 @@
 // tiles through L2 and each expert's weights stream from HBM about once.
 #include <cuda.h>
 
+#include <algorithm>
+#include <atomic>
+
 #include "common.cuh"
 #include "ptx.cuh"
 
@@ -34,11 +37,8 @@ namespace {
 
 constexpr int BM = 128;
 constexpr int BN = 256;
-constexpr int STAGES = 4;
 constexpr int ROW_BYTES = 128;             // K bytes per stage (one 128B swizzle atom)
 constexpr int A_BYTES = BM * ROW_BYTES;    // 16 KiB
-constexpr int B_BYTES = BN * ROW_BYTES;    // 32 KiB
-constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int NUM_THREADS = 192;
 constexpr int GROUP_M = 16;
 constexpr int TMEM_COLS = 512;             // 2 accumulators x 256 columns
@@ -69,23 +69,26 @@ struct Params {
   int top_k;
 };
 
-// Tile t -> (m tile, n tile, expert) in expert-major, banded order.
-__device__ __forceinline__ void decode_tile(int t, const int32_t* s_cum, int E, int NT, int& m, int& n, int& e) {
-  int lo = 0, hi = E;  // invariant: s_cum[lo]*NT <= t < s_cum[hi]*NT
+// Scheduling unit t -> (unit u, n tile, expert e) in expert-major order:
+// the units of expert e in bands of `group` units, each band swept over all
+// n tiles, so concurrently running CTAs share weight tiles through L2.
+__device__ __forceinline__ void decode_unit(int t, const int32_t* s_u, int E, int NT, int group, int& u, int& n,
+                                            int& e) {
+  int lo = 0, hi = E;  // invariant: s_u[lo]*NT <= t < s_u[hi]*NT
   while (hi - lo > 1) {
     const int mid = (lo + hi) >> 1;
-    if (s_cum[mid] * NT <= t) lo = mid;
+    if (s_u[mid] * NT <= t) lo = mid;
     else hi = mid;
   }
   e = lo;
-  const int mt = s_cum[e + 1] - s_cum[e];
-  const int local = t - s_cum[e] * NT;
-  const int band = local / (GROUP_M * NT);
-  const int m0 = band * GROUP_M;
-  const int bsz = min(GROUP_M, mt - m0);
-  const int rem = local - band * GROUP_M * NT;
+  const int mt = s_u[e + 1] - s_u[e];
+  const int local = t - s_u[e] * NT;
+  const int band = local / (group * NT);
+  const int m0 = band * group;
+  const int bsz = min(group, mt - m0);
+  const int rem = local - band * group * NT;
   n = rem / bsz;
-  m = s_cum[e] + m0 + rem % bsz;
+  u = s_u[e] + m0 + rem % bsz;
 }
 
 __device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.0f + __expf(-g)) * u; }
@@ -122,35 +125,52 @@ __device__ __forceinline__ float acc_value(uint32_t bits) {
   else return __uint_as_float(bits);
 }
 
-template <int KIND, bool SWIGLU>
+// Pipeline geometry of the two variants. A scheduling unit is one 128-row M
+// tile (single CTA) or two consecutive M tiles of one expert (CTA pair).
+template <bool PAIR>
+struct Cfg {
+  static constexpr int kStages = PAIR ? 6 : 4;
+  static constexpr int kBRows = PAIR ? BN / 2 : BN;  // B rows this CTA loads per stage
+  static constexpr int kBBytes = kBRows * ROW_BYTES;
+  static constexpr int kStageBytes = A_BYTES + kBBytes;
+  static constexpr uint32_t kTxBytes = PAIR ? 2 * kStageBytes : kStageBytes;  // per stage, whole MMA
+  static constexpr int kGroupUnits = PAIR ? GROUP_M / 2 : GROUP_M;
+};
+
+template <int KIND, bool SWIGLU, bool PAIR>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     moe_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                     const Params p) {
+  using C = Cfg<PAIR>;
+  constexpr int S = C::kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
-  uint8_t* sB = smem + STAGES * A_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);
-  uint64_t* empty = full + STAGES;
-  uint64_t* tfull = empty + STAGES;
+  uint8_t* sB = smem + S * A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + S * C::kBBytes);
+  uint64_t* empty = full + S;
+  uint64_t* tfull = empty + S;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  int32_t* s_cum = reinterpret_cast<int32_t*>(smem + STAGES * STAGE_BYTES + BAR_BYTES);
+  int32_t* s_cum = reinterpret_cast<int32_t*>(smem + S * C::kStageBytes + BAR_BYTES);
+  int32_t* s_ucum = PAIR ? s_cum + (p.E + 1) : s_cum;  // scheduling-unit prefix per expert
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int E = p.E;
+  const uint32_t rank = PAIR ? ptx::cluster_ctarank() : 0;
+  const bool leader = rank == 0;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
+    for (int s = 0; s < S; ++s) {
       ptx::mbar_init(&full[s], 1);
       ptx::mbar_init(&empty[s], 1);
     }
     for (int a = 0; a < 2; ++a) {
       ptx::mbar_init(&tfull[a], 1);
-      ptx::mbar_init(&tempty[a], 4 * 32);
+      ptx::mbar_init(&tempty[a], (PAIR ? 2 : 1) * 4 * 32);  // epilogue threads of the whole MMA
     }
     ptx::mbar_init(drain, 1);
     *abort_flag = 0;
@@ -161,72 +181,140 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     ptx::prefetch_tmap(&tmap_b);
   }
   for (int i = threadIdx.x; i <= E; i += blockDim.x) s_cum[i] = p.table[TileTable::cum_off() + i];
+  if constexpr (PAIR) {
+    __syncthreads();
+    if (warp == 0) {  // pairs per expert = ceil(tiles / 2), prefix-summed by one warp
+      const int per = (E + 31) / 32;
+      const int lo = min(E, lane * per), hi = min(E, lo + per);
+      int sum = 0;
+      for (int e = lo; e < hi; ++e) sum += (s_cum[e + 1] - s_cum[e] + 1) >> 1;
+      int incl = sum;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += v;
+      }
+      int run = incl - sum;
+      for (int e = lo; e < hi; ++e) {
+        s_ucum[e] = run;
+        run += (s_cum[e + 1] - s_cum[e] + 1) >> 1;
+      }
+      if (lane == 31) s_ucum[E] = incl;
+    }
+  }
   if (warp == 1) {
-    ptx::tmem_alloc(tmem_slot, TMEM_COLS);
-    ptx::tmem_relinquish();
+    if constexpr (PAIR) {
+      ptx::tmem_alloc_pair(tmem_slot, TMEM_COLS);
+      ptx::tmem_relinquish_pair();
+    } else {
+      ptx::tmem_alloc(tmem_slot, TMEM_COLS);
+      ptx::tmem_relinquish();
+    }
   }
   ptx::tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) ptx::cluster_sync();  // the leader's barriers exist before the peer signals them
   ptx::tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
   const int NT = p.n_tiles;
-  const int total = s_cum[E] * NT;
+  const int total = s_ucum[E] * NT;
+  const int unit0 = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+  const int ustride = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
   const int32_t* row_start_tab = p.table + TileTable::start_off(E);
   const int32_t* row_count_tab = p.table + TileTable::count_off(E, p.max_tiles);
+
+  // unit t -> (expert e, n tile, this CTA's M tile m, whether m holds rows)
+  auto locate = [&](int t, int& e, int& n, int& m, bool& valid) {
+    int u;
+    decode_unit(t, s_ucum, E, NT, C::kGroupUnits, u, n, e);
+    if constexpr (PAIR) {
+      m = s_cum[e] + 2 * (u - s_ucum[e]) + (int)rank;
+      valid = m < s_cum[e + 1];
+    } else {
+      m = u;
+      valid = true;
+    }
+  };
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
-      int last_par[STAGES];
+      int last_par[S];
 #pragma unroll
-      for (int s = 0; s < STAGES; ++s) last_par[s] = -1;
+      for (int s = 0; s < S; ++s) last_par[s] = -1;
       bool ok = true;
-      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
-        int m, n, e;
-        decode_tile(t, s_cum, E, NT, m, n, e);
-        const int row0 = row_start_tab[m];
-        const int brow = e * p.b_rows_per_expert + n * (SWIGLU ? BN / 2 : BN);
+      for (int t = unit0; t < total && ok; t += ustride) {
+        int e, n, m;
+        bool valid;
+        locate(t, e, n, m, valid);
+        // an empty peer half still loads a (masked) A box: the rows after the
+        // expert's last tile
+        const int row0 = valid ? row_start_tab[m] : row_start_tab[m - 1] + BM;
+        int brow;
+        if constexpr (SWIGLU)
+          brow = e * p.b_rows_per_expert + n * (BN / 2) + ((PAIR && rank) ? p.inter : 0);
+        else
+          brow = e * p.b_rows_per_expert + n * BN + (PAIR ? (int)rank * (BN / 2) : 0);
         for (int kb = 0; kb < p.num_kb; ++kb) {
           if (!ptx::mbar_wait(&empty[stage], phase ^ 1, abort_flag)) {
             ok = false;
             break;
           }
-          ptx::mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
           const int kx = kb * (ROW_BYTES / (KIND == 0 ? 2 : (KIND == 1 ? 4 : 1)));
-          ptx::tma_load_2d(sA + stage * A_BYTES, &tmap_a, &full[stage], kx, row0);
-          if constexpr (SWIGLU) {
-            ptx::tma_load_2d(sB + stage * B_BYTES, &tmap_b, &full[stage], kx, brow);
-            ptx::tma_load_2d(sB + stage * B_BYTES + B_BYTES / 2, &tmap_b, &full[stage], kx, brow + p.inter);
+          if constexpr (PAIR) {
+            if (leader) ptx::mbar_arrive_expect_tx(&full[stage], C::kTxBytes);
+            const uint32_t bar = ptx::mapa(ptx::smem_u32(&full[stage]), 0);  // the leader's full barrier
+            ptx::tma_load_2d_pair(sA + stage * A_BYTES, &tmap_a, bar, kx, row0);
+            ptx::tma_load_2d_pair(sB + stage * C::kBBytes, &tmap_b, bar, kx, brow);
           } else {
-            ptx::tma_load_2d(sB + stage * B_BYTES, &tmap_b, &full[stage], kx, brow);
+            ptx::mbar_arrive_expect_tx(&full[stage], C::kTxBytes);
+            ptx::tma_load_2d(sA + stage * A_BYTES, &tmap_a, &full[stage], kx, row0);
+            if constexpr (SWIGLU) {
+              ptx::tma_load_2d(sB + stage * C::kBBytes, &tmap_b, &full[stage], kx, brow);
+              ptx::tma_load_2d(sB + stage * C::kBBytes + C::kBBytes / 2, &tmap_b, &full[stage], kx, brow + p.inter);
+            } else {
+              ptx::tma_load_2d(sB + stage * C::kBBytes, &tmap_b, &full[stage], kx, brow);
+            }
           }
           last_par[stage] = (int)phase;
-          if (++stage == STAGES) {
+          if (++stage == S) {
             stage = 0;
             phase ^= 1;
           }
         }
       }
+      volatile int never = 0;
       if (!ok) {
         raise_device_error(1);
         *abort_flag = 1;
-        // let the copies already in flight land before the CTA exits
-        volatile int never = 0;
-        for (int s = 0; s < STAGES; ++s)
-          if (last_par[s] >= 0) ptx::mbar_wait(&full[s], (uint32_t)last_par[s], &never);
+        // let this CTA's copies already in flight land before it exits (in a
+        // pair they are counted on the leader's barriers)
+        if (!PAIR || leader)
+          for (int s = 0; s < S; ++s)
+            if (last_par[s] >= 0) ptx::mbar_wait(&full[s], (uint32_t)last_par[s], &never);
+      } else if constexpr (PAIR) {
+        // every stage this CTA filled has been released by the leader's MMA
+        // commit (which also lands on this CTA's barriers) before exiting
+        for (int i = 0; i < S; ++i) {
+          if (!ptx::mbar_wait(&empty[stage], phase ^ 1, &never)) raise_device_error(4);
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
       }
     }
   } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    // ------------------------------------------------------------ MMA issuer (the leader of a pair)
+    if (lane == 0 && leader) {
       int stage = 0;
       uint32_t phase = 0;
       int it = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++it) {
+      for (int t = unit0; t < total && ok; t += ustride, ++it) {
         const int acc = it & 1;
         const uint32_t acc_par = (it >> 1) & 1;
         if (!ptx::mbar_wait(&tempty[acc], acc_par ^ 1, abort_flag)) {
@@ -242,27 +330,32 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           }
           ptx::tc_fence_after();
           const uint32_t a_addr = ptx::smem_u32(sA + stage * A_BYTES);
-          const uint32_t b_addr = ptx::smem_u32(sB + stage * B_BYTES);
+          const uint32_t b_addr = ptx::smem_u32(sB + stage * C::kBBytes);
 #pragma unroll
           for (int k = 0; k < ROW_BYTES / 32; ++k) {
-            ptx::umma<KIND>(d, ptx::smem_desc_k128(a_addr + k * 32), ptx::smem_desc_k128(b_addr + k * 32), p.idesc,
-                            (kb > 0 || k > 0) ? 1u : 0u);
+            const uint64_t ad = ptx::smem_desc_k128(a_addr + k * 32), bd = ptx::smem_desc_k128(b_addr + k * 32);
+            const uint32_t accum = (kb > 0 || k > 0) ? 1u : 0u;
+            if constexpr (PAIR) ptx::umma_pair<KIND>(d, ad, bd, p.idesc, accum);
+            else ptx::umma<KIND>(d, ad, bd, p.idesc, accum);
           }
-          ptx::umma_commit(&empty[stage]);
-          if (++stage == STAGES) {
+          if constexpr (PAIR) ptx::umma_commit_pair_mc(&empty[stage], 0x3);
+          else ptx::umma_commit(&empty[stage]);
+          if (++stage == S) {
             stage = 0;
             phase ^= 1;
           }
         }
         if (!ok) break;
-        ptx::umma_commit(&tfull[acc]);
+        if constexpr (PAIR) ptx::umma_commit_pair_mc(&tfull[acc], 0x3);
+        else ptx::umma_commit(&tfull[acc]);
       }
       if (!ok) {
         raise_device_error(2);
         *abort_flag = 1;
       }
       // all MMAs issued by this thread complete before TMEM is released
-      ptx::umma_commit(drain);
+      if constexpr (PAIR) ptx::umma_commit_pair(drain);
+      else ptx::umma_commit(drain);
       volatile int never = 0;
       if (!ptx::mbar_wait(drain, 0, &never)) raise_device_error(4);
     }
@@ -270,11 +363,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;          // TMEM lane quarter this warp may access
     const int r = q * 32 + lane;     // row of the tile held by this thread
+    const uint32_t tempty_leader[2] = {PAIR ? ptx::mapa(ptx::smem_u32(&tempty[0]), 0) : ptx::smem_u32(&tempty[0]),
+                                       PAIR ? ptx::mapa(ptx::smem_u32(&tempty[1]), 0) : ptx::smem_u32(&tempty[1])};
     int it = 0;
     bool ok = true;
-    for (int t = blockIdx.x; t < total; t += gridDim.x, ++it) {
-      int m, n, e;
-      decode_tile(t, s_cum, E, NT, m, n, e);
+    for (int t = unit0; t < total; t += ustride, ++it) {
+      int e, n, m;
+      bool valid;
+      locate(t, e, n, m, valid);
       const int acc = it & 1;
       const uint32_t acc_par = (it >> 1) & 1;
       bool w_ok = ptx::mbar_wait(&tfull[acc], acc_par, abort_flag);
@@ -283,8 +379,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         break;
       }
       ptx::tc_fence_after();
-      const int32_t rstart = row_start_tab[m];
-      const int32_t rcount = row_count_tab[m];
+      const int32_t rstart = valid ? row_start_tab[m] : 0;
+      const int32_t rcount = valid ? row_count_tab[m] : 0;
       const int64_t grow = (int64_t)rstart + r;
       const bool row_ok = (r < rcount) && (grow < p.a_rows);
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
@@ -366,7 +462,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
       }
       ptx::tc_fence_before();
-      ptx::mbar_arrive(&tempty[acc]);
+      if constexpr (PAIR) ptx::mbar_arrive_cluster(tempty_leader[acc]);
+      else ptx::mbar_arrive(&tempty[acc]);
     }
     if (!ok) {
       if (lane == 0) raise_device_error(3);
@@ -375,10 +472,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   }
 
   __syncthreads();
+  if constexpr (PAIR) ptx::cluster_sync();  // no CTA leaves while its peer may still signal it
   if (warp == 1) {
     __syncwarp();
     ptx::tc_fence_after();
-    ptx::tmem_dealloc(tmem_base, TMEM_COLS);
+    if constexpr (PAIR) ptx::tmem_dealloc_pair(tmem_base, TMEM_COLS);
+    else ptx::tmem_dealloc(tmem_base, TMEM_COLS);
   }
 }
 
@@ -422,7 +521,8 @@ int make_tmap(CUtensorMap* m, const void* ptr, int dtype, uint64_t inner, uint64
   return MOE_OK;
 }
 
-uint32_t make_idesc(int dtype) {
+// tcgen05 instruction descriptor: accumulator format, A/B formats, N, M.
+uint32_t make_idesc(int dtype, int m) {
   int c_fmt = 1, ab = 1;  // fp32 accumulate, bf16 operands
   if (dtype == MOE_F16) ab = 0;
   else if (dtype == MOE_F32) ab = 2;  // tf32
@@ -431,33 +531,69 @@ uint32_t make_idesc(int dtype) {
     ab = 1;     // signed int8
   }
   return ((uint32_t)c_fmt << 4) | ((uint32_t)ab << 7) | ((uint32_t)ab << 10) | ((uint32_t)(BN >> 3) << 17) |
-         ((uint32_t)(BM >> 4) << 24);
+         ((uint32_t)(m >> 4) << 24);
 }
 
 int kind_of(int dtype) { return dtype == MOE_F32 ? 1 : (dtype == MOE_I8 ? 2 : 0); }
 
-size_t gemm_smem_bytes(int E) { return 1024 + (size_t)STAGES * STAGE_BYTES + BAR_BYTES + (size_t)(E + 1) * 4; }
+// GEMM variant: 1 = CTA pairs (cta_group::2), 0 = one CTA per tile,
+// 2 = automatic: pairs when the experts average at least 4 M tiles, so that
+// an expert's odd last tile (which idles half a pair) costs little.
+std::atomic<int> g_gemm_cta_pair{2};
 
-template <int KIND, bool SWIGLU>
-int launch_kind(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, unsigned grid, cudaStream_t st) {
-  const size_t smem = gemm_smem_bytes(p.E);
-  auto kfn = moe_gemm_kernel<KIND, SWIGLU>;
+bool use_pair(int64_t max_tiles, int E) {
+  const int v = g_gemm_cta_pair.load();
+  if (v == 2) return max_tiles >= 4 * (int64_t)E;
+  return v != 0;
+}
+
+template <bool PAIR>
+size_t gemm_smem_bytes(int E) {
+  return 1024 + (size_t)Cfg<PAIR>::kStages * Cfg<PAIR>::kStageBytes + BAR_BYTES + (size_t)2 * (E + 1) * 4;
+}
+
+template <int KIND, bool SWIGLU, bool PAIR>
+int launch_kind(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, int64_t units_ub, cudaStream_t st) {
+  const size_t smem = gemm_smem_bytes<PAIR>(p.E);
+  auto kfn = moe_gemm_kernel<KIND, SWIGLU, PAIR>;
   MOE_CUDA_TRY(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  kfn<<<grid, NUM_THREADS, smem, st>>>(ta, tb, p);
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  cfg.blockDim = dim3(NUM_THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  int64_t grid;
+  if constexpr (PAIR) {
+    MOE_CUDA_TRY(cudaFuncSetAttribute(kfn, cudaFuncAttributeNonPortableClusterSizeAllowed, 0));
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cfg.gridDim = dim3(2 * (unsigned)(num_sms() / 2));
+    int clusters = 0;
+    MOE_CUDA_TRY(cudaOccupancyMaxActiveClusters(&clusters, kfn, &cfg));
+    if (clusters <= 0) return set_error(MOE_ERR_CUDA, "moe_gemm_kernel: no CTA pair fits on the device");
+    grid = 2 * std::min<int64_t>(clusters, units_ub);
+  } else {
+    grid = std::min<int64_t>(num_sms(), units_ub);
+  }
+  if (grid <= 0) return MOE_OK;
+  cfg.gridDim = dim3((unsigned)grid);
+  MOE_CUDA_TRY(cudaLaunchKernelEx(&cfg, kfn, ta, tb, p));
   MOE_LAUNCH_CHECK("moe_gemm_kernel");
   return MOE_OK;
 }
 
-template <bool SWIGLU>
+template <bool SWIGLU, bool PAIR>
 int launch(int dtype, const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, cudaStream_t st) {
-  int64_t tiles_ub = (int64_t)p.max_tiles * p.n_tiles;
-  int64_t grid = num_sms();
-  if (tiles_ub < grid) grid = tiles_ub;
-  if (grid <= 0) return MOE_OK;
+  // units: M tiles (single CTA) or M-tile pairs, upper bound max_tiles
+  const int64_t units_ub = (int64_t)(PAIR ? (p.max_tiles + p.E) / 2 + p.E : p.max_tiles) * p.n_tiles;
   switch (kind_of(dtype)) {
-    case 0: return launch_kind<0, SWIGLU>(ta, tb, p, (unsigned)grid, st);
-    case 1: return launch_kind<1, SWIGLU>(ta, tb, p, (unsigned)grid, st);
-    default: return launch_kind<2, SWIGLU>(ta, tb, p, (unsigned)grid, st);
+    case 0: return launch_kind<0, SWIGLU, PAIR>(ta, tb, p, units_ub, st);
+    case 1: return launch_kind<1, SWIGLU, PAIR>(ta, tb, p, units_ub, st);
+    default: return launch_kind<2, SWIGLU, PAIR>(ta, tb, p, units_ub, st);
   }
 }
 
@@ -503,6 +639,7 @@ extern "C" int moe_gemm1_swiglu(const void* a, int dtype, int64_t a_rows, int64_
                 "moe_gemm1_swiglu: pointers must be 16-byte aligned");
   if (a_rows == 0 || max_tiles == 0) return MOE_OK;
   CUtensorMap ta, tb;
+  const bool pair = use_pair(max_tiles, num_experts);
   MOE_TRY(make_tmap(&ta, a, dtype, hidden, a_rows, BM));
   MOE_TRY(make_tmap(&tb, w13, dtype, hidden, (uint64_t)num_experts * 2 * inter, BN / 2));
   Params p{};
@@ -512,7 +649,7 @@ extern "C" int moe_gemm1_swiglu(const void* a, int dtype, int64_t a_rows, int64_
   p.n_valid = (int)inter;
   p.b_rows_per_expert = (int)(2 * inter);
   p.inter = (int)inter;
-  p.idesc = make_idesc(dtype);
+  p.idesc = make_idesc(dtype, pair ? 2 * BM : BM);
   p.table = tile_table;
   p.max_tiles = (int)max_tiles;
   p.a_rows = a_rows;
@@ -524,7 +661,8 @@ extern "C" int moe_gemm1_swiglu(const void* a, int dtype, int64_t a_rows, int64_
   p.a_scale = a_scale;
   p.b_scale = w13_scale;
   p.top_k = 1;
-  return launch<true>(dtype, ta, tb, p, as_stream(stream));
+  return pair ? launch<true, true>(dtype, ta, tb, p, as_stream(stream))
+              : launch<true, false>(dtype, ta, tb, p, as_stream(stream));
 }
 
 extern "C" int moe_gemm2(const void* h, int dtype, int64_t h_rows, int64_t inter, const void* w2, int num_experts,
@@ -551,8 +689,9 @@ extern "C" int moe_gemm2(const void* h, int dtype, int64_t h_rows, int64_t inter
                 "moe_gemm2: pointers must be 16-byte aligned");
   if (h_rows == 0 || max_tiles == 0) return MOE_OK;
   CUtensorMap ta, tb;
+  const bool pair = use_pair(max_tiles, num_experts);
   MOE_TRY(make_tmap(&ta, h, dtype, inter, h_rows, BM));
-  MOE_TRY(make_tmap(&tb, w2, dtype, inter, (uint64_t)num_experts * hidden, BN));
+  MOE_TRY(make_tmap(&tb, w2, dtype, inter, (uint64_t)num_experts * hidden, pair ? BN / 2 : BN));
   Params p{};
   p.E = num_experts;
   p.num_kb = (int)ceil_div(inter * dtype_size(dtype), ROW_BYTES);
@@ -560,7 +699,7 @@ extern "C" int moe_gemm2(const void* h, int dtype, int64_t h_rows, int64_t inter
   p.n_valid = (int)hidden;
   p.b_rows_per_expert = (int)hidden;
   p.inter = (int)inter;
-  p.idesc = make_idesc(dtype);
+  p.idesc = make_idesc(dtype, pair ? 2 * BM : BM);
   p.table = tile_table;
   p.max_tiles = (int)max_tiles;
   p.a_rows = h_rows;
@@ -574,5 +713,20 @@ extern "C" int moe_gemm2(const void* h, int dtype, int64_t h_rows, int64_t inter
   p.row_map = row_map;
   p.row_weight = row_weight;
   p.top_k = top_k > 0 ? top_k : 1;
-  return launch<false>(dtype, ta, tb, p, as_stream(stream));
+  return pair ? launch<false, true>(dtype, ta, tb, p, as_stream(stream))
+              : launch<false, false>(dtype, ta, tb, p, as_stream(stream));
+}
+
+extern "C" int moe_set_option(int option, int value) {
+  if (option == MOE_OPT_GEMM_CTA_PAIR) {
+    MOE_CHECK_ARG(value >= 0 && value <= 2, "moe_set_option: GEMM_CTA_PAIR takes 0, 1 or 2");
+    g_gemm_cta_pair.store(value);
+    return MOE_OK;
+  }
+  return set_error(MOE_ERR_INVALID_ARG, "moe_set_option: unknown option %d", option);
+}
+
+extern "C" int moe_get_option(int option) {
+  if (option == MOE_OPT_GEMM_CTA_PAIR) return g_gemm_cta_pair.load();
+  return -1;
 }

@@ -39,6 +39,17 @@ def assert_no_device_error():
     assert mb.device_error(dev()) == 0
 
 
+@pytest.fixture(params=[1, 0], ids=["cta_pair", "single_cta"])
+def gemm_variant(request):
+    """Runs a test with the CTA-pair (cta_group::2) GEMMs and again with one
+    CTA per tile."""
+    lib = _lib.load()
+    old = lib.moe_get_option(_lib.OPT_GEMM_CTA_PAIR)
+    assert lib.moe_set_option(_lib.OPT_GEMM_CTA_PAIR, request.param) == 0
+    yield request.param
+    lib.moe_set_option(_lib.OPT_GEMM_CTA_PAIR, old)
+
+
 # --------------------------------------------------------------------------- tile schedule
 
 
@@ -146,7 +157,7 @@ def test_gather_rows_bit_exact():
 
 @pytest.mark.parametrize("case", ["mlp_selfcheck_f32", "mlp_selftest_f16", "mlp_ragged_f32"])
 @pytest.mark.parametrize("dtype", [None, torch.bfloat16])
-def test_pre_routed_matches_reference_golden(case, dtype):
+def test_pre_routed_matches_reference_golden(case, dtype, gemm_variant):
     d = np.load(os.path.join(GOLDEN, case + ".npz"))
     dt = dtype or {np.float16: torch.float16, np.float32: torch.float32}[d["x"].dtype.type]
     x = torch.from_numpy(d["x"]).to(dev(), dt)
@@ -165,7 +176,7 @@ def test_pre_routed_matches_reference_golden(case, dtype):
     assert_no_device_error()
 
 
-def test_pre_routed_non_kmajor_weights_and_tail_rows():
+def test_pre_routed_non_kmajor_weights_and_tail_rows(gemm_variant):
     rng = np.random.default_rng(9)
     E, H, I = 3, 256, 384
     gs = np.array([100, 0, 77])
@@ -205,7 +216,7 @@ def run_topk(x, w13, w2, ids, wts, scales=None):
     (256, 2048, 768, 128, 8, "zipf1.2", torch.bfloat16),
     (777, 256, 136, 6, 3, "uniform-softmax", torch.bfloat16),   # ragged I (not a multiple of 128)
 ])
-def test_topk_matches_oracle(T, H, I, E, k, routing, dtype):
+def test_topk_matches_oracle(T, H, I, E, k, routing, dtype, gemm_variant):
     x, w13, w2, ids, wts = topk_case(T, H, I, E, k, routing, dtype)
     y = run_topk(x, w13, w2, ids, wts)
     assert y.dtype == dtype and y.shape == (T, H)
@@ -216,7 +227,7 @@ def test_topk_matches_oracle(T, H, I, E, k, routing, dtype):
     assert_no_device_error()
 
 
-def test_topk_drops_out_of_range_ids():
+def test_topk_drops_out_of_range_ids(gemm_variant):
     x, w13, w2, ids, wts = topk_case(128, 256, 128, 4, 2, "uniform-softmax", torch.bfloat16)
     ids = ids.copy()
     ids[::3, 1] = -1      # expert-parallel style "not mine"
@@ -226,7 +237,7 @@ def test_topk_drops_out_of_range_ids():
     assert max_abs_rel(npf(y), ref) < TOL
 
 
-def test_w8a8_matches_oracle():
+def test_w8a8_matches_oracle(gemm_variant):
     T, H, I, E, k = 256, 512, 256, 16, 4
     x, w13, w2, ids, wts = topk_case(T, H, I, E, k, "sigmoid", torch.bfloat16, seed=3)
     w13q, w2q, scales = mb.quantize_weights_int8(w13, w2)
@@ -283,7 +294,7 @@ def test_mixtral_full_size_sampled_and_properties():
 
 
 @pytest.mark.parametrize("quant", [False, True])
-def test_large_output_uses_row_store_combine(quant):
+def test_large_output_uses_row_store_combine(quant, gemm_variant):
     """T x H fp32 accumulator above 80 MiB: GEMM2 stores rows and the
     deterministic combine sums them (the path a DeepSeek-V3-sized batch takes)."""
     T, H, I, E, k = 4096, 7168, 256, 32, 8   # 4096 x 7168 x 4 B = 117 MB
@@ -309,7 +320,7 @@ def test_large_output_uses_row_store_combine(quant):
 
 
 @pytest.mark.parametrize("dtype,quant", [(torch.bfloat16, False), (torch.bfloat16, True), (torch.float32, False)])
-def test_fused_expert_rows_matches_oracle(dtype, quant):
+def test_fused_expert_rows_matches_oracle(dtype, quant, gemm_variant):
     R, H, I, E = 333, 512, 384, 6
     rng = np.random.default_rng(8)
     x = torch.from_numpy(rng.standard_normal((R, H), dtype=np.float32)).to(dev(), dtype)
