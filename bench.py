@@ -241,6 +241,9 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="mixtral", choices=sorted(CONFIGS))
     ap.add_argument("--tokens", type=int, default=0, help="override tokens per GPU (profiling cases)")
+    ap.add_argument("--ep", default="peer", choices=["peer", "nccl"],
+                    help="expert-parallel exchange (N > 1): fused into the kernels over NVLink peer memory, "
+                         "or NCCL all-to-all")
     ap.add_argument("--gemm", default="auto", choices=["auto", "pair", "single"],
                     help="grouped GEMM variant: CTA pairs (cta_group::2), one CTA per tile, or chosen by size")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -259,6 +262,7 @@ def main():
     config_json = {"workload": cfg["desc"], "tokens_per_gpu": T, "hidden": H, "inter": I, "experts": E,
                    "top_k": k, "routing": cfg["routing"], "dtype": cfg["dtype"] + ("+w8a8" if cfg["quant"] else ""),
                    "parallelism": f"ep{world}" if world > 1 else "single", "gemm": args.gemm,
+                   "ep_exchange": args.ep if world > 1 else None,
                    "l2": "weights (%.2f GB) exceed the 126 MB L2, streamed every step" %
                          (E * 3 * H * I * (1 if cfg["quant"] else (4 if cfg["dtype"] == "fp32" else 2)) / 1e9)}
 
@@ -297,7 +301,10 @@ def main():
         assert E % world == 0, "experts must divide evenly over ranks"
         local = list(range(rank * E // world, (rank + 1) * E // world))
         w13, w2, scales = make_weights(cfg, local, device, dt)
-        layer = mep.ExpertParallelMoE(w13, w2, E, scales=scales)
+        if args.ep == "peer":
+            layer = mep.PeerExpertParallelMoE(w13, w2, E, max_tokens=T, top_k=k, dtype=dt, scales=scales)
+        else:
+            layer = mep.ExpertParallelMoE(w13, w2, E, scales=scales)
 
         def step(xx, ii, ww):
             return layer(xx, ww, ii)
@@ -420,6 +427,8 @@ def main():
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
+        if hasattr(layer, "close"):
+            layer.close()
         dist.barrier(device_ids=[local_rank])
         dist.destroy_process_group()
     return 0

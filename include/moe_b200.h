@@ -272,6 +272,48 @@ MOE_API int moe_fused_expert_rows(const void* x, int x_dtype, int64_t rows, int6
                                   const int32_t* expert_ids, const float* w13_scale, const float* w2_scale,
                                   void* out, void* workspace, size_t workspace_bytes, void* stream);
 
+/* --------------------------------------------------------------------------
+ * Expert parallelism over NVLink peer memory (no reference counterpart: the
+ * reference has no distributed code). Rank r of W owns experts
+ * [r*EL, (r+1)*EL). Each rank allocates once (moe_ipc_malloc) a receive
+ * buffer of recv_cap rows laid out as the padded, expert-sorted input of its
+ * local experts, a row-tag array (int32 per row) and a return buffer, and
+ * opens its peers' buffers (moe_ipc_open). Per forward:
+ *   moe_align(block_m = 1) of the local top-k ids; all-gather of the
+ *   group sizes into counts_all [W, E] (int32);
+ *   moe_ep_plan: dest_base[e] = first row of this rank's expert-e rows in the
+ *     owner's buffer; this rank's tile table over its local experts; tag -1
+ *     on its own padding rows; ret_pos[s] = s for routed slots, else -1;
+ *   moe_ep_dispatch: row of every routed slot stored into the owner's buffer
+ *     (peer stores; int8-quantised when recv_dtype is MOE_I8) with tag
+ *     (rank << 24) | slot;
+ *   barrier across ranks;
+ *   moe_ep_expert_pass: local gate_up GEMM + SwiGLU, down GEMM whose
+ *     epilogue stores row r to peer_ret[tag >> 24] at row tag & 0xFFFFFF;
+ *   barrier; moe_combine_rows(return buffer, ret_pos, topk_weights).
+ * peer_* arguments are device arrays of W device pointers.
+ * -------------------------------------------------------------------------- */
+#define MOE_IPC_HANDLE_BYTES 64
+MOE_API int moe_ipc_malloc(size_t bytes, void** ptr, void* handle);
+MOE_API int moe_ipc_open(const void* handle, void** ptr);
+MOE_API int moe_ipc_close(void* ptr);
+MOE_API int moe_ipc_free(void* ptr);
+MOE_API int moe_ep_plan(const int32_t* counts_all, int world, int rank, int num_experts, const int32_t* slot_pos,
+                        int64_t num_slots, int32_t* dest_base, int32_t* tile_table, int64_t max_tiles,
+                        int32_t* recv_meta, int64_t recv_cap, int32_t* ret_pos, void* stream);
+MOE_API int moe_ep_dispatch(const void* x, int x_dtype, int64_t hidden, int top_k, const int32_t* topk_ids,
+                            const int32_t* sorted_slots, const int32_t* seg_start, const int32_t* dest_base,
+                            const int32_t* n_valid_dev, int64_t max_rows, int world, int rank,
+                            int experts_per_rank, int64_t recv_cap, void* const* peer_x, int recv_dtype,
+                            float* const* peer_scale, int32_t* const* peer_meta, int* err, void* stream);
+MOE_API size_t moe_ep_expert_pass_workspace_size(int64_t recv_cap, int64_t inter, int x_dtype);
+MOE_API int moe_ep_expert_pass(const void* recv_x, int x_dtype, const float* recv_scale, int64_t recv_cap,
+                               int64_t hidden, const void* w13, const void* w2, int experts_per_rank,
+                               int64_t inter, const float* w13_scale, const float* w2_scale,
+                               const int32_t* tile_table, const int32_t* recv_meta, void* const* peer_ret,
+                               int world, int64_t ret_rows, int out_dtype, void* workspace,
+                               size_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

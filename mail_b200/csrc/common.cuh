@@ -33,6 +33,9 @@ int set_error(int code, const char* fmt, ...);
 // Counts one kernel launch (moe_launch_count).
 void note_launch();
 
+// Records the caller's profiling event for stage `stage` (moe_set_stage_events).
+int record_stage(int stage, cudaStream_t st);
+
 #define MOE_LAUNCH_CHECK(name)                                                                   \
   do {                                                                                           \
     cudaError_t e_ = cudaGetLastError();                                                         \
@@ -80,6 +83,17 @@ struct TileTable {
 // Device error codes latched by the GEMM kernels (first error wins):
 // 1 = TMA producer wait, 2 = MMA issuer wait, 3 = epilogue wait, 4 = drain wait.
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+// Internal GEMM2 epilogue (expert-parallel return path): row r's result goes
+// to peer_out[meta >> 24] at row meta & 0xFFFFFF, meta = row_map[r] (< 0: skip).
+constexpr int kEpiScatterPeer = 3;
+
+// Down GEMM whose epilogue stores each output row into the buffer of the rank
+// that sent the row (peer pointers, NVLink stores). Defined in moe_gemm.cu.
+int gemm2_scatter_peer(const void* h, int dtype, int64_t h_rows, int64_t inter, const void* w2, int num_experts,
+                       int64_t hidden, const float* h_scale, const float* w2_scale, const int32_t* tile_table,
+                       int64_t max_tiles, const int32_t* row_meta, void* const* peer_out, int num_peers,
+                       int64_t peer_rows, int out_dtype, cudaStream_t stream);
 
 inline int num_sms() {
   static int cache[64] = {0};

@@ -19,12 +19,13 @@ std::atomic<int64_t> g_launches{0};
 thread_local void* const* g_stage_events = nullptr;
 thread_local int g_num_stage_events = 0;
 
+}  // namespace
+
 int record_stage(int stage, cudaStream_t st) {
   if (g_stage_events && stage < g_num_stage_events && g_stage_events[stage])
     MOE_CUDA_TRY(cudaEventRecord(static_cast<cudaEvent_t>(g_stage_events[stage]), st));
   return MOE_OK;
 }
-}  // namespace
 
 void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 

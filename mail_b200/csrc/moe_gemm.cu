@@ -67,6 +67,8 @@ struct Params {
   const int32_t* row_map;
   const float* row_weight;
   int top_k;
+  void* const* peer_out;  // kEpiScatterPeer: device array of per-rank output bases
+  int num_peers;
 };
 
 // Scheduling unit t -> (unit u, n tile, expert e) in expert-major order:
@@ -421,12 +423,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         int64_t dst_row = grow;
         float wgt = 1.f;
         bool do_store = row_ok;
+        void* obase = p.out;
         if (p.epi != MOE_EPI_STORE_ROWS && row_ok) {
           const int32_t slot = p.row_map[grow];
           do_store = slot >= 0;
           if (slot >= 0) {
-            dst_row = (p.epi == MOE_EPI_COMBINE_ADD) ? (int64_t)(slot / p.top_k) : (int64_t)slot;
-            if (p.row_weight) wgt = p.row_weight[slot];
+            if (p.epi == kEpiScatterPeer) {
+              const int src = slot >> 24;
+              dst_row = slot & 0xFFFFFF;
+              if (src < p.num_peers) obase = p.peer_out[src];
+              else do_store = false;
+            } else {
+              dst_row = (p.epi == MOE_EPI_COMBINE_ADD) ? (int64_t)(slot / p.top_k) : (int64_t)slot;
+              if (p.row_weight) wgt = p.row_weight[slot];
+            }
           }
         }
         if (dst_row >= p.out_rows) do_store = false;
@@ -454,7 +464,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                   red_add4(dst, f[0], f[1], f[2], f[3]);
                   red_add4(dst + 4, f[4], f[5], f[6], f[7]);
                 } else {
-                  store8_out(p.out, p.out_dtype, dst_row * p.ldo + cj, f);
+                  store8_out(obase, p.out_dtype, dst_row * p.ldo + cj, f);
                 }
               }
             }
@@ -665,25 +675,27 @@ extern "C" int moe_gemm1_swiglu(const void* a, int dtype, int64_t a_rows, int64_
               : launch<true, false>(dtype, ta, tb, p, as_stream(stream));
 }
 
-extern "C" int moe_gemm2(const void* h, int dtype, int64_t h_rows, int64_t inter, const void* w2, int num_experts,
-                         int64_t hidden, const float* h_scale, const float* w2_scale, const int32_t* tile_table,
-                         int64_t max_tiles, int epilogue, const int32_t* row_map, const float* row_weight,
-                         int top_k, void* out, int out_dtype, int64_t out_rows, void* stream) {
+namespace moe {
+namespace {
+int gemm2_impl(const void* h, int dtype, int64_t h_rows, int64_t inter, const void* w2, int num_experts,
+               int64_t hidden, const float* h_scale, const float* w2_scale, const int32_t* tile_table,
+               int64_t max_tiles, int epilogue, const int32_t* row_map, const float* row_weight, int top_k,
+               void* out, int out_dtype, int64_t out_rows, void* const* peer_out, int num_peers,
+               cudaStream_t stream) {
   MOE_TRY(check_gemm_common("moe_gemm2", dtype, inter, num_experts, tile_table, max_tiles));
-  MOE_CHECK_ARG(h && w2 && out, "moe_gemm2: NULL pointer");
+  MOE_CHECK_ARG(h && w2 && (out || peer_out), "moe_gemm2: NULL pointer");
   MOE_CHECK_ARG(hidden > 0 && hidden % 8 == 0, "moe_gemm2: hidden (%lld) must be a positive multiple of 8",
                 (long long)hidden);
   MOE_CHECK_ARG(h_rows >= 0 && h_rows < (int64_t(1) << 31), "moe_gemm2: h_rows out of range");
   MOE_CHECK_ARG((int64_t)num_experts * hidden < (int64_t(1) << 31), "moe_gemm2: weight rows overflow");
-  MOE_CHECK_ARG(epilogue == MOE_EPI_STORE_ROWS || epilogue == MOE_EPI_COMBINE_ADD || epilogue == MOE_EPI_SCATTER_ROWS,
-                "moe_gemm2: bad epilogue %d", epilogue);
   if (epilogue == MOE_EPI_COMBINE_ADD) {
     MOE_CHECK_ARG(out_dtype == MOE_F32, "moe_gemm2: the combine epilogue accumulates into fp32");
     MOE_CHECK_ARG(row_map && row_weight && top_k > 0, "moe_gemm2: combine needs row_map, row_weight, top_k");
   } else {
     MOE_CHECK_ARG(out_dtype == MOE_BF16 || out_dtype == MOE_F16 || out_dtype == MOE_F32, "moe_gemm2: bad out dtype");
   }
-  if (epilogue == MOE_EPI_SCATTER_ROWS) MOE_CHECK_ARG(row_map != nullptr, "moe_gemm2: scatter needs row_map");
+  if (epilogue == MOE_EPI_SCATTER_ROWS || epilogue == kEpiScatterPeer)
+    MOE_CHECK_ARG(row_map != nullptr, "moe_gemm2: scatter needs row_map");
   if (dtype == MOE_I8) MOE_CHECK_ARG(h_scale && w2_scale, "moe_gemm2: int8 needs h_scale and w2_scale");
   MOE_CHECK_ARG((uintptr_t)h % 16 == 0 && (uintptr_t)w2 % 16 == 0 && (uintptr_t)out % 16 == 0,
                 "moe_gemm2: pointers must be 16-byte aligned");
@@ -713,8 +725,32 @@ extern "C" int moe_gemm2(const void* h, int dtype, int64_t h_rows, int64_t inter
   p.row_map = row_map;
   p.row_weight = row_weight;
   p.top_k = top_k > 0 ? top_k : 1;
-  return pair ? launch<false, true>(dtype, ta, tb, p, as_stream(stream))
-              : launch<false, false>(dtype, ta, tb, p, as_stream(stream));
+  p.peer_out = peer_out;
+  p.num_peers = num_peers;
+  return pair ? launch<false, true>(dtype, ta, tb, p, stream) : launch<false, false>(dtype, ta, tb, p, stream);
+}
+}  // namespace
+
+int gemm2_scatter_peer(const void* h, int dtype, int64_t h_rows, int64_t inter, const void* w2, int num_experts,
+                       int64_t hidden, const float* h_scale, const float* w2_scale, const int32_t* tile_table,
+                       int64_t max_tiles, const int32_t* row_meta, void* const* peer_out, int num_peers,
+                       int64_t peer_rows, int out_dtype, cudaStream_t stream) {
+  MOE_CHECK_ARG(peer_out && num_peers > 0 && num_peers <= 256, "ep: bad peer output table");
+  return gemm2_impl(h, dtype, h_rows, inter, w2, num_experts, hidden, h_scale, w2_scale, tile_table, max_tiles,
+                    kEpiScatterPeer, row_meta, nullptr, 1, nullptr, out_dtype, peer_rows, peer_out, num_peers,
+                    stream);
+}
+}  // namespace moe
+
+extern "C" int moe_gemm2(const void* h, int dtype, int64_t h_rows, int64_t inter, const void* w2, int num_experts,
+                         int64_t hidden, const float* h_scale, const float* w2_scale, const int32_t* tile_table,
+                         int64_t max_tiles, int epilogue, const int32_t* row_map, const float* row_weight,
+                         int top_k, void* out, int out_dtype, int64_t out_rows, void* stream) {
+  MOE_CHECK_ARG(epilogue == MOE_EPI_STORE_ROWS || epilogue == MOE_EPI_COMBINE_ADD || epilogue == MOE_EPI_SCATTER_ROWS,
+                "moe_gemm2: bad epilogue %d", epilogue);
+  MOE_CHECK_ARG(out != nullptr, "moe_gemm2: NULL pointer");
+  return gemm2_impl(h, dtype, h_rows, inter, w2, num_experts, hidden, h_scale, w2_scale, tile_table, max_tiles,
+                    epilogue, row_map, row_weight, top_k, out, out_dtype, out_rows, nullptr, 0, as_stream(stream));
 }
 
 extern "C" int moe_set_option(int option, int value) {

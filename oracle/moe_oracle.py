@@ -335,3 +335,41 @@ def synthetic_routing(name: str, T: int, E: int, k: int, seed: int = 0):
         w = (w / w.sum(axis=1, keepdims=True)).astype(np.float32)
         return ids.astype(np.int32), w
     raise ValueError(name)
+
+
+# ---------------------------------------------------------------------------
+# Expert-parallel receive layout (no reference counterpart)
+
+
+def ep_plan(counts_all, rank: int, experts_per_rank: int, block_m: int = 128):
+    """Receive layout of expert parallelism over W ranks.
+
+    counts_all [W, E]: slots each rank routes to each global expert. Owner d
+    of expert e = e // EL stores expert e's rows at padded rows
+    [P(e), P(e) + pad(N_e)) of its buffer (P = exclusive prefix of the padded
+    totals within d's experts, N_e = sum over ranks), source s's rows after
+    those of ranks < s. Returns dest_base [E] for `rank` as the source and
+    the tile rows (row_start, row_count, tile_cumsum, total_rows) of `rank`
+    as the owner.
+    """
+    C = np.asarray(counts_all, np.int64)
+    W, E = C.shape
+    EL = experts_per_rank
+    tot = C.sum(axis=0)
+    pad = (tot + block_m - 1) // block_m * block_m
+    dest_base = np.zeros(E, np.int64)
+    for e in range(E):
+        d = e // EL
+        dest_base[e] = pad[d * EL:e].sum() + C[:rank, e].sum()
+    local = np.arange(rank * EL, (rank + 1) * EL)
+    tiles = (tot[local] + block_m - 1) // block_m
+    tcum = np.concatenate([[0], np.cumsum(tiles)])
+    starts, counts = [], []
+    for i, e in enumerate(local):
+        base = pad[rank * EL:e].sum()
+        for j in range(int(tiles[i])):
+            starts.append(base + j * block_m)
+            counts.append(min(block_m, tot[e] - j * block_m))
+    return dict(dest_base=dest_base.astype(np.int32), tile_row_start=np.array(starts, np.int64),
+                tile_row_count=np.array(counts, np.int64), tile_cumsum=tcum.astype(np.int32),
+                total_rows=int(pad[local].sum()))

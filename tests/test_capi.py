@@ -42,8 +42,10 @@ def test_version_and_pure_host_queries():
      "unsupported dtype"),
     (lambda L: L.moe_gemm1_swiglu(None, _lib.BF16, 1, 12, None, 1, 64, None, None, None, 1, None, _lib.BF16, None),
      "multiple of 16 bytes"),
-    (lambda L: L.moe_gemm2(None, _lib.BF16, 1, 64, None, 1, 64, None, None, ctypes.c_void_p(16), 1, 7, None, None,
+    (lambda L: L.moe_gemm2(None, _lib.BF16, 1, 64, None, 1, 64, None, None, ctypes.c_void_p(16), 1, 0, None, None,
                            1, None, _lib.BF16, 1, None), "NULL pointer"),
+    (lambda L: L.moe_gemm2(None, _lib.BF16, 1, 64, None, 1, 64, None, None, ctypes.c_void_p(16), 1, 7, None, None,
+                           1, ctypes.c_void_p(16), _lib.BF16, 1, None), "bad epilogue"),
     (lambda L: L.moe_align(None, 4, 2, 0, 128, None, None, None, None, None, None, 0, None), "num_experts"),
     (lambda L: L.moe_tile_schedule(None, _lib.I64, 4, 10, 128, None, None, None, None, None), "NULL"),
     (lambda L: L.moe_fused_mlp(None, _lib.I8, 10, 64, None, None, 2, 64, None, _lib.I64, 128, None, None, 0, None),

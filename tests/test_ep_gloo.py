@@ -39,13 +39,16 @@ class OracleOps:
         y = O.moe_mlp_topk(x_rows.numpy(), w13.numpy(), w2.numpy(), np.ones_like(ids, np.float32), ids)
         return torch.from_numpy(y)
 
-    def combine(self, o_back, slot_pos, topk_weights, out_dtype):
+    def combine(self, o_back, slot_pos, topk_weights, out_dtype, out=None):
         T, k = topk_weights.shape
         y = torch.zeros((T, o_back.shape[1]), dtype=torch.float32)
         pos = slot_pos.view(T, k).to(torch.int64)
         for j in range(k):
             m = pos[:, j] >= 0
             y[m] += topk_weights[m, j:j + 1] * o_back[pos[m, j]]
+        if out is not None:
+            out.copy_(y)
+            return out
         return y.to(out_dtype)
 
 
@@ -55,7 +58,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, E, T, H, I, k, drop, result_q):
+def _worker(rank, world, port, E, T, H, I, k, drop, chunks, result_q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
@@ -70,7 +73,8 @@ def _worker(rank, world, port, E, T, H, I, k, drop, result_q):
             ids[::4, 0] = -1
         el = E // world
         layer = ExpertParallelMoE(torch.from_numpy(w13[rank * el:(rank + 1) * el]),
-                                  torch.from_numpy(w2[rank * el:(rank + 1) * el]), E, ops=OracleOps())
+                                  torch.from_numpy(w2[rank * el:(rank + 1) * el]), E, ops=OracleOps(),
+                                  chunks=chunks, min_chunk_tokens=8)
         y = layer(torch.from_numpy(x), torch.from_numpy(wts), torch.from_numpy(ids))
         ref = O.moe_mlp_topk(x, w13, w2, wts, ids)
         result_q.put((rank, float(np.abs(y.numpy() - ref).max()), float(np.abs(ref).max())))
@@ -78,13 +82,14 @@ def _worker(rank, world, port, E, T, H, I, k, drop, result_q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("E,T,k,drop", [(8, 40, 2, False), (4, 33, 3, True), (6, 1, 2, False)])
-def test_expert_parallel_two_ranks_matches_oracle(E, T, k, drop):
+@pytest.mark.parametrize("E,T,k,drop,chunks", [(8, 40, 2, False, 1), (4, 33, 3, True, 3), (6, 1, 2, False, 2),
+                                                (8, 64, 2, True, 2)])
+def test_expert_parallel_two_ranks_matches_oracle(E, T, k, drop, chunks):
     world = 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, E, T, 32, 24, k, drop, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, E, T, 32, 24, k, drop, chunks, q)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:

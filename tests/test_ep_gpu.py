@@ -18,7 +18,7 @@ def _port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, cfg, q):
+def _worker(rank, world, port, cfg, transport, q):
     import torch.distributed as dist
     from datetime import timedelta
 
@@ -45,8 +45,20 @@ def _worker(rank, world, port, cfg, q):
         ids_t, wts_t = torch.from_numpy(ids).to(dev), torch.from_numpy(wts).to(dev)
         el = E // world
         lsc = None if scales is None else tuple(s[rank * el:(rank + 1) * el] for s in scales)
-        layer = ExpertParallelMoE(w13[rank * el:(rank + 1) * el], w2[rank * el:(rank + 1) * el], E, scales=lsc)
+        if transport == "peer":
+            from mail_b200.ep import PeerExpertParallelMoE
+            layer = PeerExpertParallelMoE(w13[rank * el:(rank + 1) * el], w2[rank * el:(rank + 1) * el], E,
+                                          max_tokens=T, top_k=k, scales=lsc)
+        else:
+            layer = ExpertParallelMoE(w13[rank * el:(rank + 1) * el], w2[rank * el:(rank + 1) * el], E,
+                                      scales=lsc, chunks=2, min_chunk_tokens=128)
         y = layer(x, wts_t, ids_t)
+        y_again = layer(x, wts_t, ids_t)  # the second call reuses the buffers
+        torch.cuda.synchronize()
+        assert torch.equal(y, y_again)
+        if transport == "peer":
+            assert not layer.overflowed()
+            layer.close()
         y_ref = mb.fused_moe_mlp(x, w13, w2, wts_t, ids_t, scales=scales)
         torch.cuda.synchronize()
         err = float((y.float() - y_ref.float()).abs().max() / y_ref.float().abs().max())
@@ -57,13 +69,14 @@ def _worker(rank, world, port, cfg, q):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("transport", ["peer", "nccl"])
 @pytest.mark.parametrize("cfg", [(512, 1024, 512, 8, 2, False), (300, 1024, 256, 16, 4, True)])
-def test_expert_parallel_matches_single_gpu(cfg):
+def test_expert_parallel_matches_single_gpu(cfg, transport):
     world = 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    ps = [ctx.Process(target=_worker, args=(r, world, port, cfg, q)) for r in range(world)]
+    ps = [ctx.Process(target=_worker, args=(r, world, port, cfg, transport, q)) for r in range(world)]
     for p in ps:
         p.start()
     for p in ps:
