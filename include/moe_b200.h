@@ -195,7 +195,8 @@ MOE_API int moe_quant_rows(const void* src, int src_dtype, int64_t rows, int64_t
  * w13_scale[e, n]) is applied to g and u before the SwiGLU. h is written in
  * h_dtype (the reference's weight dtype; bf16 for int8 inputs).
  * a: [a_rows, H]; w13: [E, 2I, H]; h: [a_rows, I]. dtypes: BF16, F16, F32
- * (tf32 tensor cores), I8 (a and w13 both int8, scales required).
+ * (tf32 tensor cores), I8 (a and w13 both int8, scales required). Up to
+ * 1024 experts.
  * -------------------------------------------------------------------------- */
 MOE_API int moe_gemm1_swiglu(const void* a, int dtype, int64_t a_rows, int64_t hidden, const void* w13,
                      int num_experts, int64_t inter, const float* a_scale, const float* w13_scale,
