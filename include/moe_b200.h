@@ -77,8 +77,13 @@ MOE_API int moe_version(void);
 /* Message of the last failing call on this host thread ("" if none). */
 MOE_API const char* moe_last_error(void);
 /* Copies the device error flag (0 = none, else a code identifying the stalled
- * pipeline role) into *host_code and clears it. Synchronises `stream`. */
+ * pipeline role: 1 TMA producer, 2 MMA issuer, 3 epilogue, 4 drain,
+ * 6 self-test) into *host_code and clears it. Synchronises `stream`. */
 MOE_API int moe_get_device_error(int* host_code, void* stream);
+/* Self-test of the bounded waits: one CTA waits on an mbarrier that nothing
+ * completes; the wait gives up after timeout_ns (at most 2 s), the kernel
+ * latches device error 6 and returns, and the context stays usable. */
+MOE_API int moe_selftest_wait_timeout(uint64_t timeout_ns, void* stream);
 
 /* Process-wide tuning options (moe_set_option / moe_get_option). */
 typedef enum {
@@ -129,6 +134,20 @@ MOE_API int64_t moe_tile_table_ints(int num_experts, int64_t max_tiles);
 MOE_API int moe_tile_schedule(const void* group_sizes, int gs_dtype, int num_experts, int64_t num_tokens, int block_m,
                       int64_t* tile_expert, int64_t* tile_row_start, int64_t* tile_row_count,
                       int32_t* tile_table, void* stream);
+
+/* --------------------------------------------------------------------------
+ * Router (no reference counterpart: the reference's callers route with an
+ * external op). logits [T, E] (fp32/bf16/fp16) -> topk_ids [T, k] int32 and
+ * topk_weights [T, k] fp32. The k largest logits win, in descending order,
+ * ties to the lower expert id (softmax and sigmoid are monotonic, so these
+ * are the top-k scores). Weights: softmax: exp(l - max) / sum over all
+ * experts, or over the k chosen when renormalize != 0; sigmoid:
+ * 1 / (1 + exp(-l)), divided by the sum over the k chosen when renormalize.
+ * E <= 1024, k <= min(E, 32).
+ * -------------------------------------------------------------------------- */
+typedef enum { MOE_SCORE_SOFTMAX = 0, MOE_SCORE_SIGMOID = 1 } moe_scoring_t;
+MOE_API int moe_route_topk(const void* logits, int dtype, int64_t num_tokens, int num_experts, int top_k,
+                           int scoring, int renormalize, int32_t* topk_ids, float* topk_weights, void* stream);
 
 /* --------------------------------------------------------------------------
  * Routing align (no reference counterpart; upstream of fused_moe_mlp, the

@@ -14,11 +14,12 @@ from .moe import (
     prepack_weights,
     quant_int8_rows,
     quantize_weights_int8,
+    route_topk,
     weights_from_linear,
 )
 
 __all__ = [
     "BLOCK_M", "MoeError", "build_tile_schedule", "device_error", "fused_expert_rows", "fused_moe_mlp", "gather_rows", "kmajor",
-    "load_library", "moe_align", "prepack_weights", "quant_int8_rows", "quantize_weights_int8",
+    "load_library", "moe_align", "prepack_weights", "quant_int8_rows", "quantize_weights_int8", "route_topk",
     "weights_from_linear",
 ]

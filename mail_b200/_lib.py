@@ -30,12 +30,14 @@ SIGNATURES = {
     "moe_last_error": (ctypes.c_char_p, []),
     "moe_get_device_error": (_i, [_p, _p]),
     "moe_launch_count": (_i64, []),
+    "moe_selftest_wait_timeout": (_i, [ctypes.c_uint64, _p]),
     "moe_set_option": (_i, [_i, _i]),
     "moe_get_option": (_i, [_i]),
     "moe_set_stage_events": (_i, [_p, _i]),
     "moe_tile_grid": (_i64, [_i64, _i, _i]),
     "moe_tile_table_ints": (_i64, [_i, _i64]),
     "moe_tile_schedule": (_i, [_p, _i, _i, _i64, _i, _p, _p, _p, _p, _p]),
+    "moe_route_topk": (_i, [_p, _i, _i64, _i, _i, _i, _i, _p, _p, _p]),
     "moe_align_capacity": (_i64, [_i64, _i, _i]),
     "moe_align_workspace_size": (_sz, [_i64, _i, _i, _i]),
     "moe_align": (_i, [_p, _i64, _i, _i, _i, _p, _p, _p, _p, _p, _p, _sz, _p]),

@@ -567,6 +567,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   }
 }
 
+// Waits on an mbarrier that nothing ever completes: the bounded wait must give
+// up after timeout_ns and latch error code 6 (self-test of the timeout path).
+__global__ void selftest_wait_kernel(uint64_t timeout_ns) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    ptx::mbar_init(&bar, 1);
+    abort_flag = 0;
+    ptx::fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && !ptx::mbar_wait(&bar, 0, &abort_flag, timeout_ns)) raise_device_error(6);
+}
+
 // ---------------------------------------------------------------- host side
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -842,4 +856,11 @@ extern "C" int moe_set_option(int option, int value) {
 extern "C" int moe_get_option(int option) {
   if (option == MOE_OPT_GEMM_CTA_PAIR) return g_gemm_cta_pair.load();
   return -1;
+}
+
+extern "C" int moe_selftest_wait_timeout(uint64_t timeout_ns, void* stream) {
+  MOE_CHECK_ARG(timeout_ns > 0 && timeout_ns <= 2000000000ull, "moe_selftest_wait_timeout: limit must be in (0, 2 s]");
+  selftest_wait_kernel<<<1, 32, 0, as_stream(stream)>>>(timeout_ns);
+  MOE_LAUNCH_CHECK("selftest_wait_kernel");
+  return MOE_OK;
 }

@@ -210,10 +210,132 @@ __global__ void align_scatter_kernel(const int32_t* __restrict__ ids, int64_t S,
   }
 }
 
+// ---------------------------------------------------------------------------
+// Router: logits [T, E] -> top-k ids and weights, one warp per token. The k
+// largest logits are selected (softmax and sigmoid are monotonic, so this is
+// the top-k of the scores), ties going to the lower expert id; lane l holds
+// experts l, l+32, ... in registers.
+constexpr int kRouteMaxPerLane = 32;  // E <= 1024
+
+template <typename T>
+__device__ __forceinline__ float to_f32(T v) {
+  if constexpr (sizeof(T) == 4) return v;
+  else return static_cast<float>(v);
+}
+
+template <typename T, int PER>
+__global__ void __launch_bounds__(256) route_topk_kernel(const T* __restrict__ logits, int64_t num_tokens, int E,
+                                                         int k, int sigmoid, int renormalize,
+                                                         int32_t* __restrict__ ids, float* __restrict__ wts) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t t = warp; t < num_tokens; t += nwarps) {
+    float v[PER];
+    const T* row = logits + t * E;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      const int e = lane + 32 * i;
+      v[i] = e < E ? to_f32(row[e]) : -INFINITY;
+    }
+    // softmax over all experts needs the maximum and the partition function
+    float m = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) m = fmaxf(m, v[i]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float z = 0.f;
+    if (!sigmoid && !renormalize) {
+#pragma unroll
+      for (int i = 0; i < PER; ++i)
+        if (lane + 32 * i < E) z += expf(v[i] - m);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) z += __shfl_xor_sync(0xffffffffu, z, o);
+    }
+    unsigned taken = 0u;  // bit i: this lane's expert lane + 32 i already chosen
+    float sel_sum = 0.f, my_score = 0.f;
+    int my_j = -1;
+    for (int j = 0; j < k; ++j) {
+      float best = -INFINITY;
+      int bidx = 0x7fffffff;
+#pragma unroll
+      for (int i = 0; i < PER; ++i) {
+        const int e = lane + 32 * i;
+        if (e < E && !(taken >> i & 1u) && (v[i] > best || (v[i] == best && e < bidx))) {
+          best = v[i];
+          bidx = e;
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bidx, o);
+        if (ob > best || (ob == best && oi < bidx)) {
+          best = ob;
+          bidx = oi;
+        }
+      }
+      if ((bidx & 31) == lane) taken |= 1u << (bidx >> 5);
+      const float score = sigmoid ? 1.0f / (1.0f + expf(-best)) : expf(best - m);
+      sel_sum += score;
+      if (lane == j) {
+        my_j = bidx;
+        my_score = score;
+      }
+    }
+    if (lane < k) {
+      float w = my_score;
+      if (renormalize) w = w / sel_sum;
+      else if (!sigmoid) w = w / z;
+      ids[t * k + lane] = my_j;
+      wts[t * k + lane] = w;
+    }
+  }
+}
+
 }  // namespace
 }  // namespace moe
 
 using namespace moe;
+
+extern "C" int moe_route_topk(const void* logits, int dtype, int64_t num_tokens, int num_experts, int top_k,
+                              int scoring, int renormalize, int32_t* topk_ids, float* topk_weights, void* stream) {
+  MOE_CHECK_ARG(num_tokens >= 0 && num_experts > 0 && num_experts <= 32 * kRouteMaxPerLane,
+                "moe_route_topk: num_experts %d outside [1, %d]", num_experts, 32 * kRouteMaxPerLane);
+  MOE_CHECK_ARG(top_k > 0 && top_k <= 32 && top_k <= num_experts, "moe_route_topk: top_k %d outside [1, min(E, 32)]",
+                top_k);
+  MOE_CHECK_ARG(scoring == MOE_SCORE_SOFTMAX || scoring == MOE_SCORE_SIGMOID, "moe_route_topk: bad scoring %d",
+                scoring);
+  if (num_tokens == 0) return MOE_OK;
+  MOE_CHECK_ARG(logits && topk_ids && topk_weights, "moe_route_topk: NULL pointer");
+  int64_t blocks = ceil_div(num_tokens, 8);
+  const int64_t cap = (int64_t)num_sms() * 16;
+  if (blocks > cap) blocks = cap;
+  cudaStream_t st = as_stream(stream);
+  const int sig = scoring == MOE_SCORE_SIGMOID;
+#define ROUTE(TT, PER)                                                                                      \
+  route_topk_kernel<TT, PER><<<(unsigned)blocks, 256, 0, st>>>(static_cast<const TT*>(logits), num_tokens, \
+                                                               num_experts, top_k, sig, renormalize != 0,  \
+                                                               topk_ids, topk_weights)
+#define ROUTE_T(TT)                                        \
+  if (num_experts <= 32) ROUTE(TT, 1);                     \
+  else if (num_experts <= 128) ROUTE(TT, 4);               \
+  else if (num_experts <= 256) ROUTE(TT, 8);               \
+  else ROUTE(TT, kRouteMaxPerLane);
+  if (dtype == MOE_F32) {
+    ROUTE_T(float)
+  } else if (dtype == MOE_BF16) {
+    ROUTE_T(__nv_bfloat16)
+  } else if (dtype == MOE_F16) {
+    ROUTE_T(__half)
+  } else {
+    return set_error(MOE_ERR_UNSUPPORTED, "moe_route_topk: dtype %d not supported", dtype);
+  }
+#undef ROUTE_T
+#undef ROUTE
+  MOE_LAUNCH_CHECK("route_topk_kernel");
+  return MOE_OK;
+}
 
 extern "C" int64_t moe_tile_grid(int64_t num_tokens, int num_experts, int block_m) {
   if (block_m <= 0 || num_tokens < 0 || num_experts <= 0) return -1;

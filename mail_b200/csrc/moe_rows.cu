@@ -140,62 +140,72 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const Tin* __restrict_
   }
 }
 
-// Gather + per-token int8 quantisation with one 128-thread CTA per row: each
-// thread keeps up to kQuantVecs 8-element vectors of the row in registers, so
-// the row is read from memory once with 8 independent 16-byte loads in flight
-// per thread, reduced to its absmax across the CTA, then quantised from
-// registers. Rows up to 128 * 8 * kQuantVecs columns.
+// Gather + per-token int8 quantisation with RT threads per row (a 128-thread
+// CTA handles 128 / RT rows at a time): each thread keeps up to kQuantVecs
+// 8-element vectors of its row in registers, so the row is read once with 8
+// independent 16-byte loads in flight per thread, reduced to its absmax
+// across the RT threads, then quantised from registers. RT is chosen so the
+// threads are full: 32 for rows <= 2048 columns, 64 for <= 4096, else 128
+// (rows up to 8192 columns). A padding row (slot < 0) quantises zeros.
 constexpr int kQuantVecs = 8;
 constexpr int kQuantThreads = 128;
 constexpr int64_t kQuantMaxCols = (int64_t)kQuantThreads * 8 * kQuantVecs;
 
-template <typename Tin>
+template <typename Tin, int RT>
 __global__ void __launch_bounds__(kQuantThreads) gather_quant_kernel(const Tin* __restrict__ src, int64_t cols,
                                                                      const int32_t* __restrict__ slots, int top_k,
                                                                      int64_t rows,
                                                                      const int32_t* __restrict__ rows_dev,
                                                                      int8_t* __restrict__ dst,
                                                                      float* __restrict__ dst_scale) {
+  constexpr int kRowsPerPass = kQuantThreads / RT;
+  constexpr int kWarpsPerRow = RT / 32;
   __shared__ float red[kQuantThreads / 32];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int grp = tid / RT, gt = tid % RT;
   int64_t limit = rows;
   if (rows_dev) limit = min(limit, (int64_t)*rows_dev);
-  for (int64_t p = blockIdx.x; p < limit; p += gridDim.x) {
-    const int64_t slot = slots ? (int64_t)slots[p] : p;
-    int8_t* d = dst + p * cols;
-    if (slot < 0) {
-      for (int64_t c = (int64_t)tid * 8; c < cols; c += kQuantThreads * 8) zero8(d + c);
-      if (tid == 0 && dst_scale) dst_scale[p] = 0.f;
-      continue;
-    }
-    const Tin* s = src + (slot / top_k) * cols;
+  for (int64_t base = (int64_t)blockIdx.x * kRowsPerPass; base < limit; base += (int64_t)gridDim.x * kRowsPerPass) {
+    const int64_t p = base + grp;
+    const bool active = p < limit;
+    const int64_t slot = active ? (slots ? (int64_t)slots[p] : p) : -1;
+    const Tin* s = slot >= 0 ? src + (slot / top_k) * cols : nullptr;
     float v[kQuantVecs][8];
     float amax = 0.f;
 #pragma unroll
     for (int i = 0; i < kQuantVecs; ++i) {
-      const int64_t c = ((int64_t)i * kQuantThreads + tid) * 8;
-      if (c < cols) {
+      const int64_t c = ((int64_t)i * RT + gt) * 8;
+      if (s && c < cols) {
         load8(s + c, v[i]);
 #pragma unroll
         for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(v[i][j]));
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[i][j] = 0.f;
       }
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    if (lane == 0) red[warp] = amax;
-    __syncthreads();
-    amax = red[0];
+    if constexpr (kWarpsPerRow > 1) {
+      if (lane == 0) red[warp] = amax;
+      __syncthreads();
+      const int w0 = grp * kWarpsPerRow;
+      amax = red[w0];
 #pragma unroll
-    for (int w = 1; w < kQuantThreads / 32; ++w) amax = fmaxf(amax, red[w]);
-    __syncthreads();
+      for (int w = 1; w < kWarpsPerRow; ++w) amax = fmaxf(amax, red[w0 + w]);
+      __syncthreads();
+    }
     float scale, inv;
     row_scales(amax, scale, inv);
+    if (active) {
+      int8_t* d = dst + p * cols;
 #pragma unroll
-    for (int i = 0; i < kQuantVecs; ++i) {
-      const int64_t c = ((int64_t)i * kQuantThreads + tid) * 8;
-      if (c < cols) *reinterpret_cast<uint2*>(d + c) = quant8(v[i], inv);
+      for (int i = 0; i < kQuantVecs; ++i) {
+        const int64_t c = ((int64_t)i * RT + gt) * 8;
+        if (c < cols) *reinterpret_cast<uint2*>(d + c) = quant8(v[i], inv);
+      }
+      if (gt == 0 && dst_scale) dst_scale[p] = scale;
     }
-    if (tid == 0 && dst_scale) dst_scale[p] = scale;
   }
 }
 
@@ -269,17 +279,28 @@ extern "C" int moe_gather_rows(const void* src, int src_dtype, int64_t cols, con
   } else if (dst_dtype == MOE_I8) {
     MOE_CHECK_ARG(dst_scale != nullptr, "moe_gather_rows: int8 output needs dst_scale");
     if (cols <= kQuantMaxCols) {
-      int64_t blocks = rows;
+      const int rt = cols <= 2048 ? 32 : (cols <= 4096 ? 64 : 128);
+      int64_t blocks = ceil_div(rows, kQuantThreads / rt);
       const int64_t cap = (int64_t)num_sms() * 16;
       if (blocks > cap) blocks = cap;
-#define GATHER_Q(TI)                                                                                          \
-  gather_quant_kernel<TI><<<(unsigned)blocks, kQuantThreads, 0, st>>>(static_cast<const TI*>(src), cols,     \
-                                                                     sorted_slots, top_k, rows, rows_dev,   \
-                                                                     static_cast<int8_t*>(dst), dst_scale)
-      if (src_dtype == MOE_BF16) GATHER_Q(__nv_bfloat16);
-      else if (src_dtype == MOE_F16) GATHER_Q(__half);
-      else if (src_dtype == MOE_F32) GATHER_Q(float);
-      else return set_error(MOE_ERR_UNSUPPORTED, "moe_gather_rows: dtype %d not supported", src_dtype);
+#define GATHER_Q(TI, RT)                                                                                        \
+  gather_quant_kernel<TI, RT><<<(unsigned)blocks, kQuantThreads, 0, st>>>(static_cast<const TI*>(src), cols,   \
+                                                                         sorted_slots, top_k, rows, rows_dev, \
+                                                                         static_cast<int8_t*>(dst), dst_scale)
+#define GATHER_QT(TI)           \
+  if (rt == 32) GATHER_Q(TI, 32); \
+  else if (rt == 64) GATHER_Q(TI, 64); \
+  else GATHER_Q(TI, 128);
+      if (src_dtype == MOE_BF16) {
+        GATHER_QT(__nv_bfloat16)
+      } else if (src_dtype == MOE_F16) {
+        GATHER_QT(__half)
+      } else if (src_dtype == MOE_F32) {
+        GATHER_QT(float)
+      } else {
+        return set_error(MOE_ERR_UNSUPPORTED, "moe_gather_rows: dtype %d not supported", src_dtype);
+      }
+#undef GATHER_QT
 #undef GATHER_Q
       MOE_LAUNCH_CHECK("gather_quant_kernel");
       return MOE_OK;

@@ -63,9 +63,11 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t addr, uint32_t parity) {
   return ok != 0;
 }
 
-// Wait until the phase with the given parity has completed. Returns false on
-// timeout or when *abort is raised by another role of the same CTA.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
+// Wait until the phase with the given parity has completed. Returns false
+// after timeout_ns of global time or when *abort is raised by another role of
+// the same CTA.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                          uint64_t timeout_ns = MOE_WAIT_TIMEOUT_NS) {
   const uint32_t addr = smem_u32(bar);
   if (mbar_try_wait(addr, parity)) return true;
   const uint64_t t0 = globaltimer();
@@ -74,7 +76,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
     for (int i = 0; i < 32; ++i)
       if (mbar_try_wait(addr, parity)) return true;
     if (*abort) return false;
-    if (globaltimer() - t0 > MOE_WAIT_TIMEOUT_NS) return false;
+    if (globaltimer() - t0 > timeout_ns) return false;
   }
 }
 

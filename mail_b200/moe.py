@@ -111,6 +111,21 @@ def build_tile_schedule(group_sizes: torch.Tensor, num_tokens: int, BLOCK_M: int
     return te, ts, tc, grid
 
 
+def route_topk(logits: torch.Tensor, top_k: int, scoring: str = "softmax", renormalize: bool = True):
+    """Router on the GPU: logits [T, E] -> (topk_ids int32 [T, k],
+    topk_weights fp32 [T, k]); the k largest logits, ties to the lower expert
+    id; softmax or sigmoid weights, optionally renormalised over the k."""
+    _require_cuda(logits)
+    lg = logits.contiguous()
+    T, E = lg.shape
+    ids = torch.empty((T, top_k), dtype=torch.int32, device=lg.device)
+    w = torch.empty((T, top_k), dtype=torch.float32, device=lg.device)
+    sc = {"softmax": 0, "sigmoid": 1}[scoring]
+    _lib.call("moe_route_topk", lg.data_ptr(), _code(lg), T, E, top_k, sc, int(renormalize), ids.data_ptr(),
+              w.data_ptr(), _stream(lg.device))
+    return ids, w
+
+
 def moe_align(topk_ids: torch.Tensor, num_experts: int, block_m: int = BLOCK_M) -> dict:
     """Stable block-padded sort of the T*k slots by expert (see moe_b200.h).
 

@@ -107,24 +107,27 @@ def moe_mlp_grouped(x, w13, w2, group_sizes, round_hidden=None):
 def route_topk(logits, top_k: int, scoring: str = "softmax", renormalize: bool = True):
     """logits [T, E] -> (topk_ids int32 [T, k], topk_weights fp32 [T, k]).
 
-    Scores are computed in fp32 (softmax or sigmoid); the k largest scores are
-    chosen with ties broken towards the lower expert id (stable order), and
-    the weights are renormalised by their fp32 sum.
+    The k largest logits are chosen in descending order, ties towards the
+    lower expert id (softmax and sigmoid are monotonic, so these are the
+    top-k scores). Weights in fp32: softmax exp(l - max) / sum over all
+    experts, or over the k chosen when renormalising; sigmoid 1/(1+exp(-l)),
+    divided by the sum over the k chosen when renormalising.
     """
     lg = np.asarray(logits, np.float32)
-    if scoring == "softmax":
-        m = lg.max(axis=1, keepdims=True)
-        p = np.exp(lg - m)
-        p = p / p.sum(axis=1, keepdims=True)
-    elif scoring == "sigmoid":
-        p = np.float32(1.0) / (np.float32(1.0) + np.exp(-lg))
-    else:
-        raise ValueError(scoring)
-    p = p.astype(np.float32)
-    order = np.argsort(-p, axis=1, kind="stable")[:, :top_k]
-    w = np.take_along_axis(p, order, axis=1)
-    if renormalize:
-        w = w / w.sum(axis=1, keepdims=True)
+    order = np.argsort(-lg, axis=1, kind="stable")[:, :top_k]
+    top = np.take_along_axis(lg, order, axis=1)
+    with np.errstate(over="ignore"):
+        if scoring == "softmax":
+            m = lg.max(axis=1, keepdims=True)
+            sc = np.exp(top - m).astype(np.float32)
+            den = sc.sum(axis=1, keepdims=True) if renormalize else \
+                np.exp(lg - m).astype(np.float32).sum(axis=1, keepdims=True)
+            w = sc / den
+        elif scoring == "sigmoid":
+            sc = (np.float32(1.0) / (np.float32(1.0) + np.exp(-top))).astype(np.float32)
+            w = sc / sc.sum(axis=1, keepdims=True) if renormalize else sc
+        else:
+            raise ValueError(scoring)
     return order.astype(np.int32), w.astype(np.float32)
 
 

@@ -117,6 +117,26 @@ def test_align_bit_exact(kind, T, k, E):
     np.testing.assert_array_equal(table[5 + E + mt:5 + E + mt + n], ref["tile_row_count"])
 
 
+# --------------------------------------------------------------------------- router
+
+
+@pytest.mark.parametrize("T,E,k,scoring,renorm,dtype", [
+    (64, 8, 2, "softmax", True, torch.float32), (4096, 8, 2, "softmax", True, torch.bfloat16),
+    (777, 128, 8, "softmax", False, torch.float32), (300, 256, 8, "sigmoid", True, torch.float32),
+    (5, 64, 6, "sigmoid", False, torch.float16), (33, 1000, 4, "softmax", True, torch.float32),
+])
+def test_route_topk_matches_oracle(T, E, k, scoring, renorm, dtype):
+    rng = np.random.default_rng(E + k)
+    lg = rng.standard_normal((T, E), dtype=np.float32)
+    lg[0, :] = 0.25          # all tied: lowest ids win
+    lg[1, 3] = lg[1, 5] = 9  # a tie at the top
+    lt = torch.from_numpy(lg).to(dev(), dtype)
+    ids, w = mb.route_topk(lt, k, scoring, renorm)
+    ids_ref, w_ref = O.route_topk(npf(lt), k, scoring, renorm)
+    np.testing.assert_array_equal(ids.cpu().numpy(), ids_ref)
+    np.testing.assert_allclose(w.cpu().numpy(), w_ref, rtol=2e-6, atol=1e-7)
+
+
 # --------------------------------------------------------------------------- quant / gather
 
 
@@ -350,3 +370,17 @@ def test_launch_counter_counts_kernels():
     run_topk(x, w13, w2, ids, wts)
     # align (4) + gather + gemm1 + gemm2 + convert
     assert lib.moe_launch_count() - before == 8
+
+
+def test_bounded_wait_expires_and_context_survives():
+    """A pipeline wait that nothing satisfies gives up after its limit and
+    reports through the device error flag; the GPU context stays usable."""
+    assert mb.device_error(dev()) == 0
+    _lib.call("moe_selftest_wait_timeout", 200_000_000, torch.cuda.current_stream().cuda_stream)  # 0.2 s
+    assert mb.device_error(dev()) == 6
+    assert mb.device_error(dev()) == 0  # reading clears it
+    x, w13, w2, ids, wts = topk_case(64, 256, 128, 4, 2, "uniform-softmax", torch.bfloat16)
+    y = run_topk(x, w13, w2, ids, wts)
+    ref = O.moe_mlp_topk(npf(x), npf(w13), npf(w2), wts, ids, round_hidden=O.round_bf16)
+    assert max_abs_rel(npf(y), ref) < TOL
+    assert_no_device_error()
