@@ -211,6 +211,115 @@ __global__ void align_scatter_kernel(const int32_t* __restrict__ ids, int64_t S,
 }
 
 // ---------------------------------------------------------------------------
+// Align in one CTA for small batches (S <= kAlignSmallSlots): the 32 warps
+// play the chunks of the multi-kernel version — per-warp histograms, a scan
+// of each expert column over the warps, the padded expert scan and tile
+// table, then the stable scatter — all in shared memory, one launch.
+constexpr int kAlignSmallSlots = 16384;
+
+__global__ void __launch_bounds__(kScanThreads) align_small_kernel(
+    const int32_t* __restrict__ ids, int64_t S, int E, int BM, int64_t max_tiles, int32_t* __restrict__ sorted_slots,
+    int32_t* __restrict__ slot_pos, int32_t* __restrict__ group_sizes, int32_t* __restrict__ padded_offsets,
+    int32_t* __restrict__ table) {
+  extern __shared__ int32_t sm[];
+  constexpr int W = kScanThreads / 32;
+  const int E1 = E + 1;
+  int32_t* hist = sm;                // [W][E+1]: counts, then per-warp bases, then running positions
+  int32_t* tot = sm + W * E1;        // [E+1] slots per expert (E: dropped)
+  int32_t* poff = tot + E1;          // [E+1] padded offsets (exclusive)
+  int32_t* tcum = poff + E1;         // [E+1] tile prefix (exclusive)
+  __shared__ int32_t warp_sums[32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int i = threadIdx.x; i < W * E1; i += blockDim.x) hist[i] = 0;
+  __syncthreads();
+  const int64_t per = ((S + W - 1) / W + 31) / 32 * 32;  // slots per warp, whole rounds
+  const int64_t lo = min(S, (int64_t)warp * per), hi = min(S, lo + per);
+  int32_t* h = hist + warp * E1;
+  for (int64_t b = lo; b < hi; b += 32) {
+    const int64_t sl = b + lane;
+    int key = -1;
+    if (sl < hi) {
+      const int id = ids[sl];
+      key = (id >= 0 && id < E) ? id : E;
+    }
+    const unsigned m = __match_any_sync(0xffffffffu, key);
+    if (key >= 0 && lane == __ffs(m) - 1) h[key] += __popc(m);
+    __syncwarp();
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < E1; e += blockDim.x) {  // exclusive scan of each column over the warps
+    int run = 0;
+    for (int w = 0; w < W; ++w) {
+      const int v = hist[w * E1 + e];
+      hist[w * E1 + e] = run;
+      run += v;
+    }
+    tot[e] = run;
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    const int t = (tot[e] + BM - 1) / BM;
+    poff[e + 1] = t * BM;
+    tcum[e + 1] = t;
+    group_sizes[e] = tot[e];
+  }
+  if (threadIdx.x == 0) {
+    poff[0] = 0;
+    tcum[0] = 0;
+  }
+  __syncthreads();
+  smem_inclusive_scan<int32_t>(poff + 1, E, warp_sums);
+  smem_inclusive_scan<int32_t>(tcum + 1, E, warp_sums);
+  const int32_t ntiles = tcum[E];
+  for (int e = threadIdx.x; e <= E; e += blockDim.x) {
+    padded_offsets[e] = poff[e];
+    table[TileTable::cum_off() + e] = tcum[e];
+  }
+  if (threadIdx.x == 0) {
+    table[0] = ntiles;
+    table[1] = poff[E];
+    table[2] = tot[E];
+    table[3] = 0;
+  }
+  for (int i = threadIdx.x; i < ntiles && i < max_tiles; i += blockDim.x) {
+    int a = 0, z = E - 1;
+    while (a < z) {
+      const int mid = (a + z + 1) >> 1;
+      if (tcum[mid] <= i) a = mid;
+      else z = mid - 1;
+    }
+    const int j = i - tcum[a];
+    const int32_t start = poff[a] + j * BM;
+    const int32_t cnt = min(BM, tot[a] - j * BM);
+    table[TileTable::start_off(E) + i] = start;
+    table[TileTable::count_off(E, max_tiles) + i] = cnt;
+    for (int r = cnt; r < BM; ++r) sorted_slots[start + r] = -1;
+  }
+  for (int e = lane; e < E; e += 32) h[e] += poff[e];  // this warp's first padded row per expert
+  __syncwarp();
+  const unsigned lt_mask = (1u << lane) - 1u;
+  for (int64_t b = lo; b < hi; b += 32) {
+    const int64_t sl = b + lane;
+    int key = -1;
+    if (sl < hi) {
+      const int id = ids[sl];
+      key = (id >= 0 && id < E) ? id : E;
+    }
+    const unsigned m = __match_any_sync(0xffffffffu, key);
+    if (key >= 0 && key < E) {
+      const int32_t pos = h[key] + __popc(m & lt_mask);
+      sorted_slots[pos] = (int32_t)sl;
+      slot_pos[sl] = pos;
+    } else if (key == E) {
+      slot_pos[sl] = -1;
+    }
+    __syncwarp();
+    if (key >= 0 && key < E && lane == __ffs(m) - 1) h[key] += __popc(m);
+    __syncwarp();
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Router: logits [T, E] -> top-k ids and weights, one warp per token. The k
 // largest logits are selected (softmax and sigmoid are monotonic, so this is
 // the top-k of the scores), ties going to the lower expert id; lane l holds
@@ -411,6 +520,17 @@ extern "C" int moe_align(const int32_t* topk_ids, int64_t num_tokens, int top_k,
   const AlignWs w = align_ws(S, num_experts);
   if (workspace_bytes < w.bytes || (w.bytes && !workspace))
     return set_error(MOE_ERR_WORKSPACE, "moe_align: workspace %zu < %zu bytes", workspace_bytes, w.bytes);
+  if (S <= kAlignSmallSlots && num_experts <= 1024) {
+    const int64_t max_tiles_s = moe_align_capacity(S, num_experts, block_m) / block_m;
+    const size_t smem = ((size_t)(kScanThreads / 32) + 3) * (num_experts + 1) * sizeof(int32_t);
+    if (smem > 48 * 1024)
+      MOE_CUDA_TRY(cudaFuncSetAttribute(align_small_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    align_small_kernel<<<1, kScanThreads, smem, as_stream(stream)>>>(topk_ids, S, num_experts, block_m, max_tiles_s,
+                                                                     sorted_slots, slot_pos, group_sizes,
+                                                                     padded_offsets, tile_table);
+    MOE_LAUNCH_CHECK("align_small_kernel");
+    return MOE_OK;
+  }
   char* ws = static_cast<char*>(workspace);
   int32_t* hist = reinterpret_cast<int32_t*>(ws + w.hist_off);
   int32_t* base = reinterpret_cast<int32_t*>(ws + w.base_off);

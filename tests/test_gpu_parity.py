@@ -368,8 +368,8 @@ def test_launch_counter_counts_kernels():
     lib = _lib.load()
     before = lib.moe_launch_count()
     run_topk(x, w13, w2, ids, wts)
-    # align (4) + gather + gemm1 + gemm2 + convert
-    assert lib.moe_launch_count() - before == 8
+    # align (one kernel for up to 16384 slots) + gather + gemm1 + gemm2 + convert
+    assert lib.moe_launch_count() - before == 5
 
 
 def test_bounded_wait_expires_and_context_survives():
