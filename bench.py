@@ -4,7 +4,9 @@ Workload (default, N=1): the Mixtral-8x7B-shaped MoE layer — T=4096 tokens,
 H=4096, I=14336, E=8 experts, top-2, bf16, uniform softmax routing of
 N(0,1) logits, activations N(0,1), weights N(0,0.02) (seeded synthetic data).
 One step = one call of the top-k fused_moe_mlp (align -> gather -> gate_up
-GEMM + SwiGLU -> down GEMM + weighted combine -> bf16) over the resident batch.
+GEMM + SwiGLU -> down GEMM + weighted combine -> bf16) over the resident batch,
+replayed from a CUDA graph captured once (the same kernels; --eager calls the
+op directly every step).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config NAME]
 
@@ -246,9 +248,12 @@ def main():
                          "or NCCL all-to-all")
     ap.add_argument("--gemm", default="auto", choices=["auto", "pair", "single"],
                     help="grouped GEMM variant: CTA pairs (cta_group::2), one CTA per tile, or chosen by size")
+    ap.add_argument("--eager", action="store_true",
+                    help="N=1: call the op directly each step instead of replaying it from a captured CUDA graph")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    args.graph = not args.eager
     cfg = dict(CONFIGS[args.config])
     if args.tokens:
         cfg["T"] = args.tokens
@@ -262,7 +267,7 @@ def main():
     config_json = {"workload": cfg["desc"], "tokens_per_gpu": T, "hidden": H, "inter": I, "experts": E,
                    "top_k": k, "routing": cfg["routing"], "dtype": cfg["dtype"] + ("+w8a8" if cfg["quant"] else ""),
                    "parallelism": f"ep{world}" if world > 1 else "single", "gemm": args.gemm,
-                   "ep_exchange": args.ep if world > 1 else None,
+                   "ep_exchange": args.ep if world > 1 else None, "cuda_graph": bool(args.graph and world == 1),
                    "l2": "weights (%.2f GB) exceed the 126 MB L2, streamed every step" %
                          (E * 3 * H * I * (1 if cfg["quant"] else (4 if cfg["dtype"] == "fp32" else 2)) / 1e9)}
 
@@ -310,9 +315,14 @@ def main():
             return layer(xx, ww, ii)
     else:
         w13, w2, scales = make_weights(cfg, list(range(E)), device, dt)
+        if args.graph:
+            captured = mb.CapturedMoeMLP(w13, w2, T, k, dtype=dt, scales=scales)
 
-        def step(xx, ii, ww):
-            return mb.fused_moe_mlp(xx, w13, w2, ww, ii, scales=scales)
+            def step(xx, ii, ww):
+                return captured(xx, ww, ii)
+        else:
+            def step(xx, ii, ww):
+                return mb.fused_moe_mlp(xx, w13, w2, ww, ii, scales=scales)
 
     stream = torch.cuda.current_stream(device)
 
@@ -343,7 +353,8 @@ def main():
     launches0 = lib.moe_launch_count()
     handles[0].record(stream)
     for i in range(args.steps):
-        lib.moe_set_stage_events(ev_arrays[i], STAGES)
+        if not args.graph:
+            lib.moe_set_stage_events(ev_arrays[i], STAGES)
         step(x, ids, wts)
     lib.moe_set_stage_events(None, 0)
     handles[1].record(stream)
@@ -352,6 +363,15 @@ def main():
     clocks = sampler.stop()
     launches = lib.moe_launch_count() - launches0
     ms = handles[0].elapsed_time(handles[1]) / args.steps
+    if args.graph:
+        # replays launch the captured kernels without going through the
+        # library; stage times come from an eager pass of the same op
+        launches = captured.kernels * args.steps
+        for i in range(args.steps):
+            lib.moe_set_stage_events(ev_arrays[i], STAGES)
+            mb.fused_moe_mlp(x, w13, w2, wts, ids, scales=scales)
+        lib.moe_set_stage_events(None, 0)
+        torch.cuda.synchronize()
 
     def stage_ms(a, b):
         return statistics.mean(row[a].elapsed_time(row[b]) for row in ev)

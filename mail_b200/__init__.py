@@ -4,6 +4,7 @@ include/moe_b200.h); this package is the thin PyTorch-facing host side."""
 from ._lib import MoeError, load as load_library
 from .moe import (
     BLOCK_M,
+    CapturedMoeMLP,
     build_tile_schedule,
     device_error,
     fused_expert_rows,
@@ -19,7 +20,7 @@ from .moe import (
 )
 
 __all__ = [
-    "BLOCK_M", "MoeError", "build_tile_schedule", "device_error", "fused_expert_rows", "fused_moe_mlp", "gather_rows", "kmajor",
+    "BLOCK_M", "CapturedMoeMLP", "MoeError", "build_tile_schedule", "device_error", "fused_expert_rows", "fused_moe_mlp", "gather_rows", "kmajor",
     "load_library", "moe_align", "prepack_weights", "quant_int8_rows", "quantize_weights_int8", "route_topk",
     "weights_from_linear",
 ]

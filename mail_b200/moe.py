@@ -296,6 +296,41 @@ def fused_expert_rows(x: torch.Tensor, w13: torch.Tensor, w2: torch.Tensor, expe
     return out
 
 
+class CapturedMoeMLP:
+    """The top-k fused_moe_mlp for one batch shape, captured in a CUDA graph.
+
+    At decode sizes launching the op's kernels costs about as much as running
+    them; a replay launches the whole captured sequence at once. Inputs are
+    copied into static buffers and every replay writes the same output
+    tensor (copy it if it must outlive the next call).
+    """
+
+    def __init__(self, w13: torch.Tensor, w2: torch.Tensor, num_tokens: int, top_k: int, dtype=torch.bfloat16,
+                 scales=None):
+        dev = w13.device
+        H = w13.shape[1]
+        self.x = torch.zeros((num_tokens, H), dtype=dtype, device=dev)
+        self.ids = torch.zeros((num_tokens, top_k), dtype=torch.int32, device=dev)
+        self.w = torch.zeros((num_tokens, top_k), dtype=torch.float32, device=dev)
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):  # first call outside the capture (kernel attributes, caches)
+            fused_moe_mlp(self.x, w13, w2, self.w, self.ids, scales=scales)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        self.graph = torch.cuda.CUDAGraph()
+        before = _lib.load().moe_launch_count()
+        with torch.cuda.graph(self.graph):
+            self.y = fused_moe_mlp(self.x, w13, w2, self.w, self.ids, scales=scales)
+        self.kernels = int(_lib.load().moe_launch_count() - before)  # library kernels per replay
+
+    def __call__(self, x: torch.Tensor, topk_weights: torch.Tensor, topk_ids: torch.Tensor) -> torch.Tensor:
+        self.x.copy_(x)
+        self.w.copy_(topk_weights)
+        self.ids.copy_(topk_ids)
+        self.graph.replay()
+        return self.y
+
+
 def device_error(device=None) -> int:
     """Reads and clears the kernels' device error flag (synchronises)."""
     import ctypes
