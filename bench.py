@@ -36,6 +36,9 @@ CONFIGS = {
                     desc="Mixtral-8x7B MoE layer"),
     "tiny": dict(T=64, H=1024, I=512, E=8, k=2, routing="uniform-softmax", dtype="fp32", quant=False,
                  desc="tiny fp32 MoE MLP"),
+    "mixtral-prerouted": dict(T=4096, H=4096, I=14336, E=8, k=2, routing="uniform-softmax", dtype="bf16",
+                              quant=False, prerouted=True,
+                              desc="Mixtral-8x7B MoE layer, reference form: pre-grouped rows + group sizes"),
     "qwen3-decode": dict(T=256, H=2048, I=768, E=128, k=8, routing="zipf1.2", dtype="bf16", quant=False,
                          desc="Qwen3-30B-A3B decode (T=256)"),
     "dsv3-w8a8": dict(T=8192, H=7168, I=2048, E=256, k=8, routing="sigmoid", dtype="bf16", quant=True,
@@ -313,6 +316,17 @@ def main():
 
         def step(xx, ii, ww):
             return layer(xx, ww, ii)
+    elif cfg.get("prerouted"):
+        # the reference's call: rows already grouped by expert (T*k of them),
+        # group sizes per expert (fused_moe_mlp_triton.py:121, unquant_diff.txt:13-18)
+        w13, w2, scales = make_weights(cfg, list(range(E)), device, dt)
+        args.graph = False
+        order = torch.argsort(ids.reshape(-1).to(torch.int64), stable=True)
+        x = x[order // k].contiguous()  # the step's input: T * k grouped rows
+        group_sizes = torch.bincount(ids.reshape(-1).to(torch.int64), minlength=E)
+
+        def step(xx, ii, ww):
+            return mb.fused_moe_mlp(xx, w13, w2, group_sizes)
     else:
         w13, w2, scales = make_weights(cfg, list(range(E)), device, dt)
         if args.graph:
@@ -392,7 +406,8 @@ def main():
     ids_h = ids.cpu().pin_memory()
     wts_h = wts.cpu().pin_memory()
     NB = 2
-    y_h = [torch.empty((T, H), dtype=dt).pin_memory() for _ in range(NB)]
+    out_shape = tuple(step(x, ids, wts).shape)
+    y_h = [torch.empty(out_shape, dtype=dt).pin_memory() for _ in range(NB)]
     x_d = [torch.empty_like(x) for _ in range(NB)]
     ids_d = [torch.empty_like(ids) for _ in range(NB)]
     wts_d = [torch.empty_like(wts) for _ in range(NB)]
@@ -444,18 +459,37 @@ def main():
     S_local = int(T * k)  # slots per rank (uniform routing keeps the per-rank load ~ T*k)
     flops_gemm1 = 2.0 * S_local * H * 2 * I
     gemm1_s = st_ms["gemm1"] / 1e3
+    # algorithmic bytes of one gate_up launch: the weights of the experts that
+    # received slots, the padded activation rows read, the h rows written
+    wb = 1 if cfg["quant"] else (4 if cfg["dtype"] == "fp32" else 2)
+    hb = 4 if cfg["dtype"] == "fp32" else 2
+    if world == 1:
+        counts = np.bincount(ids.cpu().numpy().reshape(-1), minlength=E)
+        active = int((counts > 0).sum())
+        rows_pad = int(((counts + 127) // 128 * 128).sum())
+    else:  # the rank's local experts, balanced routing
+        active = E // world
+        rows_pad = S_local + active * 64
+    bytes_gemm1 = active * 2.0 * I * H * wb + rows_pad * H * wb + rows_pad * I * hb
     # a timed region shorter than ~1 s runs at boost clocks (burst peak);
     # longer ones settle under the power cap (sustained peak)
     region_s = ms * args.steps / 1e3
     sustained = region_s >= 1.0
     peak_tc = (peaks["bf16_sus"] if sustained else peaks["bf16"]) * (2.0 if cfg["quant"] else 1.0)
-    roofline = {"kernel": "moe_gemm_kernel<SWIGLU> (gate_up GEMM + SwiGLU)", "bound": "tensor",
-                "achieved": flops_gemm1 / gemm1_s / 1e12, "peak": peak_tc, "unit": "TFLOP/s",
-                "frac": flops_gemm1 / gemm1_s / 1e12 / peak_tc,
-                "peak_source": f"{peaks['source']} bf16 {'sustained' if sustained else 'burst'}"
-                               + (" x2 (int8, spec ratio)" if cfg["quant"] else ""),
-                "traffic": load_traffic(args.config) if not args.tokens else None, "traffic_unit": "bytes",
-                "flops_per_launch": flops_gemm1, "ms_per_launch": st_ms["gemm1"]}
+    tensor_bound = flops_gemm1 / (peak_tc * 1e12) >= bytes_gemm1 / (peaks["hbm"] * 1e9)
+    roofline = {"kernel": "moe_gemm_kernel<SWIGLU> (gate_up GEMM + SwiGLU)",
+                "bound": "tensor" if tensor_bound else "hbm",
+                "flops_per_launch": flops_gemm1, "bytes_per_launch": bytes_gemm1, "active_experts": active,
+                "ms_per_launch": st_ms["gemm1"],
+                "traffic": load_traffic(args.config) if not args.tokens else None, "traffic_unit": "bytes"}
+    if tensor_bound:
+        roofline.update(achieved=flops_gemm1 / gemm1_s / 1e12, peak=peak_tc, unit="TFLOP/s",
+                        frac=flops_gemm1 / gemm1_s / 1e12 / peak_tc,
+                        peak_source=f"{peaks['source']} bf16 {'sustained' if sustained else 'burst'}"
+                                    + (" x2 (int8, spec ratio)" if cfg["quant"] else ""))
+    else:
+        roofline.update(achieved=bytes_gemm1 / gemm1_s / 1e9, peak=peaks["hbm"], unit="GB/s",
+                        frac=bytes_gemm1 / gemm1_s / 1e9 / peaks["hbm"], peak_source=f"{peaks['source']} HBM copy")
     flops_step = 6.0 * S_local * H * I
     value = world * T / (ms / 1e3)
 
