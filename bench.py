@@ -251,6 +251,7 @@ def main():
                          "or NCCL all-to-all")
     ap.add_argument("--gemm", default="auto", choices=["auto", "pair", "single"],
                     help="grouped GEMM variant: CTA pairs (cta_group::2), one CTA per tile, or chosen by size")
+    ap.add_argument("--band", type=int, default=0, help="GEMM tile-order band width in M tiles (0: default)")
     ap.add_argument("--eager", action="store_true",
                     help="N=1: call the op directly each step instead of replaying it from a captured CUDA graph")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -302,6 +303,8 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
     lib = _lib.load()
     lib.moe_set_option(_lib.OPT_GEMM_CTA_PAIR, {"pair": 1, "single": 0, "auto": 2}[args.gemm])
+    if args.band:
+        lib.moe_set_option(_lib.OPT_GEMM_BAND, args.band)
 
     x, ids, wts, dt = make_inputs(cfg, rank, device)
     if world > 1:

@@ -89,7 +89,10 @@ MOE_API int moe_selftest_wait_timeout(uint64_t timeout_ns, void* stream);
 typedef enum {
   MOE_OPT_GEMM_CTA_PAIR = 1 /* 1: grouped GEMMs run one tcgen05 MMA across a pair of CTAs on neighbouring
                                SMs (cta_group::2, 256-row tiles); 0: one CTA per 128-row tile; 2 (default):
-                               pairs when the experts average at least 4 M tiles of 128 rows */
+                               pairs when the experts average at least 4 M tiles of 128 rows */,
+  MOE_OPT_GEMM_BAND = 2     /* M tiles per band of the GEMMs' expert-major tile order (default 16): each
+                               expert's tiles run in bands of this many M tiles, every band swept over
+                               all N tiles, so CTAs running together share weight tiles in L2 */
 } moe_option_t;
 MOE_API int moe_set_option(int option, int value);
 /* Current value of an option, or -1 for an unknown option. */

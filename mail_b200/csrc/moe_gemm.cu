@@ -73,6 +73,7 @@ struct Params {
   int top_k;
   void* const* peer_out;  // kEpiScatterPeer: device array of per-rank output bases
   int num_peers;
+  int band_tiles;         // M tiles per band of the expert-major raster
 };
 
 // Scheduling unit t -> (unit u, n tile, expert e) in expert-major order:
@@ -180,7 +181,6 @@ struct Cfg {
   static constexpr int kBBytes = kBRows * ROW_BYTES;
   static constexpr int kStageBytes = A_BYTES + kBBytes;
   static constexpr uint32_t kTxBytes = PAIR ? 2 * kStageBytes : kStageBytes;  // per stage, whole MMA
-  static constexpr int kGroupUnits = PAIR ? GROUP_M / 2 : GROUP_M;
 };
 
 template <int KIND, bool SWIGLU, bool PAIR>
@@ -271,10 +271,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const int32_t* row_start_tab = p.table + TileTable::start_off(E);
   const int32_t* row_count_tab = p.table + TileTable::count_off(E, p.max_tiles);
 
+  const int group_units = max(1, PAIR ? p.band_tiles / 2 : p.band_tiles);
   // unit t -> (expert e, n tile, this CTA's M tile m, whether m holds rows)
   auto locate = [&](int t, int& e, int& n, int& m, bool& valid) {
     int u;
-    decode_unit(t, s_ucum, E, NT, C::kGroupUnits, u, n, e);
+    decode_unit(t, s_ucum, E, NT, group_units, u, n, e);
     if constexpr (PAIR) {
       m = s_cum[e] + 2 * (u - s_ucum[e]) + (int)rank;
       valid = m < s_cum[e + 1];
@@ -640,6 +641,7 @@ int kind_of(int dtype) { return dtype == MOE_F32 ? 1 : (dtype == MOE_I8 ? 2 : 0)
 // 2 = automatic: pairs when the experts average at least 4 M tiles, so that
 // an expert's odd last tile (which idles half a pair) costs little.
 std::atomic<int> g_gemm_cta_pair{2};
+std::atomic<int> g_gemm_band{GROUP_M};  // M tiles per band of the tile raster
 
 bool use_pair(int64_t max_tiles, int E) {
   const int v = g_gemm_cta_pair.load();
@@ -751,6 +753,7 @@ extern "C" int moe_gemm1_swiglu(const void* a, int dtype, int64_t a_rows, int64_
   p.b_rows_per_expert = (int)(2 * inter);
   p.inter = (int)inter;
   p.idesc = make_idesc(dtype, pair ? 2 * BM : BM);
+  p.band_tiles = g_gemm_band.load();
   p.table = tile_table;
   p.max_tiles = (int)max_tiles;
   p.a_rows = a_rows;
@@ -803,6 +806,7 @@ int gemm2_impl(const void* h, int dtype, int64_t h_rows, int64_t inter, const vo
   p.b_rows_per_expert = (int)hidden;
   p.inter = (int)inter;
   p.idesc = make_idesc(dtype, pair ? 2 * BM : BM);
+  p.band_tiles = g_gemm_band.load();
   p.table = tile_table;
   p.max_tiles = (int)max_tiles;
   p.a_rows = h_rows;
@@ -850,11 +854,17 @@ extern "C" int moe_set_option(int option, int value) {
     g_gemm_cta_pair.store(value);
     return MOE_OK;
   }
+  if (option == MOE_OPT_GEMM_BAND) {
+    MOE_CHECK_ARG(value >= 1 && value <= 1 << 20, "moe_set_option: GEMM_BAND takes 1 .. 2^20 tiles");
+    g_gemm_band.store(value);
+    return MOE_OK;
+  }
   return set_error(MOE_ERR_INVALID_ARG, "moe_set_option: unknown option %d", option);
 }
 
 extern "C" int moe_get_option(int option) {
   if (option == MOE_OPT_GEMM_CTA_PAIR) return g_gemm_cta_pair.load();
+  if (option == MOE_OPT_GEMM_BAND) return g_gemm_band.load();
   return -1;
 }
 
