@@ -92,7 +92,11 @@ typedef enum {
                                pairs when the experts average at least 4 M tiles of 128 rows */,
   MOE_OPT_GEMM_BAND = 2     /* M tiles per band of the GEMMs' expert-major tile order (default 16): each
                                expert's tiles run in bands of this many M tiles, every band swept over
-                               all N tiles, so CTAs running together share weight tiles in L2 */
+                               all N tiles, so CTAs running together share weight tiles in L2 */,
+  MOE_OPT_GEMM_STREAM_K = 3 /* 1: the down GEMM with the combine epilogue (MOE_EPI_COMBINE_ADD, additive)
+                               runs its full waves as whole tiles and splits the partial last wave's
+                               (tile, K block) work evenly over the grid, adding partial sums;
+                               0 (default): whole tiles only */
 } moe_option_t;
 MOE_API int moe_set_option(int option, int value);
 /* Current value of an option, or -1 for an unknown option. */

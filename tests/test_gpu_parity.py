@@ -400,3 +400,30 @@ def test_cuda_graph_replay_matches_eager(T):
         # runs can differ by the order of those additions (bf16 ulp level)
         assert max_abs_rel(npf(y), npf(y_ref)) < 2e-3
     assert_no_device_error()
+
+
+@pytest.mark.parametrize("pair", [1, 0])
+def test_stream_k_combine_matches_whole_tiles(pair):
+    """With MOE_OPT_GEMM_STREAM_K the down GEMM's combine epilogue splits the
+    partial last wave's (tile, K block) work over the grid; partial sums must
+    add up to the whole-tile result (fp32 atomics: equal up to summation
+    order)."""
+    lib = _lib.load()
+    T, H, I, E, k = 1000, 1024, 1536, 8, 2  # K = I: 24 blocks per tile, tiles not a multiple of the grid
+    x, w13, w2, ids, wts = topk_case(T, H, I, E, k, "uniform-softmax", torch.bfloat16, seed=21)
+    old_pair = lib.moe_get_option(_lib.OPT_GEMM_CTA_PAIR)
+    lib.moe_set_option(_lib.OPT_GEMM_CTA_PAIR, pair)
+    try:
+        lib.moe_set_option(_lib.OPT_GEMM_STREAM_K, 1)
+        y_sk = run_topk(x, w13, w2, ids, wts)
+        lib.moe_set_option(_lib.OPT_GEMM_STREAM_K, 0)
+        y_tiles = run_topk(x, w13, w2, ids, wts)
+    finally:
+        lib.moe_set_option(_lib.OPT_GEMM_STREAM_K, 0)
+        lib.moe_set_option(_lib.OPT_GEMM_CTA_PAIR, old_pair)
+    # partial sums reach the fp32 accumulator in another order: the bf16
+    # outputs may differ by one rounding step (2^-7 relative)
+    assert max_abs_rel(npf(y_sk), npf(y_tiles)) <= 2.0 ** -7
+    ref = O.moe_mlp_topk(npf(x), npf(w13), npf(w2), wts, ids, round_hidden=O.round_bf16)
+    assert max_abs_rel(npf(y_sk), ref) < TOL
+    assert_no_device_error()
