@@ -496,6 +496,25 @@ def main():
     flops_step = 6.0 * S_local * H * I
     value = world * T / (ms / 1e3)
 
+    # yardstick: cuBLAS (torch.matmul) on a dense GEMM with the gate_up
+    # launch's shape [S, H] x [H, 2I], timed the same way right after
+    if world == 1 and not cfg["quant"] and cfg["dtype"] == "bf16":
+        a = torch.randn(S_local, H, device=device, dtype=dt)
+        b = torch.randn(H, 2 * I, device=device, dtype=dt)
+        for _ in range(3):
+            torch.matmul(a, b)
+        c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = max(3, args.steps)
+        c0.record(stream)
+        for _ in range(reps):
+            torch.matmul(a, b)
+        c1.record(stream)
+        torch.cuda.synchronize()
+        cub_ms = c0.elapsed_time(c1) / reps
+        roofline["cublas_dense_same_shape"] = {"ms": cub_ms, "tflops": flops_gemm1 / (cub_ms / 1e3) / 1e12,
+                                               "ours_vs_cublas": cub_ms / st_ms["gemm1"]}
+        del a, b
+
     line = {"metric": "fused MoE MLP tokens/s", "value": value, "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": dtype_name, "data": "synthetic", "config": config_json,
