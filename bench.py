@@ -73,29 +73,64 @@ def load_traffic(config: str):
 
 
 class ClockSampler:
-    """Samples nvidia-smi clocks/throttle reasons while running."""
+    """Samples the SM clock and the clock-event (throttle) reasons of one GPU
+    every 10 ms through NVML on a background thread (nvidia-smi at 200 ms if
+    NVML is unavailable); `stop(t0, t1)` summarises the samples taken between
+    two host timestamps, the timed region."""
 
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"),
+               ("hw_power_brake_slowdown", "nvmlClocksEventReasonHwPowerBrakeSlowdown"))
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,utilization.gpu,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
+    def __init__(self, device_index: int):
+        self.dev = device_index
+        self.samples = []  # (host time, sm MHz, max sm MHz, [reasons])
+        self.thread = None
         self.proc = None
         self.file = None
+        self.stop_flag = False
 
     def start(self):
+        import threading
+
+        try:
+            import pynvml
+            import torch
+
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByIndex(torch.cuda._get_nvml_device_index(self.dev))
+            smax = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+            masks = [(n, int(getattr(pynvml, attr))) for n, attr in self.REASONS]
+
+            def run():
+                while not self.stop_flag:
+                    try:
+                        sm = float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM))
+                        bits = int(pynvml.nvmlDeviceGetCurrentClocksEventReasons(h))
+                        self.samples.append((time.time(), sm, smax, [n for n, b in masks if bits & b]))
+                    except Exception:
+                        pass
+                    time.sleep(0.01)
+
+            self.thread = threading.Thread(target=run, daemon=True)
+            self.thread.start()
+            return
+        except Exception:
+            self.thread = None
         try:
             self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
-                 "-i", str(self.gpu)], stdout=self.file, stderr=subprocess.DEVNULL)
+                 "-i", str(self.dev)], stdout=self.file, stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
 
-    def stop(self):
-        if self.proc is None:
-            return None
+    def _smi_rows(self):
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
@@ -106,21 +141,33 @@ class ClockSampler:
         rows = [r.split(",") for r in self.file.read().strip().splitlines() if r.strip()]
         self.file.close()
         os.unlink(self.file.name)
-        sm, smax, reasons = [], [], set()
+        out = []
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for r in rows:
             try:
-                sm.append(float(r[1]))
-                smax.append(float(r[2]))
-                for n, v in zip(names, r[6:10]):
-                    if v.strip().lower() == "active":
-                        reasons.add(n)
+                out.append((None, float(r[1]), float(r[2]),
+                            [n for n, v in zip(names, r[6:10]) if v.strip().lower() == "active"]))
             except (ValueError, IndexError):
                 continue
-        if not sm:
+        return out
+
+    def stop(self, t0=None, t1=None):
+        if self.thread is not None:
+            self.stop_flag = True
+            self.thread.join(timeout=5)
+            rows, source = self.samples, "nvml 10 ms"
+            if t0 is not None and t1 is not None:
+                inside = [r for r in rows if t0 <= r[0] <= t1]
+                rows = inside or [r for r in rows if r[0] >= t0][:1]
+        elif self.proc is not None:
+            rows, source = self._smi_rows(), "nvidia-smi 200 ms"
+        else:
             return None
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(smax), "reasons": sorted(reasons),
-                "samples": len(sm)}
+        if not rows:
+            return None
+        reasons = sorted({n for r in rows for n in r[3]})
+        return {"sm_mhz": statistics.median(r[1] for r in rows), "sm_max_mhz": max(r[2] for r in rows),
+                "reasons": reasons, "samples": len(rows), "sampler": source}
 
 
 # --------------------------------------------------------------------------- inputs
@@ -252,6 +299,8 @@ def main():
     ap.add_argument("--gemm", default="auto", choices=["auto", "pair", "single"],
                     help="grouped GEMM variant: CTA pairs (cta_group::2), one CTA per tile, or chosen by size")
     ap.add_argument("--band", type=int, default=0, help="GEMM tile-order band width in M tiles (0: default)")
+    ap.add_argument("--half-units", type=int, default=1, choices=[0, 1],
+                    help="CTA-pair GEMMs: each expert's odd last M tile as an M=128 pair MMA (1, default)")
     ap.add_argument("--eager", action="store_true",
                     help="N=1: call the op directly each step instead of replaying it from a captured CUDA graph")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -271,6 +320,7 @@ def main():
     config_json = {"workload": cfg["desc"], "tokens_per_gpu": T, "hidden": H, "inter": I, "experts": E,
                    "top_k": k, "routing": cfg["routing"], "dtype": cfg["dtype"] + ("+w8a8" if cfg["quant"] else ""),
                    "parallelism": f"ep{world}" if world > 1 else "single", "gemm": args.gemm,
+                   "half_units": bool(args.half_units),
                    "ep_exchange": args.ep if world > 1 else None, "cuda_graph": bool(args.graph and world == 1),
                    "l2": "weights (%.2f GB) exceed the 126 MB L2, streamed every step" %
                          (E * 3 * H * I * (1 if cfg["quant"] else (4 if cfg["dtype"] == "fp32" else 2)) / 1e9)}
@@ -305,6 +355,7 @@ def main():
     lib.moe_set_option(_lib.OPT_GEMM_CTA_PAIR, {"pair": 1, "single": 0, "auto": 2}[args.gemm])
     if args.band:
         lib.moe_set_option(_lib.OPT_GEMM_BAND, args.band)
+    lib.moe_set_option(_lib.OPT_GEMM_HALF_UNITS, args.half_units)
 
     x, ids, wts, dt = make_inputs(cfg, rank, device)
     if world > 1:
@@ -368,6 +419,7 @@ def main():
     barrier()
     torch.cuda.synchronize()
     launches0 = lib.moe_launch_count()
+    t_region0 = time.time()
     handles[0].record(stream)
     for i in range(args.steps):
         if not args.graph:
@@ -376,8 +428,9 @@ def main():
     lib.moe_set_stage_events(None, 0)
     handles[1].record(stream)
     torch.cuda.synchronize()
+    t_region1 = time.time()
     barrier()
-    clocks = sampler.stop()
+    clocks = sampler.stop(t_region0, t_region1)
     launches = lib.moe_launch_count() - launches0
     ms = handles[0].elapsed_time(handles[1]) / args.steps
     if args.graph:

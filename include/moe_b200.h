@@ -96,7 +96,10 @@ typedef enum {
   MOE_OPT_GEMM_STREAM_K = 3 /* 1: the down GEMM with the combine epilogue (MOE_EPI_COMBINE_ADD, additive)
                                runs its full waves as whole tiles and splits the partial last wave's
                                (tile, K block) work evenly over the grid, adding partial sums;
-                               0 (default): whole tiles only */
+                               0 (default): whole tiles only */,
+  MOE_OPT_GEMM_HALF_UNITS = 4 /* CTA pairs only. 1 (default): an expert's odd last M tile runs as one
+                               M=128 pair MMA, 64 of its rows on each CTA; 0: as an M=256 pair MMA
+                               whose second CTA's rows are idle */
 } moe_option_t;
 MOE_API int moe_set_option(int option, int value);
 /* Current value of an option, or -1 for an unknown option. */
@@ -168,7 +171,9 @@ MOE_API int moe_route_topk(const void* logits, int dtype, int64_t num_tokens, in
  *   padded_offsets[e] first padded row of expert e; [E] = total padded rows
  *   tile_table       compact schedule consumed by the GEMMs
  * Ids outside [0, num_experts) are dropped (counted in tile_table[2]).
- * sorted_slots needs moe_align_capacity() entries.
+ * sorted_slots needs moe_align_capacity() entries: num_slots plus block_m - 1
+ * padding rows for each expert that can hold a slot (at most
+ * min(num_experts, num_slots)), rounded up to whole tiles of block_m rows.
  * -------------------------------------------------------------------------- */
 MOE_API int64_t moe_align_capacity(int64_t num_slots, int num_experts, int block_m);
 MOE_API size_t moe_align_workspace_size(int64_t num_tokens, int top_k, int num_experts, int block_m);

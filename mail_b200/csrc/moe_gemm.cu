@@ -58,6 +58,8 @@ struct Params {
   int b_rows_per_expert;  // rows of B per expert (2I or H)
   int inter;              // GEMM1: row offset of the up half within an expert
   uint32_t idesc;         // tcgen05 instruction descriptor
+  uint32_t idesc_half;    // CTA pair: descriptor of the M=128 MMA (64 rows per CTA) for an odd last tile
+  int half_units;         // CTA pair: run each expert's odd last tile as an M=128 pair MMA
   const int32_t* table;
   int max_tiles;
   int64_t a_rows;
@@ -209,7 +211,13 @@ __device__ __forceinline__ float acc_value(uint32_t bits) {
 }
 
 // Pipeline geometry of the two variants. A scheduling unit is one 128-row M
-// tile (single CTA) or two consecutive M tiles of one expert (CTA pair).
+// tile (single CTA) or two consecutive M tiles of one expert (CTA pair). In a
+// pair, the odd last tile of an expert is a half unit: one M=128 pair MMA
+// (cta_group::2) whose 128 rows split 64 / 64 over the two CTAs, which runs at
+// the same rate per row as the M=256 MMA (64 vs 128 cycles for N=256, K=16),
+// so no CTA idles. Its accumulator layout in each CTA's tensor memory: lanes
+// 0-63 hold the CTA's 64 rows x N columns [0, N/2), lanes 64-127 the same rows
+// x columns [N/2, N), both at TMEM columns [0, N/2).
 template <bool PAIR>
 struct Cfg {
   static constexpr int kStages = PAIR ? 6 : 4;
@@ -219,10 +227,12 @@ struct Cfg {
   static constexpr uint32_t kTxBytes = PAIR ? 2 * kStageBytes : kStageBytes;  // per stage, whole MMA
 };
 
+// tmap_b64: B with 64-row boxes; the gate_up GEMM's half units load 64 gate
+// and 64 up rows per CTA so that one thread's TMEM lane holds both.
 template <int KIND, bool SWIGLU, bool PAIR>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     moe_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
-                    const Params p) {
+                    const __grid_constant__ CUtensorMap tmap_b64, const Params p) {
   using C = Cfg<PAIR>;
   constexpr int S = C::kStages;
   extern __shared__ uint8_t smem_raw[];
@@ -262,6 +272,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   if (warp == 0 && lane == 0) {
     ptx::prefetch_tmap(&tmap_a);
     ptx::prefetch_tmap(&tmap_b);
+    if (SWIGLU && PAIR && p.half_units) ptx::prefetch_tmap(&tmap_b64);
   }
   for (int i = threadIdx.x; i <= E; i += blockDim.x) s_cum[i] = p.table[TileTable::cum_off() + i];
   if constexpr (PAIR) {
@@ -308,16 +319,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const int32_t* row_count_tab = p.table + TileTable::count_off(E, p.max_tiles);
 
   const int group_units = max(1, PAIR ? p.band_tiles / 2 : p.band_tiles);
-  // unit t -> (expert e, n tile, this CTA's M tile m, whether m holds rows)
-  auto locate = [&](int t, int& e, int& n, int& m, bool& valid) {
+  // unit t -> (expert e, n tile, this CTA's M tile m, whether m holds rows,
+  // whether the unit is a half unit: one tile split 64 / 64 over the pair)
+  auto locate = [&](int t, int& e, int& n, int& m, bool& valid, bool& half) {
     int u;
     decode_unit(t, s_ucum, E, NT, group_units, u, n, e);
     if constexpr (PAIR) {
-      m = s_cum[e] + 2 * (u - s_ucum[e]) + (int)rank;
+      const int m0 = s_cum[e] + 2 * (u - s_ucum[e]);
+      half = p.half_units && m0 + 1 == s_cum[e + 1];
+      m = half ? m0 : m0 + (int)rank;
       valid = m < s_cum[e + 1];
     } else {
       m = u;
       valid = true;
+      half = false;
     }
   };
 
@@ -334,16 +349,22 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       int t, kb_begin, kb_end;
       while (ok && seg.next(t, kb_begin, kb_end)) {
         int e, n, m;
-        bool valid;
-        locate(t, e, n, m, valid);
+        bool valid, half;
+        locate(t, e, n, m, valid, half);
         // an empty peer half still loads a (masked) A box: the rows after the
-        // expert's last tile
-        const int row0 = valid ? row_start_tab[m] : row_start_tab[m - 1] + BM;
+        // expert's last tile; in a half unit each CTA's MMA rows are the first
+        // 64 of its box
+        const int row0 = half ? row_start_tab[m] + (int)rank * (BM / 2)
+                              : (valid ? row_start_tab[m] : row_start_tab[m - 1] + BM);
         int brow;
-        if constexpr (SWIGLU)
-          brow = e * p.b_rows_per_expert + n * (BN / 2) + ((PAIR && rank) ? p.inter : 0);
-        else
+        if constexpr (SWIGLU) {
+          if (half)  // gate rows [64 r, 64 r + 64) of the N tile, then the same up rows
+            brow = e * p.b_rows_per_expert + n * (BN / 2) + (int)rank * (BN / 4);
+          else
+            brow = e * p.b_rows_per_expert + n * (BN / 2) + ((PAIR && rank) ? p.inter : 0);
+        } else {
           brow = e * p.b_rows_per_expert + n * BN + (PAIR ? (int)rank * (BN / 2) : 0);
+        }
         for (int kb = kb_begin; kb < kb_end; ++kb) {
           if (!ptx::mbar_wait(&empty[stage], phase ^ 1, abort_flag)) {
             ok = false;
@@ -354,7 +375,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             if (leader) ptx::mbar_arrive_expect_tx(&full[stage], C::kTxBytes);
             const uint32_t bar = ptx::mapa(ptx::smem_u32(&full[stage]), 0);  // the leader's full barrier
             ptx::tma_load_2d_pair(sA + stage * A_BYTES, &tmap_a, bar, kx, row0);
-            ptx::tma_load_2d_pair(sB + stage * C::kBBytes, &tmap_b, bar, kx, brow);
+            if (SWIGLU && half) {
+              ptx::tma_load_2d_pair(sB + stage * C::kBBytes, &tmap_b64, bar, kx, brow);
+              ptx::tma_load_2d_pair(sB + stage * C::kBBytes + C::kBBytes / 2, &tmap_b64, bar, kx, brow + p.inter);
+            } else {
+              ptx::tma_load_2d_pair(sB + stage * C::kBBytes, &tmap_b, bar, kx, brow);
+            }
           } else {
             ptx::mbar_arrive_expect_tx(&full[stage], C::kTxBytes);
             ptx::tma_load_2d(sA + stage * A_BYTES, &tmap_a, &full[stage], kx, row0);
@@ -411,6 +437,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
         ptx::tc_fence_after();
         const uint32_t d = tmem_base + acc * BN;
+        uint32_t idesc = p.idesc;
+        if constexpr (PAIR) {
+          int e, n, m;
+          bool valid, half;
+          locate(t, e, n, m, valid, half);
+          if (half) idesc = p.idesc_half;
+        }
         for (int kb = kb_begin; kb < kb_end; ++kb) {
           if (!ptx::mbar_wait(&full[stage], phase, abort_flag)) {
             ok = false;
@@ -423,8 +456,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           for (int k = 0; k < ROW_BYTES / 32; ++k) {
             const uint64_t ad = ptx::smem_desc_k128(a_addr + k * 32), bd = ptx::smem_desc_k128(b_addr + k * 32);
             const uint32_t accum = (kb > kb_begin || k > 0) ? 1u : 0u;
-            if constexpr (PAIR) ptx::umma_pair<KIND>(d, ad, bd, p.idesc, accum);
-            else ptx::umma<KIND>(d, ad, bd, p.idesc, accum);
+            if constexpr (PAIR) ptx::umma_pair<KIND>(d, ad, bd, idesc, accum);
+            else ptx::umma<KIND>(d, ad, bd, idesc, accum);
           }
           if constexpr (PAIR) ptx::umma_commit_pair_mc(&empty[stage], 0x3);
           else ptx::umma_commit(&empty[stage]);
@@ -450,7 +483,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   } else {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;          // TMEM lane quarter this warp may access
-    const int r = q * 32 + lane;     // row of the tile held by this thread
     const uint32_t tempty_leader[2] = {PAIR ? ptx::mapa(ptx::smem_u32(&tempty[0]), 0) : ptx::smem_u32(&tempty[0]),
                                        PAIR ? ptx::mapa(ptx::smem_u32(&tempty[1]), 0) : ptx::smem_u32(&tempty[1])};
     int it = 0;
@@ -459,8 +491,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     int t, kb_begin, kb_end;
     for (; seg.next(t, kb_begin, kb_end); ++it) {
       int e, n, m;
-      bool valid;
-      locate(t, e, n, m, valid);
+      bool valid, half;
+      locate(t, e, n, m, valid, half);
       const int acc = it & 1;
       const uint32_t acc_par = (it >> 1) & 1;
       bool w_ok = ptx::mbar_wait(&tfull[acc], acc_par, abort_flag);
@@ -471,6 +503,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       ptx::tc_fence_after();
       const int32_t rstart = valid ? row_start_tab[m] : 0;
       const int32_t rcount = valid ? row_count_tab[m] : 0;
+      // tile row of this thread, and the first accumulator column it holds
+      // (TMEM column 0 of its lane) relative to the unit's N tile
+      const int r = half ? (int)rank * (BM / 2) + (q & 1) * 32 + lane : q * 32 + lane;
       const int64_t grow = (int64_t)rstart + r;
       const bool row_ok = (r < rcount) && (grow < p.a_rows);
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
@@ -479,13 +514,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
       if constexpr (SWIGLU) {
         const int64_t wrow = (int64_t)e * p.b_rows_per_expert;
+        // whole unit: gate at TMEM columns [0, 128), up at [128, 256), 128
+        // features; half unit: this lane's 64 features, gate at [0, 64), up
+        // at [64, 128)
+        const int nchunk = half ? 2 : 4;
+        const int up_col = half ? BN / 4 : BN / 2;
+        const int cbase = n * (BN / 2) + (half ? (q >> 1) * (BN / 4) : 0);
 #pragma unroll 1
-        for (int c = 0; c < (BN / 2) / 32; ++c) {
+        for (int c = 0; c < nchunk; ++c) {
           uint32_t g[32], u[32];
           ptx::tmem_ld32(tbase + c * 32, g);
-          ptx::tmem_ld32(tbase + BN / 2 + c * 32, u);
+          ptx::tmem_ld32(tbase + up_col + c * 32, u);
           ptx::tmem_ld_wait();
-          const int col0 = n * (BN / 2) + c * 32;
+          const int col0 = cbase + c * 32;
           if (row_ok && col0 < p.n_valid) {
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
@@ -529,15 +570,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
         if (dst_row >= p.out_rows) do_store = false;
         const int64_t wrow = (int64_t)e * p.b_rows_per_expert;
+        // whole unit: N tile columns [0, 256) at TMEM columns [0, 256); half
+        // unit: this lane's half of the N tile at TMEM columns [0, 128)
+        const int ncols = half ? BN / 2 : BN;
+        const int cbase = n * BN + (half ? (q >> 1) * (BN / 2) : 0);
         if (p.out_dtype != MOE_F32 && p.epi != MOE_EPI_COMBINE_ADD) {
           uint8_t* stage = epi_stage + (warp - 2) * STAGE_WARP_BYTES;
 #pragma unroll 1
-          for (int c2 = 0; c2 < BN / 64; ++c2) {
+          for (int c2 = 0; c2 < ncols / 64; ++c2) {
             uint32_t v0[32], v1[32];
             ptx::tmem_ld32(tbase + c2 * 64, v0);
             ptx::tmem_ld32(tbase + c2 * 64 + 32, v1);
             ptx::tmem_ld_wait();
-            const int col0 = n * BN + c2 * 64;
+            const int col0 = cbase + c2 * 64;
             uint32_t packed[32];
 #pragma unroll
             for (int i = 0; i < 32; ++i) {
@@ -560,11 +605,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           }
         } else {
 #pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
+        for (int c = 0; c < ncols / 32; ++c) {
           uint32_t v[32];
           ptx::tmem_ld32(tbase + c * 32, v);
           ptx::tmem_ld_wait();
-          const int col0 = n * BN + c * 32;
+          const int col0 = cbase + c * 32;
           if (do_store && col0 < p.n_valid) {
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
@@ -680,8 +725,13 @@ uint32_t make_idesc(int dtype, int m) {
 int kind_of(int dtype) { return dtype == MOE_F32 ? 1 : (dtype == MOE_I8 ? 2 : 0); }
 
 // GEMM variant: 1 = CTA pairs (cta_group::2), 0 = one CTA per tile,
-// 2 = automatic: pairs when the experts average at least 4 M tiles, so that
-// an expert's odd last tile (which idles half a pair) costs little.
+// 2 = automatic: pairs when the experts average at least 4 M tiles (measured:
+// Mixtral layer, 9 tiles per expert, pairs 3 % faster per step), or when the
+// launch has fewer (M tile, N tile) units than SMs, where a pair spreads each
+// unit's weight stream over two SMs (Qwen3 decode at 1 token: 0.056 vs
+// 0.064 ms per step); one CTA per tile otherwise (DeepSeek-V3 w8a8 at one GPU,
+// 2 tiles per expert: 3.81 vs 4.28 ms per step; Qwen3 decode at 256 tokens:
+// 0.277 vs 0.290 ms).
 std::atomic<int> g_gemm_cta_pair{2};
 std::atomic<int> g_gemm_band{GROUP_M};  // M tiles per band of the tile raster
 // Stream-K split of the partial last wave for the additive combine epilogue.
@@ -689,10 +739,13 @@ std::atomic<int> g_gemm_band{GROUP_M};  // M tiles per band of the tile raster
 // and 0.745 ms without (the persistent grid's tail costs less than the extra
 // partial-tile epilogues and the K-split tail's weaker L2 reuse).
 std::atomic<int> g_gemm_stream_k{0};
+// CTA pairs: an expert's odd last M tile as one M=128 pair MMA (64 rows per
+// CTA) instead of an M=256 one with one CTA's half idle.
+std::atomic<int> g_gemm_half_units{1};
 
-bool use_pair(int64_t max_tiles, int E) {
+bool use_pair(int64_t max_tiles, int E, int64_t n_tiles) {
   const int v = g_gemm_cta_pair.load();
-  if (v == 2) return max_tiles >= 4 * (int64_t)E;
+  if (v == 2) return max_tiles >= 4 * (int64_t)E || max_tiles * n_tiles < num_sms();
   return v != 0;
 }
 
@@ -703,7 +756,8 @@ size_t gemm_smem_bytes(int E) {
 }
 
 template <int KIND, bool SWIGLU, bool PAIR>
-int launch_kind(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, int64_t units_ub, cudaStream_t st) {
+int launch_kind(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tb64, const Params& p,
+                int64_t units_ub, cudaStream_t st) {
   const size_t smem = gemm_smem_bytes<PAIR>(p.E);
   auto kfn = moe_gemm_kernel<KIND, SWIGLU, PAIR>;
   MOE_CUDA_TRY(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
@@ -731,19 +785,20 @@ int launch_kind(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, i
   }
   if (grid <= 0) return MOE_OK;
   cfg.gridDim = dim3((unsigned)grid);
-  MOE_CUDA_TRY(cudaLaunchKernelEx(&cfg, kfn, ta, tb, p));
+  MOE_CUDA_TRY(cudaLaunchKernelEx(&cfg, kfn, ta, tb, tb64, p));
   MOE_LAUNCH_CHECK("moe_gemm_kernel");
   return MOE_OK;
 }
 
 template <bool SWIGLU, bool PAIR>
-int launch(int dtype, const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, cudaStream_t st) {
+int launch(int dtype, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tb64, const Params& p,
+           cudaStream_t st) {
   // units: M tiles (single CTA) or M-tile pairs, upper bound max_tiles
   const int64_t units_ub = (int64_t)(PAIR ? (p.max_tiles + p.E) / 2 + p.E : p.max_tiles) * p.n_tiles;
   switch (kind_of(dtype)) {
-    case 0: return launch_kind<0, SWIGLU, PAIR>(ta, tb, p, units_ub, st);
-    case 1: return launch_kind<1, SWIGLU, PAIR>(ta, tb, p, units_ub, st);
-    default: return launch_kind<2, SWIGLU, PAIR>(ta, tb, p, units_ub, st);
+    case 0: return launch_kind<0, SWIGLU, PAIR>(ta, tb, tb64, p, units_ub, st);
+    case 1: return launch_kind<1, SWIGLU, PAIR>(ta, tb, tb64, p, units_ub, st);
+    default: return launch_kind<2, SWIGLU, PAIR>(ta, tb, tb64, p, units_ub, st);
   }
 }
 
@@ -788,10 +843,13 @@ extern "C" int moe_gemm1_swiglu(const void* a, int dtype, int64_t a_rows, int64_
   MOE_CHECK_ARG((uintptr_t)a % 16 == 0 && (uintptr_t)w13 % 16 == 0 && (uintptr_t)h % 16 == 0,
                 "moe_gemm1_swiglu: pointers must be 16-byte aligned");
   if (a_rows == 0 || max_tiles == 0) return MOE_OK;
-  CUtensorMap ta, tb;
-  const bool pair = use_pair(max_tiles, num_experts);
+  CUtensorMap ta, tb, tb64;
+  const bool pair = use_pair(max_tiles, num_experts, ceil_div(inter, BN / 2));
+  const bool half_units = pair && g_gemm_half_units.load() != 0;
   MOE_TRY(make_tmap(&ta, a, dtype, hidden, a_rows, BM));
   MOE_TRY(make_tmap(&tb, w13, dtype, hidden, (uint64_t)num_experts * 2 * inter, BN / 2));
+  if (half_units) MOE_TRY(make_tmap(&tb64, w13, dtype, hidden, (uint64_t)num_experts * 2 * inter, BN / 4));
+  else tb64 = tb;
   Params p{};
   p.E = num_experts;
   p.num_kb = (int)ceil_div(hidden * dtype_size(dtype), ROW_BYTES);
@@ -800,6 +858,8 @@ extern "C" int moe_gemm1_swiglu(const void* a, int dtype, int64_t a_rows, int64_
   p.b_rows_per_expert = (int)(2 * inter);
   p.inter = (int)inter;
   p.idesc = make_idesc(dtype, pair ? 2 * BM : BM);
+  p.idesc_half = make_idesc(dtype, BM);
+  p.half_units = half_units;
   p.band_tiles = g_gemm_band.load();
   p.table = tile_table;
   p.max_tiles = (int)max_tiles;
@@ -812,8 +872,8 @@ extern "C" int moe_gemm1_swiglu(const void* a, int dtype, int64_t a_rows, int64_
   p.a_scale = a_scale;
   p.b_scale = w13_scale;
   p.top_k = 1;
-  return pair ? launch<true, true>(dtype, ta, tb, p, as_stream(stream))
-              : launch<true, false>(dtype, ta, tb, p, as_stream(stream));
+  return pair ? launch<true, true>(dtype, ta, tb, tb64, p, as_stream(stream))
+              : launch<true, false>(dtype, ta, tb, tb64, p, as_stream(stream));
 }
 
 namespace moe {
@@ -842,7 +902,7 @@ int gemm2_impl(const void* h, int dtype, int64_t h_rows, int64_t inter, const vo
                 "moe_gemm2: pointers must be 16-byte aligned");
   if (h_rows == 0 || max_tiles == 0) return MOE_OK;
   CUtensorMap ta, tb;
-  const bool pair = use_pair(max_tiles, num_experts);
+  const bool pair = use_pair(max_tiles, num_experts, ceil_div(hidden, BN));
   MOE_TRY(make_tmap(&ta, h, dtype, inter, h_rows, BM));
   MOE_TRY(make_tmap(&tb, w2, dtype, inter, (uint64_t)num_experts * hidden, pair ? BN / 2 : BN));
   Params p{};
@@ -853,6 +913,8 @@ int gemm2_impl(const void* h, int dtype, int64_t h_rows, int64_t inter, const vo
   p.b_rows_per_expert = (int)hidden;
   p.inter = (int)inter;
   p.idesc = make_idesc(dtype, pair ? 2 * BM : BM);
+  p.idesc_half = make_idesc(dtype, BM);
+  p.half_units = pair && g_gemm_half_units.load() != 0;
   p.band_tiles = g_gemm_band.load();
   p.table = tile_table;
   p.max_tiles = (int)max_tiles;
@@ -872,7 +934,7 @@ int gemm2_impl(const void* h, int dtype, int64_t h_rows, int64_t inter, const vo
   // the weighted combine adds partial sums, so its work can be split along K
   // evenly over the grid (no partly idle last wave)
   p.stream_k = epilogue == MOE_EPI_COMBINE_ADD && g_gemm_stream_k.load() != 0;
-  return pair ? launch<false, true>(dtype, ta, tb, p, stream) : launch<false, false>(dtype, ta, tb, p, stream);
+  return pair ? launch<false, true>(dtype, ta, tb, tb, p, stream) : launch<false, false>(dtype, ta, tb, tb, p, stream);
 }
 }  // namespace
 
@@ -913,6 +975,10 @@ extern "C" int moe_set_option(int option, int value) {
     g_gemm_stream_k.store(value != 0);
     return MOE_OK;
   }
+  if (option == MOE_OPT_GEMM_HALF_UNITS) {
+    g_gemm_half_units.store(value != 0);
+    return MOE_OK;
+  }
   return set_error(MOE_ERR_INVALID_ARG, "moe_set_option: unknown option %d", option);
 }
 
@@ -920,6 +986,7 @@ extern "C" int moe_get_option(int option) {
   if (option == MOE_OPT_GEMM_CTA_PAIR) return g_gemm_cta_pair.load();
   if (option == MOE_OPT_GEMM_BAND) return g_gemm_band.load();
   if (option == MOE_OPT_GEMM_STREAM_K) return g_gemm_stream_k.load();
+  if (option == MOE_OPT_GEMM_HALF_UNITS) return g_gemm_half_units.load();
   return -1;
 }
 

@@ -494,9 +494,11 @@ AlignWs align_ws(int64_t S, int E) {
 
 extern "C" int64_t moe_align_capacity(int64_t num_slots, int num_experts, int block_m) {
   if (num_slots < 0 || num_experts <= 0 || block_m <= 0) return -1;
-  // every expert's segment is padded by at most block_m - 1 rows; round the
-  // total up to whole tiles so TMA boxes of block_m rows stay in bounds.
-  int64_t cap = num_slots + (int64_t)num_experts * (block_m - 1);
+  // every non-empty expert's segment is padded by at most block_m - 1 rows,
+  // and at most min(E, slots) experts are non-empty; round the total up to
+  // whole tiles so TMA boxes of block_m rows stay in bounds.
+  const int64_t nonempty = std::min<int64_t>(num_experts, num_slots);
+  int64_t cap = num_slots + nonempty * (block_m - 1);
   return ceil_div(cap, block_m) * block_m;
 }
 

@@ -4,9 +4,11 @@ import ctypes
 import os
 import re
 
+import numpy as np
 import pytest
 
 from mail_b200 import _lib
+from oracle import moe_oracle as O
 
 HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include", "moe_b200.h")
 
@@ -30,8 +32,9 @@ def test_version_and_pure_host_queries():
     assert lib.moe_version() >= 100
     assert lib.moe_tile_grid(120, 4, 128) == 1 + 4
     assert lib.moe_tile_grid(0, 4, 128) == 4
-    assert lib.moe_align_capacity(8192, 8, 128) == 8192 + 8 * 128 - 0 or lib.moe_align_capacity(8192, 8, 128) >= 8192
-    assert lib.moe_align_capacity(8192, 8, 128) % 128 == 0
+    assert lib.moe_align_capacity(8192, 8, 128) == 9216  # 8192 + 8 * 127, whole tiles
+    assert lib.moe_align_capacity(8, 128, 128) == 1024    # decode: at most 8 experts hold a slot
+    assert lib.moe_align_capacity(0, 128, 128) == 0
     assert lib.moe_tile_table_ints(8, 100) == 4 + 9 + 200
     assert lib.moe_fused_experts_workspace_size(4096, 4096, 14336, 8, 2, _lib.BF16, _lib.BF16) > 0
     assert lib.moe_fused_mlp_workspace_size(120, 256, 512, 4, _lib.F16, 64) == 0  # block_m must be 128
@@ -66,3 +69,15 @@ def test_python_wrapper_raises_without_cuda_tensors():
     x = torch.zeros(4, 8)
     with pytest.raises(ValueError, match="CUDA"):
         mail_b200.fused_moe_mlp(x, torch.zeros(2, 8, 16), torch.zeros(2, 8, 8), torch.tensor([2, 2]))
+
+
+@pytest.mark.parametrize("T,E,k,routing", [(1, 128, 8, "zipf1.2"), (3, 256, 8, "sigmoid"), (4096, 8, 2, "uniform-softmax"),
+                                           (300, 16, 4, "hot25-zipf1.0")])
+def test_align_capacity_bounds_padded_rows(T, E, k, routing):
+    """The capacity covers the padded rows of any routing (oracle align)."""
+    ids, _ = O.synthetic_routing(routing, T, E, k, seed=T)
+    cap = _lib.load().moe_align_capacity(T * k, E, 128)
+    assert int(O.align(ids, E, 128)["padded_offsets"][-1]) <= cap
+    # worst case: every slot on its own expert
+    worst = np.arange(T * k, dtype=np.int32).reshape(T, k) % E
+    assert int(O.align(worst, E, 128)["padded_offsets"][-1]) <= cap

@@ -39,15 +39,19 @@ def assert_no_device_error():
     assert mb.device_error(dev()) == 0
 
 
-@pytest.fixture(params=[1, 0], ids=["cta_pair", "single_cta"])
+@pytest.fixture(params=[(1, 1), (1, 0), (0, 1)], ids=["cta_pair", "cta_pair_no_half_units", "single_cta"])
 def gemm_variant(request):
-    """Runs a test with the CTA-pair (cta_group::2) GEMMs and again with one
-    CTA per tile."""
+    """Runs a test with the CTA-pair (cta_group::2) GEMMs — each expert's odd
+    last tile as an M=128 pair MMA (half unit), and as an M=256 one with half
+    of it idle — and with one CTA per tile."""
     lib = _lib.load()
-    old = lib.moe_get_option(_lib.OPT_GEMM_CTA_PAIR)
-    assert lib.moe_set_option(_lib.OPT_GEMM_CTA_PAIR, request.param) == 0
-    yield request.param
-    lib.moe_set_option(_lib.OPT_GEMM_CTA_PAIR, old)
+    pair, half = request.param
+    old = lib.moe_get_option(_lib.OPT_GEMM_CTA_PAIR), lib.moe_get_option(_lib.OPT_GEMM_HALF_UNITS)
+    assert lib.moe_set_option(_lib.OPT_GEMM_CTA_PAIR, pair) == 0
+    assert lib.moe_set_option(_lib.OPT_GEMM_HALF_UNITS, half) == 0
+    yield pair
+    lib.moe_set_option(_lib.OPT_GEMM_CTA_PAIR, old[0])
+    lib.moe_set_option(_lib.OPT_GEMM_HALF_UNITS, old[1])
 
 
 # --------------------------------------------------------------------------- tile schedule
@@ -208,6 +212,23 @@ def test_pre_routed_non_kmajor_weights_and_tail_rows(gemm_variant):
     ref = O.moe_mlp_grouped(npf(x), npf(w13), npf(w2), gs)
     assert max_abs_rel(npf(out), ref) < TOL
     assert (npf(out)[int(gs.sum()):] == 0).all()
+
+
+def test_pre_routed_odd_and_even_tile_counts(gemm_variant):
+    """Experts with odd and even numbers of 128-row tiles (and an empty one):
+    in a CTA pair each odd last tile is a half unit (64 rows per CTA), with
+    rows past the expert's end inside the tile."""
+    rng = np.random.default_rng(17)
+    E, H, I = 5, 512, 640
+    gs = np.array([128 * 3 + 5, 256, 7, 0, 128 * 4 + 100])  # 4, 2, 1, 0, 5 tiles
+    T = int(gs.sum())
+    x = torch.from_numpy(rng.standard_normal((T, H), dtype=np.float32)).to(dev(), torch.bfloat16)
+    w13 = (torch.randn(E, 2 * I, H, device=dev()) * 0.03).to(torch.bfloat16).transpose(1, 2)
+    w2 = (torch.randn(E, H, I, device=dev()) * 0.03).to(torch.bfloat16).transpose(1, 2)
+    out = mb.fused_moe_mlp(x, w13, w2, torch.from_numpy(gs).to(dev()))
+    ref = O.moe_mlp_grouped(npf(x), npf(w13), npf(w2), gs)
+    assert max_abs_rel(npf(out), ref) < TOL
+    assert_no_device_error()
 
 
 # --------------------------------------------------------------------------- top-k form
@@ -399,6 +420,22 @@ def test_cuda_graph_replay_matches_eager(T):
         # the fused combine adds the k expert rows with fp32 atomics, so two
         # runs can differ by the order of those additions (bf16 ulp level)
         assert max_abs_rel(npf(y), npf(y_ref)) < 2e-3
+    assert_no_device_error()
+
+
+def test_cuda_graph_replay_pair_gemms():
+    """A layer large enough for CTA pairs (experts with odd tile counts, so
+    half units too), captured once and replayed with new inputs."""
+    T, H, I, E, k = 2048, 1024, 1024, 4, 2  # ~1024 slots per expert: pairs, odd tile counts
+    x, w13, w2, ids, wts = topk_case(T, H, I, E, k, "uniform-softmax", torch.bfloat16, seed=3)
+    cap = mb.CapturedMoeMLP(w13, w2, T, k)
+    for seed in (4, 5):
+        x2, _, _, ids2, wts2 = topk_case(T, H, I, E, k, "uniform-softmax", torch.bfloat16, seed=seed)
+        y = cap(x2, torch.from_numpy(wts2).to(dev()), torch.from_numpy(ids2).to(dev())).clone()
+        y_ref = run_topk(x2, w13, w2, ids2, wts2)
+        assert max_abs_rel(npf(y), npf(y_ref)) < 2e-3
+        ref = O.moe_mlp_topk(npf(x2), npf(w13), npf(w2), wts2, ids2, round_hidden=O.round_bf16)
+        assert max_abs_rel(npf(y), ref) < TOL
     assert_no_device_error()
 
 
