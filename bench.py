@@ -433,21 +433,43 @@ def main():
     clocks = sampler.stop(t_region0, t_region1)
     launches = lib.moe_launch_count() - launches0
     ms = handles[0].elapsed_time(handles[1]) / args.steps
+    stage_rows = None
+    stage_source = "eager calls, stage events recorded by the library"
     if args.graph:
         # replays launch the captured kernels without going through the
-        # library; stage times come from an eager pass of the same op
+        # library. Stage times: a second capture of the same op with the
+        # library's stage events as graph nodes, replayed once per timed
+        # step right after the timed region
         launches = captured.kernels * args.steps
-        for i in range(args.steps):
-            lib.moe_set_stage_events(ev_arrays[i], STAGES)
-            mb.fused_moe_mlp(x, w13, w2, wts, ids, scales=scales)
-        lib.moe_set_stage_events(None, 0)
-        torch.cuda.synchronize()
+        try:
+            lib.moe_set_stage_events(ev_arrays[0], STAGES)
+            try:
+                cap_ev = mb.CapturedMoeMLP(w13, w2, T, k, dtype=dt, scales=scales)
+            finally:
+                lib.moe_set_stage_events(None, 0)
+            stage_rows = []
+            for i in range(args.steps):
+                cap_ev(x, wts, ids)
+                torch.cuda.synchronize()
+                stage_rows.append([ev[0][j].elapsed_time(ev[0][j + 1]) for j in range(STAGES - 1)])
+            del cap_ev
+            stage_source = "graph replay with the stage events as graph nodes"
+        except Exception:
+            stage_rows = None
+        if stage_rows is None:
+            for i in range(args.steps):
+                lib.moe_set_stage_events(ev_arrays[i], STAGES)
+                mb.fused_moe_mlp(x, w13, w2, wts, ids, scales=scales)
+            lib.moe_set_stage_events(None, 0)
+            torch.cuda.synchronize()
+    if stage_rows is None:
+        stage_rows = [[row[j].elapsed_time(row[j + 1]) for j in range(STAGES - 1)] for row in ev]
 
     def stage_ms(a, b):
-        return statistics.mean(row[a].elapsed_time(row[b]) for row in ev)
+        return statistics.mean(sum(r[a:b]) for r in stage_rows)
 
     st_ms = {"route": stage_ms(0, 1), "gather": stage_ms(1, 2), "gemm1": stage_ms(2, 3), "pre_gemm2": stage_ms(3, 4),
-             "gemm2": stage_ms(4, 5), "finalize": stage_ms(5, 6)}
+             "gemm2": stage_ms(4, 5), "finalize": stage_ms(5, 6), "source": stage_source}
     if world > 1:
         t = torch.tensor([ms], device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -549,24 +571,41 @@ def main():
     flops_step = 6.0 * S_local * H * I
     value = world * T / (ms / 1e3)
 
-    # yardstick: cuBLAS (torch.matmul) on a dense GEMM with the gate_up
-    # launch's shape [S, H] x [H, 2I], timed the same way right after
-    if world == 1 and not cfg["quant"] and cfg["dtype"] == "bf16":
-        a = torch.randn(S_local, H, device=device, dtype=dt)
-        b = torch.randn(H, 2 * I, device=device, dtype=dt)
+    # yardsticks: cuBLAS (torch.matmul / torch.bmm) on the gate_up launch's
+    # flops, timed the same way right after: one dense GEMM [S, H] x [H, 2I]
+    # (no expert boundaries, one weight matrix), and a batched GEMM with one
+    # weight matrix per expert and S / E rows each (the MoE launch's weight
+    # bytes, no routing imbalance, no padding)
+    def time_cublas(fn):
         for _ in range(3):
-            torch.matmul(a, b)
+            fn()
         c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         reps = max(3, args.steps)
         c0.record(stream)
         for _ in range(reps):
-            torch.matmul(a, b)
+            fn()
         c1.record(stream)
         torch.cuda.synchronize()
-        cub_ms = c0.elapsed_time(c1) / reps
+        return c0.elapsed_time(c1) / reps
+
+    if world == 1 and not cfg["quant"] and cfg["dtype"] == "bf16":
+        a = torch.randn(S_local, H, device=device, dtype=dt)
+        b = torch.randn(H, 2 * I, device=device, dtype=dt)
+        cub_ms = time_cublas(lambda: torch.matmul(a, b))
         roofline["cublas_dense_same_shape"] = {"ms": cub_ms, "tflops": flops_gemm1 / (cub_ms / 1e3) / 1e12,
                                                "ours_vs_cublas": cub_ms / st_ms["gemm1"]}
         del a, b
+        rows = S_local // E
+        if rows >= 128 and E * H * 2 * I * 2 <= 8 << 30:
+            a = torch.randn(E, rows, H, device=device, dtype=dt)
+            b = torch.randn(E, H, 2 * I, device=device, dtype=dt)
+            bmm_ms = time_cublas(lambda: torch.bmm(a, b))
+            bmm_flops = 2.0 * E * rows * H * 2 * I
+            roofline["cublas_batched_per_expert"] = {
+                "shape": f"{E} x [{rows}, {H}] x [{H}, {2 * I}]", "ms": bmm_ms,
+                "tflops": bmm_flops / (bmm_ms / 1e3) / 1e12,
+                "ours_vs_cublas": (flops_gemm1 / st_ms["gemm1"]) / (bmm_flops / bmm_ms)}
+            del a, b
 
     line = {"metric": "fused MoE MLP tokens/s", "value": value, "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
