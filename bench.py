@@ -299,6 +299,8 @@ def main():
     ap.add_argument("--gemm", default="auto", choices=["auto", "pair", "single"],
                     help="grouped GEMM variant: CTA pairs (cta_group::2), one CTA per tile, or chosen by size")
     ap.add_argument("--band", type=int, default=0, help="GEMM tile-order band width in M tiles (0: default)")
+    ap.add_argument("--pdl", type=int, default=1, choices=[0, 1],
+                    help="launch the kernels with programmatic dependent launch (1, default)")
     ap.add_argument("--half-units", type=int, default=1, choices=[0, 1],
                     help="CTA-pair GEMMs: each expert's odd last M tile as an M=128 pair MMA (1, default)")
     ap.add_argument("--eager", action="store_true",
@@ -320,7 +322,7 @@ def main():
     config_json = {"workload": cfg["desc"], "tokens_per_gpu": T, "hidden": H, "inter": I, "experts": E,
                    "top_k": k, "routing": cfg["routing"], "dtype": cfg["dtype"] + ("+w8a8" if cfg["quant"] else ""),
                    "parallelism": f"ep{world}" if world > 1 else "single", "gemm": args.gemm,
-                   "half_units": bool(args.half_units),
+                   "half_units": bool(args.half_units), "pdl": bool(args.pdl),
                    "ep_exchange": args.ep if world > 1 else None, "cuda_graph": bool(args.graph and world == 1),
                    "l2": "weights (%.2f GB) exceed the 126 MB L2, streamed every step" %
                          (E * 3 * H * I * (1 if cfg["quant"] else (4 if cfg["dtype"] == "fp32" else 2)) / 1e9)}
@@ -356,6 +358,7 @@ def main():
     if args.band:
         lib.moe_set_option(_lib.OPT_GEMM_BAND, args.band)
     lib.moe_set_option(_lib.OPT_GEMM_HALF_UNITS, args.half_units)
+    lib.moe_set_option(_lib.OPT_PDL, args.pdl)
 
     x, ids, wts, dt = make_inputs(cfg, rank, device)
     if world > 1:

@@ -99,7 +99,10 @@ typedef enum {
                                0 (default): whole tiles only */,
   MOE_OPT_GEMM_HALF_UNITS = 4 /* CTA pairs only. 1 (default): an expert's odd last M tile runs as one
                                M=128 pair MMA, 64 of its rows on each CTA; 0: as an M=256 pair MMA
-                               whose second CTA's rows are idle */
+                               whose second CTA's rows are idle */,
+  MOE_OPT_PDL = 5             /* 1 (default): kernels are launched with programmatic dependent launch,
+                               so each one's launch and prologue overlap the kernel before it in the
+                               stream (every kernel first waits for its predecessors' results); 0: off */
 } moe_option_t;
 MOE_API int moe_set_option(int option, int value);
 /* Current value of an option, or -1 for an unknown option. */

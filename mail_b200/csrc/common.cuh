@@ -95,6 +95,43 @@ int gemm2_scatter_peer(const void* h, int dtype, int64_t h_rows, int64_t inter, 
                        int64_t max_tiles, const int32_t* row_meta, void* const* peer_out, int num_peers,
                        int64_t peer_rows, int out_dtype, cudaStream_t stream);
 
+// Programmatic dependent launch (PDL). Every kernel of this library starts
+// with pdl_begin(): it waits until the grids launched before it in the stream
+// have completed and their memory is visible, then lets the next grid in the
+// stream be scheduled, so that grid's launch and prologue overlap this one.
+// A grid launched without the programmatic-serialisation attribute returns
+// from the wait at once. Nothing before the wait touches global memory.
+__device__ __forceinline__ void pdl_begin() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Whether launches carry the programmatic-serialisation attribute
+// (MOE_OPT_PDL, default on). Defined in moe_gemm.cu.
+bool pdl_enabled();
+
+// cudaLaunchKernelEx with the PDL attribute when enabled.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                          Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  if (pdl_enabled()) {
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
+// Zeroes `bytes` of device memory on `st` (a kernel launch: moe_rows.cu).
+int zero_fill(void* dst, size_t bytes, cudaStream_t st);
+
 inline int num_sms() {
   static int cache[64] = {0};
   int dev = 0;

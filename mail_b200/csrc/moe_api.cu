@@ -193,7 +193,7 @@ int run_experts(const ExpertsArgs& a) {
   const int g2_dtype = q ? MOE_I8 : h_dtype;
   if (a.mode == ExpertsOut::kCombineAtomic) {
     float* acc = (a.x_dtype == MOE_F32) ? static_cast<float*>(a.y) : reinterpret_cast<float*>(ws + w.y32);
-    MOE_CUDA_TRY(cudaMemsetAsync(acc, 0, (size_t)a.T * a.H * sizeof(float), st));
+    MOE_TRY(zero_fill(acc, (size_t)a.T * a.H * sizeof(float), st));
     MOE_TRY(record_stage(MOE_STAGE_PRE_GEMM2, st));
     MOE_TRY(moe_gemm2(a2, g2_dtype, w.cap, a.I, a.w2, a.E, a.H, hs, a.w2_scale, table, w.max_tiles,
                       MOE_EPI_COMBINE_ADD, sorted, a.topk_weights, a.k, acc, MOE_F32, a.T, stream));
@@ -261,7 +261,7 @@ extern "C" int moe_fused_mlp(const void* x, int dtype, int64_t num_tokens, int64
   MOE_TRY(moe_tile_schedule(group_sizes, gs_dtype, num_experts, num_tokens, block_m, nullptr, nullptr, nullptr,
                             table, stream));
   // the reference zero-initialises its output; rows no group covers stay 0
-  MOE_CUDA_TRY(cudaMemsetAsync(out, 0, (size_t)num_tokens * hidden * dtype_size(dtype), st));
+  MOE_TRY(zero_fill(out, (size_t)num_tokens * hidden * dtype_size(dtype), st));
   MOE_TRY(record_stage(MOE_STAGE_ROUTED, st));
   MOE_TRY(record_stage(MOE_STAGE_GATHERED, st));
   MOE_TRY(moe_gemm1_swiglu(x, dtype, num_tokens, hidden, w13, num_experts, inter, nullptr, nullptr, table, w.grid, h,

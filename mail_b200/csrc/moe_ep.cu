@@ -38,6 +38,7 @@ __global__ void __launch_bounds__(kPlanThreads) ep_plan_kernel(
     const int32_t* __restrict__ counts_all, int W, int r, int E, int EL, int BM, int32_t* __restrict__ dest_base,
     int32_t* __restrict__ table, int64_t max_tiles, int32_t* __restrict__ meta_local, int64_t recv_cap,
     const int32_t* __restrict__ slot_pos, int64_t S, int32_t* __restrict__ ret_pos) {
+  pdl_begin();
   extern __shared__ int32_t sm[];
   int32_t* pad = sm;       // [E]    padded totals, then their inclusive prefix
   int32_t* tcum = sm + E;  // [EL+1] tiles of this rank's local experts, prefix
@@ -129,6 +130,7 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(
     const int32_t* __restrict__ dest_base, const int32_t* __restrict__ n_valid_dev, int64_t max_rows, int EL,
     int rank, int64_t recv_cap, void* const* __restrict__ peer_x, float* const* __restrict__ peer_scale,
     int32_t* const* __restrict__ peer_meta, int* __restrict__ err) {
+  pdl_begin();
   const int lane = threadIdx.x & 31;
   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
@@ -249,9 +251,9 @@ extern "C" int moe_ep_plan(const int32_t* counts_all, int world, int rank, int n
   const size_t smem = (size_t)(num_experts + EL + 1) * sizeof(int32_t);
   if (smem > 48 * 1024)
     MOE_CUDA_TRY(cudaFuncSetAttribute(ep_plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  ep_plan_kernel<<<1, kPlanThreads, smem, as_stream(stream)>>>(counts_all, world, rank, num_experts, EL, kBlockM,
-                                                              dest_base, tile_table, max_tiles, recv_meta, recv_cap,
-                                                              slot_pos, num_slots, ret_pos);
+  MOE_CUDA_TRY(launch_kernel(ep_plan_kernel, dim3(1), dim3(kPlanThreads), smem, as_stream(stream),
+                             counts_all, world, rank, num_experts, EL, kBlockM, dest_base, tile_table,
+                             max_tiles, recv_meta, recv_cap, slot_pos, num_slots, ret_pos));
   MOE_LAUNCH_CHECK("ep_plan_kernel");
   return MOE_OK;
 }
@@ -272,11 +274,11 @@ extern "C" int moe_ep_dispatch(const void* x, int x_dtype, int64_t hidden, int t
   const int64_t cap = (int64_t)num_sms() * 16;
   if (blocks > cap) blocks = cap;
   cudaStream_t st = as_stream(stream);
-#define DISPATCH(TI, Q)                                                                                         \
-  ep_dispatch_kernel<TI, Q><<<(unsigned)blocks, 256, 0, st>>>(static_cast<const TI*>(x), hidden, top_k, topk_ids, \
-                                                              sorted_slots, seg_start, dest_base, n_valid_dev,   \
-                                                              max_rows, experts_per_rank, rank, recv_cap, peer_x, \
-                                                              peer_scale, peer_meta, err)
+#define DISPATCH(TI, Q)                                                                                   \
+  MOE_CUDA_TRY(launch_kernel(ep_dispatch_kernel<TI, Q>, dim3((unsigned)blocks), dim3(256), 0, st,         \
+                             static_cast<const TI*>(x), hidden, top_k, topk_ids, sorted_slots, seg_start, \
+                             dest_base, n_valid_dev, max_rows, experts_per_rank, rank, recv_cap, peer_x,  \
+                             peer_scale, peer_meta, err))
   if (recv_dtype == MOE_I8) {
     MOE_CHECK_ARG(peer_scale != nullptr, "moe_ep_dispatch: int8 receive buffers need scales");
     if (x_dtype == MOE_BF16) DISPATCH(__nv_bfloat16, true);

@@ -274,6 +274,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     ptx::prefetch_tmap(&tmap_b);
     if (SWIGLU && PAIR && p.half_units) ptx::prefetch_tmap(&tmap_b64);
   }
+  pdl_begin();  // the tile table and operands come from the grids before this one
   for (int i = threadIdx.x; i <= E; i += blockDim.x) s_cum[i] = p.table[TileTable::cum_off() + i];
   if constexpr (PAIR) {
     __syncthreads();
@@ -742,6 +743,8 @@ std::atomic<int> g_gemm_stream_k{0};
 // CTA pairs: an expert's odd last M tile as one M=128 pair MMA (64 rows per
 // CTA) instead of an M=256 one with one CTA's half idle.
 std::atomic<int> g_gemm_half_units{1};
+// Programmatic dependent launch for every kernel of the library.
+std::atomic<int> g_pdl{1};
 
 bool use_pair(int64_t max_tiles, int E, int64_t n_tiles) {
   const int v = g_gemm_cta_pair.load();
@@ -762,7 +765,7 @@ int launch_kind(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap&
   auto kfn = moe_gemm_kernel<KIND, SWIGLU, PAIR>;
   MOE_CUDA_TRY(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   cfg.blockDim = dim3(NUM_THREADS);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
@@ -785,6 +788,12 @@ int launch_kind(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap&
   }
   if (grid <= 0) return MOE_OK;
   cfg.gridDim = dim3((unsigned)grid);
+  if (pdl_enabled()) {
+    attr[cfg.numAttrs].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[cfg.numAttrs].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs += 1;
+  }
   MOE_CUDA_TRY(cudaLaunchKernelEx(&cfg, kfn, ta, tb, tb64, p));
   MOE_LAUNCH_CHECK("moe_gemm_kernel");
   return MOE_OK;
@@ -938,6 +947,8 @@ int gemm2_impl(const void* h, int dtype, int64_t h_rows, int64_t inter, const vo
 }
 }  // namespace
 
+bool pdl_enabled() { return g_pdl.load(std::memory_order_relaxed) != 0; }
+
 int gemm2_scatter_peer(const void* h, int dtype, int64_t h_rows, int64_t inter, const void* w2, int num_experts,
                        int64_t hidden, const float* h_scale, const float* w2_scale, const int32_t* tile_table,
                        int64_t max_tiles, const int32_t* row_meta, void* const* peer_out, int num_peers,
@@ -979,6 +990,10 @@ extern "C" int moe_set_option(int option, int value) {
     g_gemm_half_units.store(value != 0);
     return MOE_OK;
   }
+  if (option == MOE_OPT_PDL) {
+    g_pdl.store(value != 0);
+    return MOE_OK;
+  }
   return set_error(MOE_ERR_INVALID_ARG, "moe_set_option: unknown option %d", option);
 }
 
@@ -987,6 +1002,7 @@ extern "C" int moe_get_option(int option) {
   if (option == MOE_OPT_GEMM_BAND) return g_gemm_band.load();
   if (option == MOE_OPT_GEMM_STREAM_K) return g_gemm_stream_k.load();
   if (option == MOE_OPT_GEMM_HALF_UNITS) return g_gemm_half_units.load();
+  if (option == MOE_OPT_PDL) return g_pdl.load();
   return -1;
 }
 

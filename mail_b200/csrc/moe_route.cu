@@ -25,6 +25,7 @@ constexpr int kChunk = 256;  // slots per align chunk (one warp, 8 rounds)
 __global__ void __launch_bounds__(kScanThreads) tile_schedule_kernel(
     const void* __restrict__ gs_ptr, int gs_is64, int E, int BM, int64_t grid, int64_t* __restrict__ tile_expert,
     int64_t* __restrict__ tile_row_start, int64_t* __restrict__ tile_row_count, int32_t* __restrict__ table) {
+  pdl_begin();
   extern __shared__ int64_t sh[];
   int64_t* offsets = sh;          // [E+1]  offsets[e] = sum gs[<e]
   int64_t* tcum = sh + (E + 1);   // [E+1]  tiles_cumsum
@@ -83,6 +84,7 @@ __global__ void __launch_bounds__(kScanThreads) tile_schedule_kernel(
 // Align, pass 1: per-chunk histogram (key E collects ids outside [0, E)).
 __global__ void align_count_kernel(const int32_t* __restrict__ ids, int64_t S, int E,
                                    int32_t* __restrict__ chunk_hist) {
+  pdl_begin();
   extern __shared__ int32_t hist[];  // [E+1]
   const int lane = threadIdx.x;
   for (int e = lane; e <= E; e += 32) hist[e] = 0;
@@ -109,6 +111,7 @@ __global__ void __launch_bounds__(kScanThreads) align_colscan_kernel(const int32
                                                                      int num_chunks, int E,
                                                                      int32_t* __restrict__ chunk_base,
                                                                      int32_t* __restrict__ totals) {
+  pdl_begin();
   __shared__ int32_t warp_sums[32];
   const int e = blockIdx.x;  // 0..E (E = dropped column)
   int32_t carry = 0;
@@ -130,6 +133,7 @@ __global__ void __launch_bounds__(kScanThreads) align_colscan_kernel(const int32
 __global__ void __launch_bounds__(kScanThreads) align_finalize_kernel(
     const int32_t* __restrict__ totals, int E, int BM, int64_t max_tiles, int32_t* __restrict__ group_sizes,
     int32_t* __restrict__ padded_offsets, int32_t* __restrict__ table, int32_t* __restrict__ sorted_slots) {
+  pdl_begin();
   extern __shared__ int32_t sm[];
   int32_t* poff = sm;            // [E+1] padded offsets (exclusive)
   int32_t* tcum = sm + (E + 1);  // [E+1] tile cumsum (exclusive)
@@ -181,6 +185,7 @@ __global__ void align_scatter_kernel(const int32_t* __restrict__ ids, int64_t S,
                                      const int32_t* __restrict__ chunk_base,
                                      const int32_t* __restrict__ padded_offsets,
                                      int32_t* __restrict__ sorted_slots, int32_t* __restrict__ slot_pos) {
+  pdl_begin();
   extern __shared__ int32_t run[];  // [E]
   const int lane = threadIdx.x;
   const int32_t* cb = chunk_base + (int64_t)blockIdx.x * (E + 1);
@@ -221,6 +226,7 @@ __global__ void __launch_bounds__(kScanThreads) align_small_kernel(
     const int32_t* __restrict__ ids, int64_t S, int E, int BM, int64_t max_tiles, int32_t* __restrict__ sorted_slots,
     int32_t* __restrict__ slot_pos, int32_t* __restrict__ group_sizes, int32_t* __restrict__ padded_offsets,
     int32_t* __restrict__ table) {
+  pdl_begin();
   extern __shared__ int32_t sm[];
   constexpr int W = kScanThreads / 32;
   const int E1 = E + 1;
@@ -336,6 +342,7 @@ template <typename T, int PER>
 __global__ void __launch_bounds__(256) route_topk_kernel(const T* __restrict__ logits, int64_t num_tokens, int E,
                                                          int k, int sigmoid, int renormalize,
                                                          int32_t* __restrict__ ids, float* __restrict__ wts) {
+  pdl_begin();
   const int lane = threadIdx.x & 31;
   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
@@ -422,14 +429,14 @@ extern "C" int moe_route_topk(const void* logits, int dtype, int64_t num_tokens,
   if (blocks > cap) blocks = cap;
   cudaStream_t st = as_stream(stream);
   const int sig = scoring == MOE_SCORE_SIGMOID;
-#define ROUTE(TT, PER)                                                                                      \
-  route_topk_kernel<TT, PER><<<(unsigned)blocks, 256, 0, st>>>(static_cast<const TT*>(logits), num_tokens, \
-                                                               num_experts, top_k, sig, renormalize != 0,  \
-                                                               topk_ids, topk_weights)
-#define ROUTE_T(TT)                                        \
-  if (num_experts <= 32) ROUTE(TT, 1);                     \
-  else if (num_experts <= 128) ROUTE(TT, 4);               \
-  else if (num_experts <= 256) ROUTE(TT, 8);               \
+#define ROUTE(TT, PER)                                                                             \
+  MOE_CUDA_TRY(launch_kernel(route_topk_kernel<TT, PER>, dim3((unsigned)blocks), dim3(256), 0, st, \
+                             static_cast<const TT*>(logits), num_tokens, num_experts, top_k, sig,  \
+                             renormalize != 0, topk_ids, topk_weights))
+#define ROUTE_T(TT)                          \
+  if (num_experts <= 32) ROUTE(TT, 1);       \
+  else if (num_experts <= 128) ROUTE(TT, 4); \
+  else if (num_experts <= 256) ROUTE(TT, 8); \
   else ROUTE(TT, kRouteMaxPerLane);
   if (dtype == MOE_F32) {
     ROUTE_T(float)
@@ -468,9 +475,9 @@ extern "C" int moe_tile_schedule(const void* group_sizes, int gs_dtype, int num_
   const size_t smem = 2 * (num_experts + 1) * sizeof(int64_t);
   if (smem > 48 * 1024)
     MOE_CUDA_TRY(cudaFuncSetAttribute(tile_schedule_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  tile_schedule_kernel<<<1, kScanThreads, smem, as_stream(stream)>>>(group_sizes, gs_dtype == MOE_I64, num_experts,
-                                                                     block_m, grid, tile_expert, tile_row_start,
-                                                                     tile_row_count, tile_table);
+  MOE_CUDA_TRY(launch_kernel(tile_schedule_kernel, dim3(1), dim3(kScanThreads), smem, as_stream(stream),
+                             group_sizes, gs_dtype == MOE_I64, num_experts, block_m, grid, tile_expert,
+                             tile_row_start, tile_row_count, tile_table));
   MOE_LAUNCH_CHECK("tile_schedule_kernel");
   return MOE_OK;
 }
@@ -527,9 +534,9 @@ extern "C" int moe_align(const int32_t* topk_ids, int64_t num_tokens, int top_k,
     const size_t smem = ((size_t)(kScanThreads / 32) + 3) * (num_experts + 1) * sizeof(int32_t);
     if (smem > 48 * 1024)
       MOE_CUDA_TRY(cudaFuncSetAttribute(align_small_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    align_small_kernel<<<1, kScanThreads, smem, as_stream(stream)>>>(topk_ids, S, num_experts, block_m, max_tiles_s,
-                                                                     sorted_slots, slot_pos, group_sizes,
-                                                                     padded_offsets, tile_table);
+    MOE_CUDA_TRY(launch_kernel(align_small_kernel, dim3(1), dim3(kScanThreads), smem, as_stream(stream),
+                               topk_ids, S, num_experts, block_m, max_tiles_s, sorted_slots, slot_pos,
+                               group_sizes, padded_offsets, tile_table));
     MOE_LAUNCH_CHECK("align_small_kernel");
     return MOE_OK;
   }
@@ -541,17 +548,20 @@ extern "C" int moe_align(const int32_t* topk_ids, int64_t num_tokens, int top_k,
   const int64_t max_tiles = moe_align_capacity(S, num_experts, block_m) / block_m;
   const size_t hsmem = (num_experts + 1) * sizeof(int32_t);
   if (w.chunks > 0) {
-    align_count_kernel<<<(unsigned)w.chunks, 32, hsmem, st>>>(topk_ids, S, num_experts, hist);
+    MOE_CUDA_TRY(launch_kernel(align_count_kernel, dim3((unsigned)w.chunks), dim3(32), hsmem, st,
+                               topk_ids, S, num_experts, hist));
     MOE_LAUNCH_CHECK("align_count_kernel");
   }
-  align_colscan_kernel<<<num_experts + 1, kScanThreads, 0, st>>>(hist, (int)w.chunks, num_experts, base, totals);
+  MOE_CUDA_TRY(launch_kernel(align_colscan_kernel, dim3(num_experts + 1), dim3(kScanThreads), 0, st,
+                             hist, (int)w.chunks, num_experts, base, totals));
   MOE_LAUNCH_CHECK("align_colscan_kernel");
-  align_finalize_kernel<<<1, kScanThreads, 2 * hsmem, st>>>(totals, num_experts, block_m, max_tiles, group_sizes,
-                                                            padded_offsets, tile_table, sorted_slots);
+  MOE_CUDA_TRY(launch_kernel(align_finalize_kernel, dim3(1), dim3(kScanThreads), 2 * hsmem, st,
+                             totals, num_experts, block_m, max_tiles, group_sizes, padded_offsets, tile_table,
+                             sorted_slots));
   MOE_LAUNCH_CHECK("align_finalize_kernel");
   if (w.chunks > 0) {
-    align_scatter_kernel<<<(unsigned)w.chunks, 32, hsmem, st>>>(topk_ids, S, num_experts, base, padded_offsets,
-                                                                sorted_slots, slot_pos);
+    MOE_CUDA_TRY(launch_kernel(align_scatter_kernel, dim3((unsigned)w.chunks), dim3(32), hsmem, st,
+                               topk_ids, S, num_experts, base, padded_offsets, sorted_slots, slot_pos));
     MOE_LAUNCH_CHECK("align_scatter_kernel");
   }
   return MOE_OK;
@@ -615,17 +625,20 @@ extern "C" int moe_align_static(const int32_t* topk_ids, int64_t num_tokens, int
   const int64_t max_tiles = moe_align_capacity(S, num_experts, block_m) / block_m;
   const size_t hsmem = (num_experts + 1) * sizeof(int32_t);
   if (w.chunks > 0) {
-    align_count_kernel<<<(unsigned)w.chunks, 32, hsmem, st>>>(topk_ids, S, num_experts, hist);
+    MOE_CUDA_TRY(launch_kernel(align_count_kernel, dim3((unsigned)w.chunks), dim3(32), hsmem, st,
+                               topk_ids, S, num_experts, hist));
     MOE_LAUNCH_CHECK("align_count_kernel");
   }
-  align_colscan_kernel<<<num_experts + 1, kScanThreads, 0, st>>>(hist, (int)w.chunks, num_experts, base, totals);
+  MOE_CUDA_TRY(launch_kernel(align_colscan_kernel, dim3(num_experts + 1), dim3(kScanThreads), 0, st,
+                             hist, (int)w.chunks, num_experts, base, totals));
   MOE_LAUNCH_CHECK("align_colscan_kernel");
-  align_finalize_kernel<<<1, kScanThreads, 2 * hsmem, st>>>(totals, num_experts, block_m, max_tiles, group_sizes,
-                                                            padded_offsets, tile_table, sorted_slots);
+  MOE_CUDA_TRY(launch_kernel(align_finalize_kernel, dim3(1), dim3(kScanThreads), 2 * hsmem, st,
+                             totals, num_experts, block_m, max_tiles, group_sizes, padded_offsets, tile_table,
+                             sorted_slots));
   MOE_LAUNCH_CHECK("align_finalize_kernel");
   if (w.chunks > 0) {
-    align_scatter_kernel<<<(unsigned)w.chunks, 32, hsmem, st>>>(topk_ids, S, num_experts, base, padded_offsets,
-                                                                sorted_slots, slot_pos);
+    MOE_CUDA_TRY(launch_kernel(align_scatter_kernel, dim3((unsigned)w.chunks), dim3(32), hsmem, st,
+                               topk_ids, S, num_experts, base, padded_offsets, sorted_slots, slot_pos));
     MOE_LAUNCH_CHECK("align_scatter_kernel");
   }
   return MOE_OK;

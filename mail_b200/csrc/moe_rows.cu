@@ -101,6 +101,7 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const Tin* __restrict_
                                                           const int32_t* __restrict__ slots, int top_k,
                                                           int64_t rows, const int32_t* __restrict__ rows_dev,
                                                           Tout* __restrict__ dst, float* __restrict__ dst_scale) {
+  pdl_begin();
   const int lane = threadIdx.x & 31;
   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
@@ -158,6 +159,7 @@ __global__ void __launch_bounds__(kQuantThreads) gather_quant_kernel(const Tin* 
                                                                      const int32_t* __restrict__ rows_dev,
                                                                      int8_t* __restrict__ dst,
                                                                      float* __restrict__ dst_scale) {
+  pdl_begin();
   constexpr int kRowsPerPass = kQuantThreads / RT;
   constexpr int kWarpsPerRow = RT / 32;
   __shared__ float red[kQuantThreads / 32];
@@ -214,6 +216,7 @@ __global__ void __launch_bounds__(256) combine_rows_kernel(const To* __restrict_
                                                            const int32_t* __restrict__ slot_pos,
                                                            const float* __restrict__ w, int64_t T, int k,
                                                            Tacc* __restrict__ y) {
+  pdl_begin();
   const int lane = threadIdx.x & 31;
   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
@@ -237,6 +240,7 @@ __global__ void __launch_bounds__(256) combine_rows_kernel(const To* __restrict_
 template <typename Tout>
 __global__ void __launch_bounds__(256) convert_f32_kernel(const float* __restrict__ src, int64_t n8,
                                                           Tout* __restrict__ dst) {
+  pdl_begin();
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += (int64_t)gridDim.x * blockDim.x) {
     float v[8];
     load8(src + i * 8, v);
@@ -252,7 +256,30 @@ unsigned row_grid(int64_t rows) {
   return (unsigned)(blocks < 1 ? 1 : blocks);
 }
 
+// Zero fill of n16 16-byte words (a kernel rather than a memset so that it
+// takes part in programmatic dependent launch).
+__global__ void __launch_bounds__(256) zero16_kernel(uint4* __restrict__ dst, int64_t n16) {
+  pdl_begin();
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n16; i += (int64_t)gridDim.x * blockDim.x)
+    dst[i] = make_uint4(0u, 0u, 0u, 0u);
+}
+
 }  // namespace
+
+int zero_fill(void* dst, size_t bytes, cudaStream_t st) {
+  if (bytes == 0) return MOE_OK;
+  if ((uintptr_t)dst % 16 != 0 || bytes % 16 != 0) {  // not the case for the library's own buffers
+    MOE_CUDA_TRY(cudaMemsetAsync(dst, 0, bytes, st));
+    return MOE_OK;
+  }
+  const int64_t n16 = (int64_t)(bytes / 16);
+  int64_t blocks = ceil_div(n16, 256 * 4);
+  const int64_t cap = (int64_t)num_sms() * 8;
+  if (blocks > cap) blocks = cap;
+  MOE_CUDA_TRY(launch_kernel(zero16_kernel, dim3((unsigned)blocks), dim3(256), 0, st, static_cast<uint4*>(dst), n16));
+  MOE_LAUNCH_CHECK("zero16_kernel");
+  return MOE_OK;
+}
 }  // namespace moe
 
 using namespace moe;
@@ -264,13 +291,15 @@ extern "C" int moe_gather_rows(const void* src, int src_dtype, int64_t cols, con
   MOE_CHECK_ARG(cols > 0 && cols % 8 == 0, "moe_gather_rows: cols (%lld) must be a positive multiple of 8",
                 (long long)cols);
   MOE_CHECK_ARG(top_k > 0 && rows >= 0, "moe_gather_rows: bad top_k/rows");
-  MOE_CHECK_ARG(((uintptr_t)src % 16 == 0) && ((uintptr_t)dst % 16 == 0), "moe_gather_rows: pointers must be 16-byte aligned");
+  MOE_CHECK_ARG(((uintptr_t)src % 16 == 0) && ((uintptr_t)dst % 16 == 0),
+                "moe_gather_rows: pointers must be 16-byte aligned");
   if (rows == 0) return MOE_OK;
   cudaStream_t st = as_stream(stream);
   const unsigned grid = row_grid(rows);
-#define GATHER(TI, TO)                                                                                     \
-  gather_rows_kernel<TI, TO><<<grid, 256, 0, st>>>(static_cast<const TI*>(src), cols, sorted_slots, top_k, \
-                                                   rows, rows_dev, static_cast<TO*>(dst), dst_scale)
+#define GATHER(TI, TO)                                                                               \
+  MOE_CUDA_TRY(launch_kernel(gather_rows_kernel<TI, TO>, dim3(grid), dim3(256), 0, st,               \
+                             static_cast<const TI*>(src), cols, sorted_slots, top_k, rows, rows_dev, \
+                             static_cast<TO*>(dst), dst_scale))
   if (dst_dtype == src_dtype) {
     if (src_dtype == MOE_BF16) GATHER(__nv_bfloat16, __nv_bfloat16);
     else if (src_dtype == MOE_F16) GATHER(__half, __half);
@@ -283,12 +312,12 @@ extern "C" int moe_gather_rows(const void* src, int src_dtype, int64_t cols, con
       int64_t blocks = ceil_div(rows, kQuantThreads / rt);
       const int64_t cap = (int64_t)num_sms() * 16;
       if (blocks > cap) blocks = cap;
-#define GATHER_Q(TI, RT)                                                                                        \
-  gather_quant_kernel<TI, RT><<<(unsigned)blocks, kQuantThreads, 0, st>>>(static_cast<const TI*>(src), cols,   \
-                                                                         sorted_slots, top_k, rows, rows_dev, \
-                                                                         static_cast<int8_t*>(dst), dst_scale)
-#define GATHER_QT(TI)           \
-  if (rt == 32) GATHER_Q(TI, 32); \
+#define GATHER_Q(TI, RT)                                                                                      \
+  MOE_CUDA_TRY(launch_kernel(gather_quant_kernel<TI, RT>, dim3((unsigned)blocks), dim3(kQuantThreads), 0, st, \
+                             static_cast<const TI*>(src), cols, sorted_slots, top_k, rows, rows_dev,          \
+                             static_cast<int8_t*>(dst), dst_scale))
+#define GATHER_QT(TI)                  \
+  if (rt == 32) GATHER_Q(TI, 32);      \
   else if (rt == 64) GATHER_Q(TI, 64); \
   else GATHER_Q(TI, 128);
       if (src_dtype == MOE_BF16) {
@@ -332,8 +361,9 @@ extern "C" int moe_combine_rows(const void* o, int o_dtype, int64_t hidden, cons
   cudaStream_t st = as_stream(stream);
   const unsigned grid = row_grid(num_tokens);
 #define COMBINE(TO, TY)                                                                                    \
-  combine_rows_kernel<TO, TY><<<grid, 256, 0, st>>>(static_cast<const TO*>(o), hidden, slot_pos, topk_weights, \
-                                                    num_tokens, top_k, static_cast<TY*>(y))
+  MOE_CUDA_TRY(launch_kernel(combine_rows_kernel<TO, TY>, dim3(grid), dim3(256), 0, st,                    \
+                             static_cast<const TO*>(o), hidden, slot_pos, topk_weights, num_tokens, top_k, \
+                             static_cast<TY*>(y)))
   if (o_dtype == MOE_BF16 && y_dtype == MOE_BF16) COMBINE(__nv_bfloat16, __nv_bfloat16);
   else if (o_dtype == MOE_F16 && y_dtype == MOE_F16) COMBINE(__half, __half);
   else if (o_dtype == MOE_F32 && y_dtype == MOE_F32) COMBINE(float, float);
@@ -354,11 +384,14 @@ extern "C" int moe_convert_f32(const float* src, int64_t n, void* dst, int dst_d
   const int64_t cap = (int64_t)num_sms() * 8;
   if (blocks > cap) blocks = cap;
   if (dst_dtype == MOE_BF16)
-    convert_f32_kernel<__nv_bfloat16><<<(unsigned)blocks, 256, 0, st>>>(src, n8, static_cast<__nv_bfloat16*>(dst));
+    MOE_CUDA_TRY(launch_kernel(convert_f32_kernel<__nv_bfloat16>, dim3((unsigned)blocks), dim3(256), 0, st,
+                               src, n8, static_cast<__nv_bfloat16*>(dst)));
   else if (dst_dtype == MOE_F16)
-    convert_f32_kernel<__half><<<(unsigned)blocks, 256, 0, st>>>(src, n8, static_cast<__half*>(dst));
+    MOE_CUDA_TRY(launch_kernel(convert_f32_kernel<__half>, dim3((unsigned)blocks), dim3(256), 0, st,
+                               src, n8, static_cast<__half*>(dst)));
   else if (dst_dtype == MOE_F32)
-    convert_f32_kernel<float><<<(unsigned)blocks, 256, 0, st>>>(src, n8, static_cast<float*>(dst));
+    MOE_CUDA_TRY(launch_kernel(convert_f32_kernel<float>, dim3((unsigned)blocks), dim3(256), 0, st,
+                               src, n8, static_cast<float*>(dst)));
   else
     return set_error(MOE_ERR_UNSUPPORTED, "moe_convert_f32: dtype %d not supported", dst_dtype);
   MOE_LAUNCH_CHECK("convert_f32_kernel");

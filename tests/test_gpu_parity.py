@@ -389,8 +389,37 @@ def test_launch_counter_counts_kernels():
     lib = _lib.load()
     before = lib.moe_launch_count()
     run_topk(x, w13, w2, ids, wts)
-    # align (one kernel for up to 16384 slots) + gather + gemm1 + gemm2 + convert
-    assert lib.moe_launch_count() - before == 5
+    # align (one kernel for up to 16384 slots) + gather + gemm1 + output clear
+    # + gemm2 + convert
+    assert lib.moe_launch_count() - before == 6
+
+
+@pytest.mark.parametrize("T", [1, 256])
+def test_programmatic_dependent_launch_matches_serial(T):
+    """Kernels chained by programmatic dependent launch (the default) give the
+    results of plain stream-ordered launches: every kernel waits for its
+    predecessors before touching memory."""
+    lib = _lib.load()
+    H, I, E, k = 2048, 768, 128, 8
+    x, w13, w2, ids, wts = topk_case(T, H, I, E, k, "zipf1.2", torch.bfloat16, seed=40 + T)
+    gs = torch.from_numpy(np.bincount(ids.reshape(-1), minlength=E)).to(dev())
+    order = np.argsort(ids.reshape(-1), kind="stable")
+    xg = x[torch.from_numpy(order // k).to(dev())].contiguous()
+    outs = {}
+    for pdl in (1, 0):
+        assert lib.moe_set_option(_lib.OPT_PDL, pdl) == 0
+        try:
+            ys = [run_topk(x, w13, w2, ids, wts) for _ in range(3)]  # back to back on one stream
+            pre = mb.fused_moe_mlp(xg, w13, w2, gs)
+        finally:
+            lib.moe_set_option(_lib.OPT_PDL, 1)
+        outs[pdl] = (ys, pre)
+    ref = O.moe_mlp_topk(npf(x), npf(w13), npf(w2), wts, ids, round_hidden=O.round_bf16)
+    for y in outs[1][0] + outs[0][0]:
+        assert max_abs_rel(npf(y), ref) < TOL
+    # the pre-routed form has no atomics: bit-identical with and without
+    assert torch.equal(outs[1][1], outs[0][1])
+    assert_no_device_error()
 
 
 def test_bounded_wait_expires_and_context_survives():
