@@ -364,6 +364,7 @@ def main():
     if world > 1:
         from mail_b200 import ep as mep
         assert E % world == 0, "experts must divide evenly over ranks"
+        args.graph = False  # the expert-parallel layer is called directly (host-side plan per call)
         local = list(range(rank * E // world, (rank + 1) * E // world))
         w13, w2, scales = make_weights(cfg, local, device, dt)
         if args.ep == "peer":
