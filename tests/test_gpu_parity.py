@@ -447,8 +447,10 @@ def test_cuda_graph_replay_matches_eager(T):
         y = cap(x2, torch.from_numpy(wts2).to(dev()), torch.from_numpy(ids2).to(dev())).clone()
         y_ref = run_topk(x2, w13, w2, ids2, wts2)
         # the fused combine adds the k expert rows with fp32 atomics, so two
-        # runs can differ by the order of those additions (bf16 ulp level)
-        assert max_abs_rel(npf(y), npf(y_ref)) < 2e-3
+        # runs can differ by the order of those additions: after the bf16
+        # rounding, by one rounding step (2^-8 of an element, bounded here
+        # by 2^-7 of the largest)
+        assert max_abs_rel(npf(y), npf(y_ref)) <= 2.0 ** -7
     assert_no_device_error()
 
 
@@ -462,7 +464,7 @@ def test_cuda_graph_replay_pair_gemms():
         x2, _, _, ids2, wts2 = topk_case(T, H, I, E, k, "uniform-softmax", torch.bfloat16, seed=seed)
         y = cap(x2, torch.from_numpy(wts2).to(dev()), torch.from_numpy(ids2).to(dev())).clone()
         y_ref = run_topk(x2, w13, w2, ids2, wts2)
-        assert max_abs_rel(npf(y), npf(y_ref)) < 2e-3
+        assert max_abs_rel(npf(y), npf(y_ref)) <= 2.0 ** -7  # fp32 atomic order, as above
         ref = O.moe_mlp_topk(npf(x2), npf(w13), npf(w2), wts2, ids2, round_hidden=O.round_bf16)
         assert max_abs_rel(npf(y), ref) < TOL
     assert_no_device_error()
