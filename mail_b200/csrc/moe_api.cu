@@ -144,7 +144,7 @@ int check_experts(const ExpertsArgs& a) {
   MOE_CHECK_ARG(!(a.w_dtype == MOE_I8 && a.x_dtype == MOE_F32), "%s: w8a8 takes bf16/fp16 activations", a.name);
   if (a.w_dtype == MOE_I8) MOE_CHECK_ARG(a.w13_scale && a.w2_scale, "%s: int8 weights need scales", a.name);
   MOE_CHECK_ARG(a.T >= 0 && a.H > 0 && a.I > 0 && a.E > 0 && a.k > 0, "%s: bad sizes", a.name);
-  MOE_CHECK_ARG(a.y != nullptr, "%s: output is NULL", a.name);
+  MOE_CHECK_ARG(a.T == 0 || a.y != nullptr, "%s: output is NULL", a.name);  // empty batch: nothing to write
   return MOE_OK;
 }
 
@@ -248,8 +248,8 @@ extern "C" int moe_fused_mlp(const void* x, int dtype, int64_t num_tokens, int64
                 "moe_fused_mlp: dtype must be bf16, fp16 or fp32");
   MOE_CHECK_ARG(block_m == kBlockM, "moe_fused_mlp: block_m must be %d on sm_100a (got %d)", kBlockM, block_m);
   MOE_CHECK_ARG(num_tokens >= 0 && hidden > 0 && inter > 0 && num_experts > 0, "moe_fused_mlp: bad sizes");
-  MOE_CHECK_ARG(out != nullptr, "moe_fused_mlp: out is NULL");
-  if (num_tokens == 0) return MOE_OK;
+  MOE_CHECK_ARG(num_tokens == 0 || out != nullptr, "moe_fused_mlp: out is NULL");
+  if (num_tokens == 0) return MOE_OK;  // empty batch: empty output, as the reference returns
   const FusedMlpWs w = fused_mlp_ws(num_tokens, inter, num_experts, dtype, block_m);
   if (workspace_bytes < w.bytes || !workspace)
     return set_error(MOE_ERR_WORKSPACE, "moe_fused_mlp: workspace %zu < %zu bytes", workspace_bytes, w.bytes);

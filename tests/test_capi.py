@@ -63,6 +63,18 @@ def test_invalid_arguments_are_rejected_on_host(call, needle):
     assert needle in lib.moe_last_error().decode()
 
 
+def test_empty_batch_is_a_no_op():
+    """Zero tokens: both fused entry points return OK without touching any
+    buffer (all NULL here) and without launching work."""
+    lib = _lib.load()
+    before = lib.moe_launch_count()
+    assert lib.moe_fused_experts(None, _lib.BF16, 0, 64, None, None, _lib.BF16, 4, 64, None, None, 2, None, None,
+                                 None, None, 0, None) == 0
+    assert lib.moe_fused_mlp(None, _lib.BF16, 0, 64, None, None, 4, 64, None, _lib.I64, 128, None, None, 0,
+                             None) == 0
+    assert lib.moe_launch_count() == before
+
+
 def test_python_wrapper_raises_without_cuda_tensors():
     torch = pytest.importorskip("torch")
     import mail_b200

@@ -268,6 +268,39 @@ def test_topk_matches_oracle(T, H, I, E, k, routing, dtype, gemm_variant):
     assert_no_device_error()
 
 
+def test_topk_max_experts(gemm_variant):
+    """1024 experts (the GEMMs' and router's limit), 8 per token, through the
+    GPU router and the fused op."""
+    T, H, I, E, k = 96, 256, 128, 1024, 8
+    rng = np.random.default_rng(11)
+    x = torch.from_numpy(rng.standard_normal((T, H), dtype=np.float32)).to(dev(), torch.bfloat16)
+    w13 = (torch.randn(E, 2 * I, H, device=dev()) * 0.05).to(torch.bfloat16).transpose(1, 2)
+    w2 = (torch.randn(E, H, I, device=dev()) * 0.05).to(torch.bfloat16).transpose(1, 2)
+    logits = torch.from_numpy(rng.standard_normal((T, E), dtype=np.float32)).to(dev())
+    ids, wts = mb.route_topk(logits, top_k=k)
+    ids_ref, _ = O.route_topk(npf(logits), k, "softmax")
+    np.testing.assert_array_equal(ids.cpu().numpy(), ids_ref)
+    y = mb.fused_moe_mlp(x, w13, w2, wts, ids)
+    ref = O.moe_mlp_topk(npf(x), npf(w13), npf(w2), wts.cpu().numpy(), ids.cpu().numpy(), round_hidden=O.round_bf16)
+    assert max_abs_rel(npf(y), ref) < TOL
+    assert_no_device_error()
+
+
+def test_empty_batch_returns_empty():
+    """Zero tokens in either form: an empty [0, H] output, as the reference
+    returns for an empty batch."""
+    E, H, I = 4, 256, 128
+    w13 = (torch.randn(E, 2 * I, H, device=dev()) * 0.05).to(torch.bfloat16).transpose(1, 2)
+    w2 = (torch.randn(E, H, I, device=dev()) * 0.05).to(torch.bfloat16).transpose(1, 2)
+    x = torch.empty((0, H), dtype=torch.bfloat16, device=dev())
+    y = mb.fused_moe_mlp(x, w13, w2, torch.empty((0, 2), device=dev()),
+                         torch.empty((0, 2), dtype=torch.int32, device=dev()))
+    assert tuple(y.shape) == (0, H)
+    y = mb.fused_moe_mlp(x, w13, w2, torch.zeros(E, dtype=torch.int64, device=dev()))
+    assert tuple(y.shape) == (0, H)
+    assert_no_device_error()
+
+
 def test_topk_drops_out_of_range_ids(gemm_variant):
     x, w13, w2, ids, wts = topk_case(128, 256, 128, 4, 2, "uniform-softmax", torch.bfloat16)
     ids = ids.copy()
