@@ -563,7 +563,9 @@ def main():
                 "bound": "tensor" if tensor_bound else "hbm",
                 "flops_per_launch": flops_gemm1, "bytes_per_launch": bytes_gemm1, "active_experts": active,
                 "ms_per_launch": st_ms["gemm1"],
-                "traffic": load_traffic(args.config) if not args.tokens else None, "traffic_unit": "bytes"}
+                # the committed capture is of the one-GPU launch at the default size
+                "traffic": load_traffic(args.config) if not args.tokens and world == 1 else None,
+                "traffic_unit": "bytes"}
     if tensor_bound:
         roofline.update(achieved=flops_gemm1 / gemm1_s / 1e12, peak=peak_tc, unit="TFLOP/s",
                         frac=flops_gemm1 / gemm1_s / 1e12 / peak_tc,
@@ -572,6 +574,10 @@ def main():
     else:
         roofline.update(achieved=bytes_gemm1 / gemm1_s / 1e9, peak=peaks["hbm"], unit="GB/s",
                         frac=bytes_gemm1 / gemm1_s / 1e9 / peaks["hbm"], peak_source=f"{peaks['source']} HBM copy")
+    # the same against NVIDIA's dense spec figures (2.25 PFLOP/s bf16, 4.5 POP/s
+    # int8, 7.7 TB/s HBM3e), for context
+    spec = (4500.0 if cfg["quant"] else 2250.0) if tensor_bound else 7700.0
+    roofline.update(spec_peak=spec, frac_of_spec=roofline["achieved"] / spec)
     flops_step = 6.0 * S_local * H * I
     value = world * T / (ms / 1e3)
 

@@ -9,12 +9,14 @@
 // _grouped_gemm2_kernel (partially_fused_moe_mlp_triton.py:59-162) and the two
 // halves of _fused_moe_mlp_kernel (fused_moe_mlp_triton.py:35-88).
 //
-// CTA layout (192 threads, one CTA per SM):
-//   warp 0      TMA producer: A tile (128 rows x 128 B) + B tile (256 rows x
-//               128 B) per stage, 128B-swizzled, 4-stage ring in shared memory
-//   warp 1      TMEM allocator + single-thread tcgen05.mma issuer
-//               (M=128, N=256, K=32 bytes per instruction) into one of two
-//               256-column fp32/int32 accumulators in tensor memory
+// CTA layout (192 threads, one CTA per SM; two variants, see Cfg):
+//   warp 0      TMA producer, 128B-swizzled ring in shared memory. One CTA per
+//               tile: A (128 rows x 128 B) + B (256 rows x 128 B) per stage,
+//               4 stages. CTA pair: each CTA its own 128 A rows + half of B
+//               (128 rows), 6 stages, both counted on the leader's barrier.
+//   warp 1      TMEM allocator + single-thread tcgen05.mma issuer (M=128 or,
+//               for a pair, M=256 / M=128; N=256; K=32 bytes per instruction)
+//               into one of two 256-column fp32/int32 accumulators
 //   warps 2..5  epilogue: tcgen05.ld of the accumulator (warp w reads TMEM
 //               lanes 32*(w%4)..+31), fused SwiGLU / dequant / combine, stores
 // The two accumulators let the epilogue of tile i overlap the MMAs of tile
