@@ -132,6 +132,10 @@ cudaError_t launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_
 // Zeroes `bytes` of device memory on `st` (a kernel launch: moe_rows.cu).
 int zero_fill(void* dst, size_t bytes, cudaStream_t st);
 
+// moe_gather_rows, with padding rows zero-filled or left untouched (moe_rows.cu).
+int gather_rows(const void* src, int src_dtype, int64_t cols, const int32_t* sorted_slots, int top_k, int64_t rows,
+                const int32_t* rows_dev, void* dst, int dst_dtype, float* dst_scale, bool zero_pad, void* stream);
+
 inline int num_sms() {
   static int cache[64] = {0};
   int dev = 0;

@@ -175,8 +175,9 @@ int run_experts(const ExpertsArgs& a) {
   const int32_t* rows_dev = table + 1;  // padded rows in use
   void* xp = ws + w.xp;
   float* xs = q ? reinterpret_cast<float*>(ws + w.xs) : nullptr;
-  MOE_TRY(moe_gather_rows(a.x, a.x_dtype, a.H, sorted, a.k, w.cap, rows_dev, xp, q ? MOE_I8 : a.x_dtype, xs,
-                          stream));
+  // padding rows are left as they are: the GEMMs never store their results
+  MOE_TRY(gather_rows(a.x, a.x_dtype, a.H, sorted, a.k, w.cap, rows_dev, xp, q ? MOE_I8 : a.x_dtype, xs, false,
+                      stream));
   MOE_TRY(record_stage(MOE_STAGE_GATHERED, st));
   void* h = ws + w.h;
   MOE_TRY(moe_gemm1_swiglu(xp, q ? MOE_I8 : a.x_dtype, w.cap, a.H, a.w13, a.E, a.I, xs, a.w13_scale, table,

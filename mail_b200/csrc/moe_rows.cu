@@ -100,7 +100,8 @@ template <typename Tin, typename Tout>
 __global__ void __launch_bounds__(256) gather_rows_kernel(const Tin* __restrict__ src, int64_t cols,
                                                           const int32_t* __restrict__ slots, int top_k,
                                                           int64_t rows, const int32_t* __restrict__ rows_dev,
-                                                          Tout* __restrict__ dst, float* __restrict__ dst_scale) {
+                                                          Tout* __restrict__ dst, float* __restrict__ dst_scale,
+                                                          int zero_pad) {
   pdl_begin();
   const int lane = threadIdx.x & 31;
   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -111,6 +112,7 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const Tin* __restrict_
     const int64_t slot = slots ? (int64_t)slots[p] : p;
     Tout* d = dst + p * cols;
     if (slot < 0) {
+      if (!zero_pad) continue;
       for (int64_t c = lane * 8; c < cols; c += 256) zero8(d + c);
       if constexpr (sizeof(Tout) == 1)
         if (lane == 0 && dst_scale) dst_scale[p] = 0.f;
@@ -147,7 +149,8 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const Tin* __restrict_
 // independent 16-byte loads in flight per thread, reduced to its absmax
 // across the RT threads, then quantised from registers. RT is chosen so the
 // threads are full: 32 for rows <= 2048 columns, 64 for <= 4096, else 128
-// (rows up to 8192 columns). A padding row (slot < 0) quantises zeros.
+// (rows up to 8192 columns). A padding row (slot < 0) quantises zeros, or is
+// skipped when zero_pad is 0.
 constexpr int kQuantVecs = 8;
 constexpr int kQuantThreads = 128;
 constexpr int64_t kQuantMaxCols = (int64_t)kQuantThreads * 8 * kQuantVecs;
@@ -158,7 +161,7 @@ __global__ void __launch_bounds__(kQuantThreads) gather_quant_kernel(const Tin* 
                                                                      int64_t rows,
                                                                      const int32_t* __restrict__ rows_dev,
                                                                      int8_t* __restrict__ dst,
-                                                                     float* __restrict__ dst_scale) {
+                                                                     float* __restrict__ dst_scale, int zero_pad) {
   pdl_begin();
   constexpr int kRowsPerPass = kQuantThreads / RT;
   constexpr int kWarpsPerRow = RT / 32;
@@ -199,7 +202,7 @@ __global__ void __launch_bounds__(kQuantThreads) gather_quant_kernel(const Tin* 
     }
     float scale, inv;
     row_scales(amax, scale, inv);
-    if (active) {
+    if (active && (slot >= 0 || zero_pad)) {
       int8_t* d = dst + p * cols;
 #pragma unroll
       for (int i = 0; i < kQuantVecs; ++i) {
@@ -284,9 +287,13 @@ int zero_fill(void* dst, size_t bytes, cudaStream_t st) {
 
 using namespace moe;
 
-extern "C" int moe_gather_rows(const void* src, int src_dtype, int64_t cols, const int32_t* sorted_slots,
-                               int top_k, int64_t rows, const int32_t* rows_dev, void* dst, int dst_dtype,
-                               float* dst_scale, void* stream) {
+namespace moe {
+// moe_gather_rows with a choice for padding rows (slot < 0): zero-filled
+// (zero_pad), or left as they are. The fused top-k pass leaves them: the
+// GEMMs compute padding rows but never store their results, so their content
+// does not matter (at one token over 128 experts the rows are 99 % padding).
+int gather_rows(const void* src, int src_dtype, int64_t cols, const int32_t* sorted_slots, int top_k, int64_t rows,
+                const int32_t* rows_dev, void* dst, int dst_dtype, float* dst_scale, bool zero_pad, void* stream) {
   MOE_CHECK_ARG(src && dst, "moe_gather_rows: NULL src/dst");
   MOE_CHECK_ARG(cols > 0 && cols % 8 == 0, "moe_gather_rows: cols (%lld) must be a positive multiple of 8",
                 (long long)cols);
@@ -299,7 +306,7 @@ extern "C" int moe_gather_rows(const void* src, int src_dtype, int64_t cols, con
 #define GATHER(TI, TO)                                                                               \
   MOE_CUDA_TRY(launch_kernel(gather_rows_kernel<TI, TO>, dim3(grid), dim3(256), 0, st,               \
                              static_cast<const TI*>(src), cols, sorted_slots, top_k, rows, rows_dev, \
-                             static_cast<TO*>(dst), dst_scale))
+                             static_cast<TO*>(dst), dst_scale, (int)zero_pad))
   if (dst_dtype == src_dtype) {
     if (src_dtype == MOE_BF16) GATHER(__nv_bfloat16, __nv_bfloat16);
     else if (src_dtype == MOE_F16) GATHER(__half, __half);
@@ -315,7 +322,7 @@ extern "C" int moe_gather_rows(const void* src, int src_dtype, int64_t cols, con
 #define GATHER_Q(TI, RT)                                                                                      \
   MOE_CUDA_TRY(launch_kernel(gather_quant_kernel<TI, RT>, dim3((unsigned)blocks), dim3(kQuantThreads), 0, st, \
                              static_cast<const TI*>(src), cols, sorted_slots, top_k, rows, rows_dev,          \
-                             static_cast<int8_t*>(dst), dst_scale))
+                             static_cast<int8_t*>(dst), dst_scale, (int)zero_pad))
 #define GATHER_QT(TI)                  \
   if (rt == 32) GATHER_Q(TI, 32);      \
   else if (rt == 64) GATHER_Q(TI, 64); \
@@ -344,6 +351,14 @@ extern "C" int moe_gather_rows(const void* src, int src_dtype, int64_t cols, con
 #undef GATHER
   MOE_LAUNCH_CHECK("gather_rows_kernel");
   return MOE_OK;
+}
+}  // namespace moe
+
+extern "C" int moe_gather_rows(const void* src, int src_dtype, int64_t cols, const int32_t* sorted_slots,
+                               int top_k, int64_t rows, const int32_t* rows_dev, void* dst, int dst_dtype,
+                               float* dst_scale, void* stream) {
+  return gather_rows(src, src_dtype, cols, sorted_slots, top_k, rows, rows_dev, dst, dst_dtype, dst_scale, true,
+                     stream);
 }
 
 extern "C" int moe_quant_rows(const void* src, int src_dtype, int64_t rows, int64_t cols, const int32_t* rows_dev,
