@@ -84,6 +84,7 @@ def test_tile_schedule_matches_reference_bit_exact(name, bm):
 ALIGN_CASES = [
     ("uniform", 64, 2, 8), ("uniform", 4096, 2, 8), ("uniform", 1, 8, 128), ("zipf", 257, 8, 128),
     ("uniform", 8192, 8, 256), ("hot", 5000, 6, 64), ("invalid", 300, 4, 16), ("one_expert", 1000, 1, 32),
+    ("uniform", 3, 8, 1024),
 ]
 
 
