@@ -1,6 +1,7 @@
 // Internal helpers shared by the MoE translation units: status/error
 // reporting, dtype sizes, the compact tile table, and the device error flag.
 #pragma once
+#include <atomic>
 #include <cstdarg>
 #include <cstdint>
 #include <cstdio>
@@ -136,17 +137,20 @@ int zero_fill(void* dst, size_t bytes, cudaStream_t st);
 int gather_rows(const void* src, int src_dtype, int64_t cols, const int32_t* sorted_slots, int top_k, int64_t rows,
                 const int32_t* rows_dev, void* dst, int dst_dtype, float* dst_scale, bool zero_pad, void* stream);
 
+// SM count of the current device (queried once per device; threads may race
+// to fill the cache with the same value).
 inline int num_sms() {
-  static int cache[64] = {0};
+  static std::atomic<int> cache[64];
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) dev = 0;
-  if (cache[dev] == 0) {
-    int n = 0;
+  int n = cache[dev].load(std::memory_order_relaxed);
+  if (n == 0) {
     cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    cache[dev] = n > 0 ? n : 148;
+    if (n <= 0) n = 148;
+    cache[dev].store(n, std::memory_order_relaxed);
   }
-  return cache[dev];
+  return n;
 }
 
 }  // namespace moe

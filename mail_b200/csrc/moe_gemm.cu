@@ -678,16 +678,21 @@ using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t
                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
 int get_encode(EncodeTiledFn* fn) {
-  static EncodeTiledFn cached = nullptr;
-  if (!cached) {
+  struct Entry {
+    EncodeTiledFn fn = nullptr;
+    cudaError_t err = cudaSuccess;
+  };
+  static const Entry entry = [] {  // looked up once, thread-safe
+    Entry r;
     void* ptr = nullptr;
     cudaDriverEntryPointQueryResult q;
-    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q);
-    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !ptr)
-      return set_error(MOE_ERR_CUDA, "cuTensorMapEncodeTiled unavailable (%s)", cudaGetErrorString(e));
-    cached = reinterpret_cast<EncodeTiledFn>(ptr);
-  }
-  *fn = cached;
+    r.err = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q);
+    if (r.err == cudaSuccess && q == cudaDriverEntryPointSuccess) r.fn = reinterpret_cast<EncodeTiledFn>(ptr);
+    return r;
+  }();
+  if (!entry.fn)
+    return set_error(MOE_ERR_CUDA, "cuTensorMapEncodeTiled unavailable (%s)", cudaGetErrorString(entry.err));
+  *fn = entry.fn;
   return MOE_OK;
 }
 
