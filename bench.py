@@ -210,12 +210,12 @@ def make_weights(cfg, experts, device, dt):
 # --------------------------------------------------------------------------- reference arm / cpu baseline
 
 
-def cpu_reference_run(cfg, steps: int, warmup: int, budget_s: float = 20.0):
+def cpu_reference_run(cfg, steps: int, warmup: int, time_limit_s: float = 20.0):
     """Times the oracle port of the reference's torch MoE path (per-expert fp32
     loop, fixed_kernel.py:232-249, extended with the top-k combine) on the
     host cores over a bounded token sample of the workload: the sample size is
     chosen from a quick sgemm calibration so one step takes about
-    budget_s / steps seconds, and only the experts the sample touches get
+    time_limit_s / steps seconds, and only the experts the sample touches get
     (host-generated) weights."""
     try:
         from threadpoolctl import threadpool_info
@@ -234,7 +234,7 @@ def cpu_reference_run(cfg, steps: int, warmup: int, budget_s: float = 20.0):
     for _ in range(3):
         a @ b
     gflops = 3 * 2 * 256 * H * 2048 / (time.perf_counter() - t0) / 1e9
-    per_step = max(budget_s / max(steps + warmup, 1), 0.25)
+    per_step = max(time_limit_s / max(steps + warmup, 1), 0.25)
     flops_per_token = 6.0 * k * H * I
     n = int(max(1, min(T, per_step * gflops * 1e9 / flops_per_token)))
     ids_all, wts_all = O.synthetic_routing(cfg["routing"], T, E, k, seed=0)
@@ -629,7 +629,7 @@ def main():
             "gpu_launches": int(launches), "clocks": clocks}
 
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        ref = cpu_reference_run(cfg, steps=3, warmup=1, budget_s=20.0)
+        ref = cpu_reference_run(cfg, steps=3, warmup=1, time_limit_s=20.0)
         line["cpu_baseline"] = {"value": ref["value"], "unit": "tokens/s", "cores": ref["cores"], "kind": "port",
                                 "sample": ref["sample"]}
     if rank == 0:

@@ -10,7 +10,7 @@
  *   - build_tile_schedule(group_sizes, num_tokens, BLOCK_M)  fused_moe_mlp_triton.py:91-119
  *   - the sglang call site fused_moe_mlp(hidden_states, w13_weight, w2_weight,
  *     expert_tokens)                                           unquant_diff.txt:13-18
- * The top-k entry point (moe_fused_experts) implements the north-star call
+ * The top-k entry point (moe_fused_experts) implements the sglang fused_experts-style call
  * fused_moe_mlp(hidden_states, w13, w2, topk_weights, topk_ids, [scales]); the
  * reference has no routing/align/quant/combine code, so those stages follow the
  * semantics documented beside each declaration.
@@ -50,7 +50,7 @@ extern "C" {
 typedef enum {
   MOE_OK = 0,
   MOE_ERR_INVALID_ARG = 1,  /* bad shape / dtype / pointer / alignment */
-  MOE_ERR_UNSUPPORTED = 2,  /* valid request this build does not implement */
+  MOE_ERR_UNSUPPORTED = 2,  /* valid request the library does not implement */
   MOE_ERR_CUDA = 3,         /* a CUDA runtime or driver call failed */
   MOE_ERR_WORKSPACE = 4,    /* workspace too small */
   MOE_ERR_DEVICE = 5        /* device-side error flag was set (timeout) */

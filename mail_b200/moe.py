@@ -2,7 +2,8 @@
 
 `fused_moe_mlp` keeps the reference's call signature
 (fused_moe_mlp_triton.py:121-130, called from sglang at unquant_diff.txt:13-18)
-and adds the north-star top-k form:
+and adds the sglang fused_experts-style top-k form (routing align and
+weighted combine inside):
 
     fused_moe_mlp(x, w13, w2, group_sizes)                      # pre-routed rows
     fused_moe_mlp(hidden_states, w13, w2, topk_weights, topk_ids, scales=None)

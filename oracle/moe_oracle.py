@@ -1,8 +1,9 @@
 """CPU oracle for the fused MoE MLP path — TEST INFRASTRUCTURE ONLY.
 
 This module restates, in numpy on the CPU, the algorithm of the reference
-(CrDem/mail) for the fused MoE MLP and defines the north-star stages the
-reference does not contain. It is the checker the parity tests, smoke() and
+(CrDem/mail) for the fused MoE MLP and defines the stages of the top-k form
+(routing, align, int8 quant, weighted combine) that the reference does not
+contain. It is what the parity tests, smoke() and
 the CPU-baseline leg of bench.py compare against; the product path
 (mail_b200 / libmoe_b200.so) never imports it.
 
@@ -204,7 +205,7 @@ def quantize_weight_per_channel(w):
 
 
 # ---------------------------------------------------------------------------
-# Top-k MoE MLP (north-star form)
+# Top-k MoE MLP (routing align + weighted combine around the expert MLP)
 
 
 def _accumulate_rows(y, rows, vals):

@@ -3,7 +3,7 @@ the reference's golden vectors.
 
 Bars: integer/index work (tile schedule, align, int8 quant) bit-exact;
 floating-point outputs within max-abs-rel error 1e-2 of an fp32 reference
-(max |y - ref| / max |ref|), the north-star tolerance for bf16 outputs.
+(max |y - ref| / max |ref|), the tolerance the workload sets for bf16 outputs.
 """
 import os
 
