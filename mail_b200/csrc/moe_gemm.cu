@@ -229,14 +229,17 @@ struct Cfg {
   static constexpr uint32_t kTxBytes = PAIR ? 2 * kStageBytes : kStageBytes;  // per stage, whole MMA
 };
 
+// tmap_a64: A with 64-row boxes, the MMA rows of a half unit's CTA.
 // tmap_b64: B with 64-row boxes; the gate_up GEMM's half units load 64 gate
 // and 64 up rows per CTA so that one thread's TMEM lane holds both.
 template <int KIND, bool SWIGLU, bool PAIR>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     moe_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
-                    const __grid_constant__ CUtensorMap tmap_b64, const Params p) {
+                    const __grid_constant__ CUtensorMap tmap_a64, const __grid_constant__ CUtensorMap tmap_b64,
+                    const Params p) {
   using C = Cfg<PAIR>;
   constexpr int S = C::kStages;
+  constexpr uint32_t kHalfTxBytes = 2 * (A_BYTES / 2 + C::kBBytes);  // per stage of a half unit, both CTAs
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -274,6 +277,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   if (warp == 0 && lane == 0) {
     ptx::prefetch_tmap(&tmap_a);
     ptx::prefetch_tmap(&tmap_b);
+    if (PAIR && p.half_units) ptx::prefetch_tmap(&tmap_a64);
     if (SWIGLU && PAIR && p.half_units) ptx::prefetch_tmap(&tmap_b64);
   }
   pdl_begin();  // the tile table and operands come from the grids before this one
@@ -375,9 +379,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           }
           const int kx = kb * (ROW_BYTES / (KIND == 0 ? 2 : (KIND == 1 ? 4 : 1)));
           if constexpr (PAIR) {
-            if (leader) ptx::mbar_arrive_expect_tx(&full[stage], C::kTxBytes);
+            // a half unit loads only its 64 MMA rows of A per CTA
+            if (leader) ptx::mbar_arrive_expect_tx(&full[stage], half ? kHalfTxBytes : C::kTxBytes);
             const uint32_t bar = ptx::mapa(ptx::smem_u32(&full[stage]), 0);  // the leader's full barrier
-            ptx::tma_load_2d_pair(sA + stage * A_BYTES, &tmap_a, bar, kx, row0);
+            ptx::tma_load_2d_pair(sA + stage * A_BYTES, half ? &tmap_a64 : &tmap_a, bar, kx, row0);
             if (SWIGLU && half) {
               ptx::tma_load_2d_pair(sB + stage * C::kBBytes, &tmap_b64, bar, kx, brow);
               ptx::tma_load_2d_pair(sB + stage * C::kBBytes + C::kBBytes / 2, &tmap_b64, bar, kx, brow + p.inter);
@@ -766,8 +771,8 @@ size_t gemm_smem_bytes(int E) {
 }
 
 template <int KIND, bool SWIGLU, bool PAIR>
-int launch_kind(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tb64, const Params& p,
-                int64_t units_ub, cudaStream_t st) {
+int launch_kind(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& ta64, const CUtensorMap& tb64,
+                const Params& p, int64_t units_ub, cudaStream_t st) {
   const size_t smem = gemm_smem_bytes<PAIR>(p.E);
   auto kfn = moe_gemm_kernel<KIND, SWIGLU, PAIR>;
   MOE_CUDA_TRY(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
@@ -801,20 +806,20 @@ int launch_kind(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap&
     cfg.attrs = attr;
     cfg.numAttrs += 1;
   }
-  MOE_CUDA_TRY(cudaLaunchKernelEx(&cfg, kfn, ta, tb, tb64, p));
+  MOE_CUDA_TRY(cudaLaunchKernelEx(&cfg, kfn, ta, tb, ta64, tb64, p));
   MOE_LAUNCH_CHECK("moe_gemm_kernel");
   return MOE_OK;
 }
 
 template <bool SWIGLU, bool PAIR>
-int launch(int dtype, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tb64, const Params& p,
-           cudaStream_t st) {
+int launch(int dtype, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& ta64, const CUtensorMap& tb64,
+           const Params& p, cudaStream_t st) {
   // units: M tiles (single CTA) or M-tile pairs, upper bound max_tiles
   const int64_t units_ub = (int64_t)(PAIR ? (p.max_tiles + p.E) / 2 + p.E : p.max_tiles) * p.n_tiles;
   switch (kind_of(dtype)) {
-    case 0: return launch_kind<0, SWIGLU, PAIR>(ta, tb, tb64, p, units_ub, st);
-    case 1: return launch_kind<1, SWIGLU, PAIR>(ta, tb, tb64, p, units_ub, st);
-    default: return launch_kind<2, SWIGLU, PAIR>(ta, tb, tb64, p, units_ub, st);
+    case 0: return launch_kind<0, SWIGLU, PAIR>(ta, tb, ta64, tb64, p, units_ub, st);
+    case 1: return launch_kind<1, SWIGLU, PAIR>(ta, tb, ta64, tb64, p, units_ub, st);
+    default: return launch_kind<2, SWIGLU, PAIR>(ta, tb, ta64, tb64, p, units_ub, st);
   }
 }
 
@@ -859,13 +864,18 @@ extern "C" int moe_gemm1_swiglu(const void* a, int dtype, int64_t a_rows, int64_
   MOE_CHECK_ARG((uintptr_t)a % 16 == 0 && (uintptr_t)w13 % 16 == 0 && (uintptr_t)h % 16 == 0,
                 "moe_gemm1_swiglu: pointers must be 16-byte aligned");
   if (a_rows == 0 || max_tiles == 0) return MOE_OK;
-  CUtensorMap ta, tb, tb64;
+  CUtensorMap ta, tb, ta64, tb64;
   const bool pair = use_pair(max_tiles, num_experts, ceil_div(inter, BN / 2));
   const bool half_units = pair && g_gemm_half_units.load() != 0;
   MOE_TRY(make_tmap(&ta, a, dtype, hidden, a_rows, BM));
   MOE_TRY(make_tmap(&tb, w13, dtype, hidden, (uint64_t)num_experts * 2 * inter, BN / 2));
-  if (half_units) MOE_TRY(make_tmap(&tb64, w13, dtype, hidden, (uint64_t)num_experts * 2 * inter, BN / 4));
-  else tb64 = tb;
+  if (half_units) {
+    MOE_TRY(make_tmap(&ta64, a, dtype, hidden, a_rows, BM / 2));
+    MOE_TRY(make_tmap(&tb64, w13, dtype, hidden, (uint64_t)num_experts * 2 * inter, BN / 4));
+  } else {
+    ta64 = ta;
+    tb64 = tb;
+  }
   Params p{};
   p.E = num_experts;
   p.num_kb = (int)ceil_div(hidden * dtype_size(dtype), ROW_BYTES);
@@ -888,8 +898,8 @@ extern "C" int moe_gemm1_swiglu(const void* a, int dtype, int64_t a_rows, int64_
   p.a_scale = a_scale;
   p.b_scale = w13_scale;
   p.top_k = 1;
-  return pair ? launch<true, true>(dtype, ta, tb, tb64, p, as_stream(stream))
-              : launch<true, false>(dtype, ta, tb, tb64, p, as_stream(stream));
+  return pair ? launch<true, true>(dtype, ta, tb, ta64, tb64, p, as_stream(stream))
+              : launch<true, false>(dtype, ta, tb, ta64, tb64, p, as_stream(stream));
 }
 
 namespace moe {
@@ -917,9 +927,12 @@ int gemm2_impl(const void* h, int dtype, int64_t h_rows, int64_t inter, const vo
   MOE_CHECK_ARG((uintptr_t)h % 16 == 0 && (uintptr_t)w2 % 16 == 0 && (uintptr_t)out % 16 == 0,
                 "moe_gemm2: pointers must be 16-byte aligned");
   if (h_rows == 0 || max_tiles == 0) return MOE_OK;
-  CUtensorMap ta, tb;
+  CUtensorMap ta, tb, ta64;
   const bool pair = use_pair(max_tiles, num_experts, ceil_div(hidden, BN));
+  const bool half_units = pair && g_gemm_half_units.load() != 0;  // read once: the maps must match
   MOE_TRY(make_tmap(&ta, h, dtype, inter, h_rows, BM));
+  if (half_units) MOE_TRY(make_tmap(&ta64, h, dtype, inter, h_rows, BM / 2));
+  else ta64 = ta;
   MOE_TRY(make_tmap(&tb, w2, dtype, inter, (uint64_t)num_experts * hidden, pair ? BN / 2 : BN));
   Params p{};
   p.E = num_experts;
@@ -930,7 +943,7 @@ int gemm2_impl(const void* h, int dtype, int64_t h_rows, int64_t inter, const vo
   p.inter = (int)inter;
   p.idesc = make_idesc(dtype, pair ? 2 * BM : BM);
   p.idesc_half = make_idesc(dtype, BM);
-  p.half_units = pair && g_gemm_half_units.load() != 0;
+  p.half_units = half_units;
   p.band_tiles = g_gemm_band.load();
   p.table = tile_table;
   p.max_tiles = (int)max_tiles;
@@ -950,7 +963,8 @@ int gemm2_impl(const void* h, int dtype, int64_t h_rows, int64_t inter, const vo
   // the weighted combine adds partial sums, so its work can be split along K
   // evenly over the grid (no partly idle last wave)
   p.stream_k = epilogue == MOE_EPI_COMBINE_ADD && g_gemm_stream_k.load() != 0;
-  return pair ? launch<false, true>(dtype, ta, tb, tb, p, stream) : launch<false, false>(dtype, ta, tb, tb, p, stream);
+  return pair ? launch<false, true>(dtype, ta, tb, ta64, tb, p, stream)
+              : launch<false, false>(dtype, ta, tb, ta64, tb, p, stream);
 }
 }  // namespace
 
