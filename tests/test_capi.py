@@ -63,6 +63,23 @@ def test_invalid_arguments_are_rejected_on_host(call, needle):
     assert needle in lib.moe_last_error().decode()
 
 
+def test_options_round_trip_and_reject_bad_values():
+    """Every documented option reads back what was set; bad values and
+    unknown options are rejected on the host."""
+    lib = _lib.load()
+    opts = {_lib.OPT_GEMM_CTA_PAIR: (0, 2), _lib.OPT_GEMM_BAND: (8, 16), _lib.OPT_GEMM_STREAM_K: (1, 0),
+            _lib.OPT_GEMM_HALF_UNITS: (0, 1), _lib.OPT_PDL: (0, 1)}
+    for opt, (val, default) in opts.items():
+        assert lib.moe_get_option(opt) == default, opt
+        assert lib.moe_set_option(opt, val) == 0
+        assert lib.moe_get_option(opt) == val
+        assert lib.moe_set_option(opt, default) == 0
+    assert lib.moe_set_option(_lib.OPT_GEMM_CTA_PAIR, 3) == 1
+    assert lib.moe_set_option(_lib.OPT_GEMM_BAND, 0) == 1
+    assert lib.moe_set_option(99, 1) == 1 and "unknown option" in lib.moe_last_error().decode()
+    assert lib.moe_get_option(99) == -1
+
+
 def test_empty_batch_is_a_no_op():
     """Zero tokens: both fused entry points return OK without touching any
     buffer (all NULL here) and without launching work."""
