@@ -20,7 +20,10 @@
  *     element counts. Nothing here allocates device memory: callers pass a
  *     workspace sized by the matching *_workspace_size() query.
  *   - Every call is asynchronous on `stream` (a cudaStream_t, NULL = legacy
- *     default stream) and never synchronises the device.
+ *     default stream) and never synchronises the device. Kernels are launched
+ *     with programmatic dependent launch (MOE_OPT_PDL) and each waits for the
+ *     work queued before it on the stream before touching memory, so ordering
+ *     against the caller's own kernels is plain stream order.
  *   - Return value: MOE_OK or a moe_status_t; moe_last_error() returns a
  *     thread-local message for the last failing call of this thread.
  *   - Weight layout ("(E, K, N)" logical, K-major physical): w13 is stored as
