@@ -173,16 +173,53 @@ class ClockSampler:
 # --------------------------------------------------------------------------- inputs
 
 
-def make_inputs(cfg, rank: int, device):
-    import torch
+def make_routing(name: str, T: int, E: int, k: int, seed: int):
+    """Seeded synthetic routing of a workload: (topk_ids int32 [T, k],
+    topk_weights fp32 [T, k]).
+      uniform-softmax / sigmoid: logits ~ N(0, 1), the k largest (ties to the
+        lower id), softmax / sigmoid scores renormalised over the k
+      zipf1.2: k distinct experts per token drawn from a Zipf(1.2) popularity
+        over a seeded permutation of the ids; weights softmax of N(0, 1)
+      hot25-zipf1.0: Zipf(1.0), then a quarter of the tokens (seeded) forced
+        to also route to one hot expert (it replaces their last choice)
+    The CPU-baseline leg builds the same inputs (a test checks they agree)."""
+    rng = np.random.default_rng(seed)
+    if name in ("uniform-softmax", "sigmoid"):
+        lg = rng.standard_normal((T, E), dtype=np.float32)
+        ids = np.argsort(-lg, axis=1, kind="stable")[:, :k]
+        top = np.take_along_axis(lg, ids, axis=1)
+        if name == "uniform-softmax":
+            sc = np.exp(top - lg.max(axis=1, keepdims=True)).astype(np.float32)
+        else:
+            sc = (np.float32(1.0) / (np.float32(1.0) + np.exp(-top))).astype(np.float32)
+        return ids.astype(np.int32), (sc / sc.sum(axis=1, keepdims=True)).astype(np.float32)
+    if name in ("zipf1.2", "hot25-zipf1.0"):
+        s = 1.2 if name == "zipf1.2" else 1.0
+        p = np.arange(1, E + 1, dtype=np.float64) ** (-s)
+        p /= p.sum()
+        perm = rng.permutation(E)
+        ids = np.empty((T, k), np.int32)
+        for t in range(T):
+            ids[t] = perm[rng.choice(E, size=k, replace=False, p=p)]
+        if name == "hot25-zipf1.0":
+            hot = int(rng.integers(E))
+            for t in rng.choice(T, size=T // 4, replace=False):
+                if hot not in ids[t]:
+                    ids[t, k - 1] = hot
+        lg = rng.standard_normal((T, k), dtype=np.float32)
+        w = np.exp(lg - lg.max(axis=1, keepdims=True))
+        return ids, (w / w.sum(axis=1, keepdims=True)).astype(np.float32)
+    raise ValueError(name)
 
-    from oracle import moe_oracle as O  # routing of the synthetic inputs only (setup, untimed)
+
+def make_inputs(cfg, rank: int, device, variant: int = 0):
+    import torch
 
     T, H, I, E, k = cfg["T"], cfg["H"], cfg["I"], cfg["E"], cfg["k"]
     dt = {"bf16": torch.bfloat16, "fp32": torch.float32, "fp16": torch.float16}[cfg["dtype"]]
-    g = torch.Generator(device=device).manual_seed(1234 + rank)
+    g = torch.Generator(device=device).manual_seed(1234 + rank + 7919 * variant)
     x = torch.randn(T, H, device=device, generator=g).to(dt)
-    ids, wts = O.synthetic_routing(cfg["routing"], T, E, k, seed=rank)
+    ids, wts = make_routing(cfg["routing"], T, E, k, seed=rank + 7919 * variant)
     return x, torch.from_numpy(ids).to(device), torch.from_numpy(wts).to(device), dt
 
 
@@ -323,9 +360,23 @@ def main():
                    "top_k": k, "routing": cfg["routing"], "dtype": cfg["dtype"] + ("+w8a8" if cfg["quant"] else ""),
                    "parallelism": f"ep{world}" if world > 1 else "single", "gemm": args.gemm,
                    "half_units": bool(args.half_units), "pdl": bool(args.pdl),
-                   "ep_exchange": args.ep if world > 1 else None, "cuda_graph": bool(args.graph and world == 1),
-                   "l2": "weights (%.2f GB) exceed the 126 MB L2, streamed every step" %
-                         (E * 3 * H * I * (1 if cfg["quant"] else (4 if cfg["dtype"] == "fp32" else 2)) / 1e9)}
+                   "ep_exchange": args.ep if world > 1 else None, "cuda_graph": bool(args.graph and world == 1)}
+
+    # When one step's active expert weights fit in the L2 (decode-sized
+    # batches), consecutive steps cycle through several routings that touch
+    # different experts, so the weights stream from HBM as they would in
+    # serving instead of being L2 hits of the previous step.
+    L2_BYTES = 126e6
+    wbytes = 1 if cfg["quant"] else (4 if cfg["dtype"] == "fp32" else 2)
+    ids0, _ = make_routing(cfg["routing"], T, E, k, seed=rank)
+    active_bytes = len(np.unique(ids0)) * 3 * H * I * wbytes
+    n_var = 1 if world > 1 or active_bytes >= 2 * L2_BYTES else int(min(16, -(-3 * L2_BYTES // active_bytes)))
+    if n_var > 1:
+        config_json["l2"] = ("active weights of one step (%.0f MB) fit in the 126 MB L2: steps cycle through %d "
+                             "routings touching different experts" % (active_bytes / 1e6, n_var))
+    else:
+        config_json["l2"] = "active weights of one step (%.2f GB) exceed the 126 MB L2, streamed every step" % (
+            active_bytes / 1e9)
 
     if args.impl == "reference":
         if rank != 0:
@@ -361,6 +412,11 @@ def main():
     lib.moe_set_option(_lib.OPT_PDL, args.pdl)
 
     x, ids, wts, dt = make_inputs(cfg, rank, device)
+    variants = [(x, ids, wts)] + [make_inputs(cfg, rank, device, v)[:3] for v in range(1, n_var)]
+
+    def inp(i):
+        return variants[i % n_var]
+
     if world > 1:
         from mail_b200 import ep as mep
         assert E % world == 0, "experts must divide evenly over ranks"
@@ -403,8 +459,8 @@ def main():
             dist.barrier(device_ids=[local_rank])
 
     # ---- warm-up
-    for _ in range(args.warmup):
-        step(x, ids, wts)
+    for i in range(args.warmup):
+        step(*inp(i))
     torch.cuda.synchronize()
 
     # ---- timed region (device-resident inputs), per-stage events every step
@@ -428,7 +484,7 @@ def main():
     for i in range(args.steps):
         if not args.graph:
             lib.moe_set_stage_events(ev_arrays[i], STAGES)
-        step(x, ids, wts)
+        step(*inp(i))
     lib.moe_set_stage_events(None, 0)
     handles[1].record(stream)
     torch.cuda.synchronize()
@@ -453,7 +509,8 @@ def main():
                 lib.moe_set_stage_events(None, 0)
             stage_rows = []
             for i in range(args.steps):
-                cap_ev(x, wts, ids)
+                xv, iv, wv = inp(i)
+                cap_ev(xv, wv, iv)
                 torch.cuda.synchronize()
                 stage_rows.append([ev[0][j].elapsed_time(ev[0][j + 1]) for j in range(STAGES - 1)])
             del cap_ev
@@ -463,7 +520,8 @@ def main():
         if stage_rows is None:
             for i in range(args.steps):
                 lib.moe_set_stage_events(ev_arrays[i], STAGES)
-                mb.fused_moe_mlp(x, w13, w2, wts, ids, scales=scales)
+                xv, iv, wv = inp(i)
+                mb.fused_moe_mlp(xv, w13, w2, wv, iv, scales=scales)
             lib.moe_set_stage_events(None, 0)
             torch.cuda.synchronize()
     if stage_rows is None:
@@ -484,9 +542,8 @@ def main():
     # copies run on their own streams (host->device, device->host) with two
     # device buffers, so step i+1's upload and step i-1's download overlap
     # step i's compute, as a serving loop would run them.
-    x_h = x.cpu().pin_memory()
-    ids_h = ids.cpu().pin_memory()
-    wts_h = wts.cpu().pin_memory()
+    host_in = [tuple(t.cpu().pin_memory() for t in v) for v in variants]
+    x_h, ids_h, wts_h = host_in[0]
     NB = 2
     out_shape = tuple(step(x, ids, wts).shape)
     y_h = [torch.empty(out_shape, dtype=dt).pin_memory() for _ in range(NB)]
@@ -503,9 +560,10 @@ def main():
         with torch.cuda.stream(up):
             if i >= NB:
                 up.wait_event(comp_ev[b])  # step i-NB has finished reading buffer b
-            x_d[b].copy_(x_h, non_blocking=True)
-            ids_d[b].copy_(ids_h, non_blocking=True)
-            wts_d[b].copy_(wts_h, non_blocking=True)
+            xh, ih, wh = host_in[i % n_var]
+            x_d[b].copy_(xh, non_blocking=True)
+            ids_d[b].copy_(ih, non_blocking=True)
+            wts_d[b].copy_(wh, non_blocking=True)
             h2d_ev[b].record(up)
         stream.wait_event(h2d_ev[b])
         y = step(x_d[b], ids_d[b], wts_d[b])
