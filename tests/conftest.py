@@ -12,6 +12,18 @@ def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA B200 (sm_100a) device")
 
 
+@pytest.fixture(scope="session", autouse=True)
+def _library_built():
+    """The C-ABI tests load mail_b200/libmoe_b200.so; build it (nvcc, no GPU
+    needed) when a fresh checkout runs the tests before the build step.
+    The library itself never builds on import: a missing library is an
+    error there."""
+    from mail_b200 import _lib, build
+
+    if not os.path.exists(_lib.LIB_PATH):
+        build.build()
+
+
 def pytest_collection_modifyitems(config, items):
     try:
         import torch
