@@ -17,8 +17,11 @@
  *
  * Conventions
  *   - All pointers are device pointers unless stated otherwise; sizes are
- *     element counts. Nothing here allocates device memory: callers pass a
- *     workspace sized by the matching *_workspace_size() query.
+ *     element counts. No compute entry point allocates device memory: callers
+ *     pass a workspace sized by the matching *_workspace_size() query (or,
+ *     for moe_align_static, none). The one allocating call is
+ *     moe_ipc_malloc, the expert-parallel set-up helper that creates the
+ *     CUDA-IPC-shareable buffers peers map.
  *   - Every call is asynchronous on `stream` (a cudaStream_t, NULL = legacy
  *     default stream) and never synchronises the device. Kernels are launched
  *     with programmatic dependent launch (MOE_OPT_PDL) and each waits for the
@@ -193,15 +196,19 @@ MOE_API int moe_align(const int32_t* topk_ids, int64_t num_tokens, int top_k, in
  * fully reserved at start-up so no cudaMalloc may happen afterwards. It has
  * no counterpart in the reference. Outputs and their meaning are exactly
  * those of moe_align; it allocates nothing and calls no cudaMalloc/cudaFree.
- * Its scratch is a file-scope device array of MOE_ALIGN_STATIC_SCRATCH_BYTES
- * (1 MiB) that every GPU which loads this library holds until the process
- * exits; requests whose scratch (moe_align_workspace_size) exceeds it fail
- * with MOE_ERR_INVALID_ARG (e.g. 65536 tokens x top-8 over 256 experts needs
- * about 0.5 MiB and fits). The first call on each device looks up the
- * array's device address with that device current; make that first call
- * before any stream capture. All calls share the one array and it keeps the
- * last call's contents: calls that overlap on the GPU (other streams, other
- * host threads) race with each other and must be serialised by the caller. */
+ * Batches of at most 16384 slots over at most 1024 experts run the one-CTA
+ * align, which needs no scratch. Larger ones keep their scratch in a
+ * file-scope device array of MOE_ALIGN_STATIC_SCRATCH_BYTES (1 MiB) that
+ * every GPU which loads this library holds until the process exits; requests
+ * whose scratch (moe_align_workspace_size) exceeds it fail with
+ * MOE_ERR_INVALID_ARG. Example, top-8 over 256 experts: 8192 tokens need
+ * 0.50 MiB and fit, the limit is 16288 tokens, and 16384 tokens (1.005 MiB)
+ * are rejected. The first call on each device that uses the array looks up
+ * its device address with that device current (again after the device's
+ * context is recreated, e.g. by cudaDeviceReset); make that first call before
+ * any stream capture. All calls share the one array and it keeps the last
+ * call's contents: calls that overlap on the GPU (other streams, other host
+ * threads) race with each other and must be serialised by the caller. */
 #define MOE_ALIGN_STATIC_SCRATCH_BYTES (1u << 20)
 MOE_API int moe_align_static(const int32_t* topk_ids, int64_t num_tokens, int top_k, int num_experts, int block_m,
                              int32_t* sorted_slots, int32_t* slot_pos, int32_t* group_sizes,

@@ -9,6 +9,8 @@
 //    routing op (fused moe mlp triton.py:11-13): per-chunk warp histograms
 //    (__match_any_sync), a per-expert scan over chunks, a per-expert scan
 //    with padding to BLOCK_M, and a stable scatter.
+#include <cuda.h>
+
 #include <mutex>
 
 #include "common.cuh"
@@ -515,6 +517,57 @@ extern "C" size_t moe_align_workspace_size(int64_t num_tokens, int top_k, int nu
   return align_ws(num_tokens * top_k, num_experts).bytes;
 }
 
+namespace {
+// One-CTA align for S <= kAlignSmallSlots slots over at most 1024 experts:
+// everything in shared memory, no scratch.
+bool align_is_small(int64_t S, int E) { return S <= kAlignSmallSlots && E <= 1024; }
+
+int launch_align_small(const int32_t* topk_ids, int64_t S, int E, int block_m, int32_t* sorted_slots,
+                       int32_t* slot_pos, int32_t* group_sizes, int32_t* padded_offsets, int32_t* tile_table,
+                       cudaStream_t st) {
+  const int64_t max_tiles = moe_align_capacity(S, E, block_m) / block_m;
+  const size_t smem = ((size_t)(kScanThreads / 32) + 3) * (E + 1) * sizeof(int32_t);
+  if (smem > 48 * 1024)
+    MOE_CUDA_TRY(cudaFuncSetAttribute(align_small_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  MOE_CUDA_TRY(launch_kernel(align_small_kernel, dim3(1), dim3(kScanThreads), smem, st, topk_ids, S, E, block_m,
+                             max_tiles, sorted_slots, slot_pos, group_sizes, padded_offsets, tile_table));
+  MOE_LAUNCH_CHECK("align_small_kernel");
+  return MOE_OK;
+}
+
+// The four-kernel align (chunk histograms, column scan, expert scan with
+// padding and tile table, stable scatter) with its scratch at `scratch`
+// (align_ws(S, E).bytes, laid out by align_ws).
+int launch_align_chunked(const int32_t* topk_ids, int64_t S, int E, int block_m, int32_t* sorted_slots,
+                         int32_t* slot_pos, int32_t* group_sizes, int32_t* padded_offsets, int32_t* tile_table,
+                         void* scratch, cudaStream_t st) {
+  const AlignWs w = align_ws(S, E);
+  char* ws = static_cast<char*>(scratch);
+  int32_t* hist = reinterpret_cast<int32_t*>(ws + w.hist_off);
+  int32_t* base = reinterpret_cast<int32_t*>(ws + w.base_off);
+  int32_t* totals = reinterpret_cast<int32_t*>(ws + w.totals_off);
+  const int64_t max_tiles = moe_align_capacity(S, E, block_m) / block_m;
+  const size_t hsmem = (E + 1) * sizeof(int32_t);
+  if (w.chunks > 0) {
+    MOE_CUDA_TRY(launch_kernel(align_count_kernel, dim3((unsigned)w.chunks), dim3(32), hsmem, st, topk_ids, S, E,
+                               hist));
+    MOE_LAUNCH_CHECK("align_count_kernel");
+  }
+  MOE_CUDA_TRY(launch_kernel(align_colscan_kernel, dim3(E + 1), dim3(kScanThreads), 0, st, hist, (int)w.chunks, E,
+                             base, totals));
+  MOE_LAUNCH_CHECK("align_colscan_kernel");
+  MOE_CUDA_TRY(launch_kernel(align_finalize_kernel, dim3(1), dim3(kScanThreads), 2 * hsmem, st, totals, E, block_m,
+                             max_tiles, group_sizes, padded_offsets, tile_table, sorted_slots));
+  MOE_LAUNCH_CHECK("align_finalize_kernel");
+  if (w.chunks > 0) {
+    MOE_CUDA_TRY(launch_kernel(align_scatter_kernel, dim3((unsigned)w.chunks), dim3(32), hsmem, st, topk_ids, S, E,
+                               base, padded_offsets, sorted_slots, slot_pos));
+    MOE_LAUNCH_CHECK("align_scatter_kernel");
+  }
+  return MOE_OK;
+}
+}  // namespace
+
 extern "C" int moe_align(const int32_t* topk_ids, int64_t num_tokens, int top_k, int num_experts, int block_m,
                          int32_t* sorted_slots, int32_t* slot_pos, int32_t* group_sizes, int32_t* padded_offsets,
                          int32_t* tile_table, void* workspace, size_t workspace_bytes, void* stream) {
@@ -529,72 +582,75 @@ extern "C" int moe_align(const int32_t* topk_ids, int64_t num_tokens, int top_k,
   const AlignWs w = align_ws(S, num_experts);
   if (workspace_bytes < w.bytes || (w.bytes && !workspace))
     return set_error(MOE_ERR_WORKSPACE, "moe_align: workspace %zu < %zu bytes", workspace_bytes, w.bytes);
-  if (S <= kAlignSmallSlots && num_experts <= 1024) {
-    const int64_t max_tiles_s = moe_align_capacity(S, num_experts, block_m) / block_m;
-    const size_t smem = ((size_t)(kScanThreads / 32) + 3) * (num_experts + 1) * sizeof(int32_t);
-    if (smem > 48 * 1024)
-      MOE_CUDA_TRY(cudaFuncSetAttribute(align_small_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    MOE_CUDA_TRY(launch_kernel(align_small_kernel, dim3(1), dim3(kScanThreads), smem, as_stream(stream),
-                               topk_ids, S, num_experts, block_m, max_tiles_s, sorted_slots, slot_pos,
-                               group_sizes, padded_offsets, tile_table));
-    MOE_LAUNCH_CHECK("align_small_kernel");
-    return MOE_OK;
-  }
-  char* ws = static_cast<char*>(workspace);
-  int32_t* hist = reinterpret_cast<int32_t*>(ws + w.hist_off);
-  int32_t* base = reinterpret_cast<int32_t*>(ws + w.base_off);
-  int32_t* totals = reinterpret_cast<int32_t*>(ws + w.totals_off);
-  cudaStream_t st = as_stream(stream);
-  const int64_t max_tiles = moe_align_capacity(S, num_experts, block_m) / block_m;
-  const size_t hsmem = (num_experts + 1) * sizeof(int32_t);
-  if (w.chunks > 0) {
-    MOE_CUDA_TRY(launch_kernel(align_count_kernel, dim3((unsigned)w.chunks), dim3(32), hsmem, st,
-                               topk_ids, S, num_experts, hist));
-    MOE_LAUNCH_CHECK("align_count_kernel");
-  }
-  MOE_CUDA_TRY(launch_kernel(align_colscan_kernel, dim3(num_experts + 1), dim3(kScanThreads), 0, st,
-                             hist, (int)w.chunks, num_experts, base, totals));
-  MOE_LAUNCH_CHECK("align_colscan_kernel");
-  MOE_CUDA_TRY(launch_kernel(align_finalize_kernel, dim3(1), dim3(kScanThreads), 2 * hsmem, st,
-                             totals, num_experts, block_m, max_tiles, group_sizes, padded_offsets, tile_table,
-                             sorted_slots));
-  MOE_LAUNCH_CHECK("align_finalize_kernel");
-  if (w.chunks > 0) {
-    MOE_CUDA_TRY(launch_kernel(align_scatter_kernel, dim3((unsigned)w.chunks), dim3(32), hsmem, st,
-                               topk_ids, S, num_experts, base, padded_offsets, sorted_slots, slot_pos));
-    MOE_LAUNCH_CHECK("align_scatter_kernel");
-  }
-  return MOE_OK;
+  if (align_is_small(S, num_experts))
+    return launch_align_small(topk_ids, S, num_experts, block_m, sorted_slots, slot_pos, group_sizes,
+                              padded_offsets, tile_table, as_stream(stream));
+  return launch_align_chunked(topk_ids, S, num_experts, block_m, sorted_slots, slot_pos, group_sizes, padded_offsets,
+                              tile_table, workspace, as_stream(stream));
 }
 
 // ---------------------------------------------------------------------------
-// moe_align_static: the same four align kernels with their scratch in a
-// file-scope device array instead of a caller workspace, for callers that
-// cannot allocate device memory. Nothing in the scratch has to start at zero:
-// every histogram, base and total the kernels read is written earlier in the
-// same call. Calls that overlap on the GPU share (and race on) the array.
+// moe_align_static: moe_align without a workspace argument. Batches the
+// one-CTA kernel handles (at most 16384 slots over at most 1024 experts) need
+// no scratch at all; larger ones run the four align kernels with their
+// scratch in a file-scope device array instead of a caller workspace, for
+// callers that cannot allocate device memory. Nothing in the scratch has to
+// start at zero: every histogram, base and total the kernels read is written
+// earlier in the same call. Calls that overlap on the GPU share (and race on)
+// the array.
 namespace {
 static __device__ __align__(256) unsigned char g_align_scratch[MOE_ALIGN_STATIC_SCRATCH_BYTES];
 
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+
+// The calling thread's current CUDA context (driver API, reached through the
+// runtime's entry-point query so the library links no libcuda).
+int current_context(CUcontext* ctx) {
+  static CtxGetCurrentFn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return (CtxGetCurrentFn) nullptr;
+    return reinterpret_cast<CtxGetCurrentFn>(p);
+  }();
+  if (!fn) return set_error(MOE_ERR_CUDA, "moe_align_static: cuCtxGetCurrent unavailable");
+  if (fn(ctx) != CUDA_SUCCESS) return set_error(MOE_ERR_CUDA, "moe_align_static: cuCtxGetCurrent failed");
+  return MOE_OK;
+}
+
+struct ScratchAddr {
+  CUcontext ctx = nullptr;
+  void* ptr = nullptr;
+};
 std::mutex g_align_scratch_mu;
-void* g_align_scratch_ptr[64] = {nullptr};
+ScratchAddr g_align_scratch_addr[64];
 
 // Device address of g_align_scratch on the current device. In host code the
-// symbol is only a host-side stand-in, so the address is looked up once per
-// device, with that device current, and cached.
+// symbol is only a host-side stand-in, so the address is looked up with the
+// device current, once per device and context, and cached; a new context on
+// the device (after cudaDeviceReset, say) loads the module afresh, possibly
+// elsewhere, so the lookup is redone then.
 int align_scratch_address(void** out) {
   int dev = 0;
   MOE_CUDA_TRY(cudaGetDevice(&dev));
   if (dev < 0 || dev >= 64) return set_error(MOE_ERR_UNSUPPORTED, "moe_align_static: device %d >= 64", dev);
+  CUcontext ctx = nullptr;
+  MOE_TRY(current_context(&ctx));
   std::lock_guard<std::mutex> lock(g_align_scratch_mu);
-  if (!g_align_scratch_ptr[dev]) {
+  ScratchAddr& a = g_align_scratch_addr[dev];
+  if (!ctx || !a.ptr || a.ctx != ctx) {
+    // no context current on this thread yet, or a different one: the lookup
+    // makes the device's primary context current and loads the module
     void* p = nullptr;
     cudaError_t e = cudaGetSymbolAddress(&p, g_align_scratch);
     if (e != cudaSuccess || !p)
       return set_error(MOE_ERR_CUDA, "moe_align_static: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
-    g_align_scratch_ptr[dev] = p;
+    MOE_TRY(current_context(&ctx));
+    a.ctx = ctx;
+    a.ptr = p;
   }
-  *out = g_align_scratch_ptr[dev];
+  *out = a.ptr;
   return MOE_OK;
 }
 }  // namespace
@@ -615,31 +671,11 @@ extern "C" int moe_align_static(const int32_t* topk_ids, int64_t num_tokens, int
                 "moe_align_static: %lld slots over %d experts need %zu bytes of scratch, more than the static "
                 "%u-byte array; use moe_align with a workspace",
                 (long long)S, num_experts, w.bytes, (unsigned)MOE_ALIGN_STATIC_SCRATCH_BYTES);
+  if (align_is_small(S, num_experts))
+    return launch_align_small(topk_ids, S, num_experts, block_m, sorted_slots, slot_pos, group_sizes,
+                              padded_offsets, tile_table, as_stream(stream));
   void* scratch = nullptr;
   MOE_TRY(align_scratch_address(&scratch));
-  char* ws = static_cast<char*>(scratch);
-  int32_t* hist = reinterpret_cast<int32_t*>(ws + w.hist_off);
-  int32_t* base = reinterpret_cast<int32_t*>(ws + w.base_off);
-  int32_t* totals = reinterpret_cast<int32_t*>(ws + w.totals_off);
-  cudaStream_t st = as_stream(stream);
-  const int64_t max_tiles = moe_align_capacity(S, num_experts, block_m) / block_m;
-  const size_t hsmem = (num_experts + 1) * sizeof(int32_t);
-  if (w.chunks > 0) {
-    MOE_CUDA_TRY(launch_kernel(align_count_kernel, dim3((unsigned)w.chunks), dim3(32), hsmem, st,
-                               topk_ids, S, num_experts, hist));
-    MOE_LAUNCH_CHECK("align_count_kernel");
-  }
-  MOE_CUDA_TRY(launch_kernel(align_colscan_kernel, dim3(num_experts + 1), dim3(kScanThreads), 0, st,
-                             hist, (int)w.chunks, num_experts, base, totals));
-  MOE_LAUNCH_CHECK("align_colscan_kernel");
-  MOE_CUDA_TRY(launch_kernel(align_finalize_kernel, dim3(1), dim3(kScanThreads), 2 * hsmem, st,
-                             totals, num_experts, block_m, max_tiles, group_sizes, padded_offsets, tile_table,
-                             sorted_slots));
-  MOE_LAUNCH_CHECK("align_finalize_kernel");
-  if (w.chunks > 0) {
-    MOE_CUDA_TRY(launch_kernel(align_scatter_kernel, dim3((unsigned)w.chunks), dim3(32), hsmem, st,
-                               topk_ids, S, num_experts, base, padded_offsets, sorted_slots, slot_pos));
-    MOE_LAUNCH_CHECK("align_scatter_kernel");
-  }
-  return MOE_OK;
+  return launch_align_chunked(topk_ids, S, num_experts, block_m, sorted_slots, slot_pos, group_sizes, padded_offsets,
+                              tile_table, scratch, as_stream(stream));
 }

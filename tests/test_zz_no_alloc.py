@@ -70,6 +70,24 @@ def test_align_static_matches_align_on_two_calls_in_a_row():
     assert mb.device_error() == 0
 
 
+@pytest.mark.parametrize("T,k,E", [
+    (16288, 8, 256),   # scratch 1,047,808 B: the last tail region ends just below the 1 MiB array
+    (2000, 8, 4096),   # more than 1024 experts: the multi-kernel path even for a small batch
+    (60, 8, 4096),     # the same with fewer slots than experts
+    (2048, 8, 128),    # 16384 slots: the one-CTA align, no scratch
+])
+def test_align_static_edges_match_align(T, k, E):
+    lib = _lib.load()
+    assert lib.moe_align_workspace_size(T, k, E, 128) <= (1 << 20)
+    ids = routing_ids(T + E, T, k, E)
+    for _ in range(2):
+        got = align_static(ids, E)
+        ref = mb.moe_align(ids, E, 128)
+        torch.cuda.synchronize()
+        assert_same_align(ref, got, E)
+    assert mb.device_error() == 0
+
+
 def test_align_static_rejects_requests_beyond_its_scratch():
     lib = _lib.load()
     T, k, E = 1 << 20, 8, 256  # 8M slots: far more scratch than the static array
