@@ -16,11 +16,12 @@ from .moe import (
     quant_int8_rows,
     quantize_weights_int8,
     route_topk,
+    weights_from_checkpoint,
     weights_from_linear,
 )
 
 __all__ = [
     "BLOCK_M", "CapturedMoeMLP", "MoeError", "build_tile_schedule", "device_error", "fused_expert_rows", "fused_moe_mlp", "gather_rows", "kmajor",
     "load_library", "moe_align", "prepack_weights", "quant_int8_rows", "quantize_weights_int8", "route_topk",
-    "weights_from_linear",
+    "weights_from_checkpoint", "weights_from_linear",
 ]

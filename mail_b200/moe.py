@@ -85,6 +85,48 @@ def weights_from_linear(w13_linear: torch.Tensor, w2_linear: torch.Tensor):
     return w13_linear.transpose(1, 2), w2_linear.transpose(1, 2)
 
 
+def weights_from_checkpoint(gate_proj, up_proj, down_proj, device=None, dtype=None, quantize: bool = False):
+    """Per-expert checkpoint tensors -> the op's weight storage, once at load.
+
+    gate_proj[e] and up_proj[e] are the HF `experts.{e}.gate_proj.weight` /
+    `up_proj.weight` matrices ([I, H], nn.Linear layout) and down_proj[e] is
+    `down_proj.weight` ([H, I]); each argument is a sequence of E tensors or
+    one stacked [E, ...] tensor. The reference's loader concatenates gate and
+    up on dim 0, stacks the experts and transposes (kernel_bench.py:212-235),
+    giving logical w13 [E, H, 2I] (gate = first I columns) and w2 [E, I, H].
+    This returns the same logical tensors, built by copying each expert
+    straight into K-major storage ([E, 2I, H] / [E, H, I] contiguous, the
+    layout the kernels' TMA reads) on `device` (default: the tensors' own),
+    cast to `dtype` if given — no concatenated or stacked intermediate.
+
+    quantize=True (CUDA device) converts to w8a8 weights with per-output-
+    channel scales (quantize_weights_int8) and returns (w13_q, w2_q, scales);
+    otherwise (w13, w2)."""
+    E = len(gate_proj)
+    if len(up_proj) != E or len(down_proj) != E or E == 0:
+        raise ValueError("weights_from_checkpoint: gate_proj, up_proj and down_proj need one entry per expert")
+    I, H = gate_proj[0].shape
+    if tuple(down_proj[0].shape) != (H, I):
+        raise ValueError(f"weights_from_checkpoint: down_proj is {tuple(down_proj[0].shape)}, expected {(H, I)}")
+    dev = torch.device(device) if device is not None else gate_proj[0].device
+    dt = dtype or gate_proj[0].dtype
+    w13 = torch.empty((E, 2 * I, H), dtype=dt, device=dev)
+    w2 = torch.empty((E, H, I), dtype=dt, device=dev)
+    for e in range(E):
+        if tuple(gate_proj[e].shape) != (I, H) or tuple(up_proj[e].shape) != (I, H):
+            raise ValueError(f"weights_from_checkpoint: expert {e}: gate/up must both be {(I, H)}")
+        if tuple(down_proj[e].shape) != (H, I):
+            raise ValueError(f"weights_from_checkpoint: expert {e}: down_proj must be {(H, I)}")
+        w13[e, :I].copy_(gate_proj[e])
+        w13[e, I:].copy_(up_proj[e])
+        w2[e].copy_(down_proj[e])
+    w13l, w2l = w13.transpose(1, 2), w2.transpose(1, 2)
+    if not quantize:
+        return w13l, w2l
+    _require_cuda(w13l)
+    return quantize_weights_int8(w13l, w2l)
+
+
 # ---------------------------------------------------------------------------
 # Building blocks (each one C-ABI call)
 
