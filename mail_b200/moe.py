@@ -240,6 +240,100 @@ def quantize_weights_int8(w13: torch.Tensor, w2: torch.Tensor):
 # The op
 
 
+def _check_shapes(x, w13, w2):
+    if x.dim() != 2 or w13.dim() != 3 or w2.dim() != 3:
+        raise ValueError("fused_moe_mlp: expected x [T, H], w13 [E, H, 2I], w2 [E, I, H]")
+    T, H = x.shape
+    E, Hw, two_i = w13.shape
+    inter = two_i // 2
+    if Hw != H or two_i != 2 * inter or tuple(w2.shape) != (E, inter, H):
+        raise ValueError(f"fused_moe_mlp: shape mismatch x{tuple(x.shape)} w13{tuple(w13.shape)} "
+                         f"w2{tuple(w2.shape)} (expected w13 [E, H, 2I], w2 [E, I, H])")
+    return T, H, E, inter
+
+
+def _prerouted_impl(x, w13, w2, group_sizes):
+    """moe_fused_mlp: the reference's call on pre-grouped rows."""
+    _require_cuda(x, w13, w2, group_sizes)
+    T, H, E, inter = _check_shapes(x, w13, w2)
+    x = x.contiguous()
+    w13k, w2k = kmajor(w13), kmajor(w2)
+    dev = x.device
+    gs = group_sizes
+    if gs.numel() != E:
+        raise ValueError("fused_moe_mlp: group_sizes must have E entries")
+    if gs.dtype not in (torch.int32, torch.int64):
+        gs = gs.to(torch.int64)
+    gs = gs.contiguous()
+    if w13.dtype != x.dtype or w2.dtype != x.dtype:
+        raise TypeError("fused_moe_mlp: x, w13 and w2 must share a dtype")
+    out = torch.empty((T, H), dtype=x.dtype, device=dev)
+    ws = _workspace(_lib.query("moe_fused_mlp_workspace_size", T, H, inter, E, _code(x), 128), dev)
+    _lib.call("moe_fused_mlp", x.data_ptr(), _code(x), T, H, w13k.data_ptr(), w2k.data_ptr(), E, inter,
+              gs.data_ptr(), _code(gs), 128, out.data_ptr(), ws.data_ptr(), ws.numel(), _stream(dev))
+    return out
+
+
+def _topk_impl(x, w13, w2, topk_weights, topk_ids, w13_scale, w2_scale):
+    """moe_fused_experts: align -> GEMMs -> weighted combine."""
+    _require_cuda(x, w13, w2, topk_weights, topk_ids)
+    T, H, E, inter = _check_shapes(x, w13, w2)
+    x = x.contiguous()
+    w13k, w2k = kmajor(w13), kmajor(w2)
+    dev = x.device
+    topk_weights = topk_weights.to(torch.float32).contiguous()
+    ids = topk_ids.to(torch.int32).contiguous()
+    if topk_weights.shape != ids.shape or ids.dim() != 2 or ids.shape[0] != T:
+        raise ValueError("fused_moe_mlp: topk_weights/topk_ids must both be [T, k]")
+    k = ids.shape[1]
+    w_code = _code(w13)
+    s13 = s2 = None
+    if w13.dtype == torch.int8:
+        if w13_scale is None or w2_scale is None:
+            raise ValueError("fused_moe_mlp: int8 weights need scales=(w13_scale, w2_scale)")
+        s13, s2 = w13_scale.to(torch.float32).contiguous(), w2_scale.to(torch.float32).contiguous()
+        if tuple(s13.shape) != (E, 2 * inter) or tuple(s2.shape) != (E, H):
+            raise ValueError("fused_moe_mlp: scales must be w13_scale [E, 2I] and w2_scale [E, H]")
+    elif w13.dtype != x.dtype or w2.dtype != x.dtype:
+        raise TypeError("fused_moe_mlp: weights must share x's dtype or be int8")
+    y = torch.empty((T, H), dtype=x.dtype, device=dev)
+    ws = _workspace(_lib.query("moe_fused_experts_workspace_size", T, H, inter, E, k, _code(x), w_code), dev)
+    _lib.call("moe_fused_experts", x.data_ptr(), _code(x), T, H, w13k.data_ptr(), w2k.data_ptr(), w_code, E, inter,
+              topk_weights.data_ptr(), ids.data_ptr(), k, _ptr(s13), _ptr(s2), y.data_ptr(), ws.data_ptr(),
+              ws.numel(), _stream(dev))
+    return y
+
+
+# The two forms as PyTorch operators (torch.ops.mail_b200.*), so a
+# torch.compile'd MoE layer sees one opaque op per call instead of a graph
+# break; the fake (meta) kernels give the output shape and dtype for tracing.
+@torch.library.custom_op("mail_b200::fused_moe_mlp", mutates_args=())
+def _op_prerouted(x: torch.Tensor, w13: torch.Tensor, w2: torch.Tensor, group_sizes: torch.Tensor) -> torch.Tensor:
+    return _prerouted_impl(x, w13, w2, group_sizes)
+
+
+@_op_prerouted.register_fake
+def _(x, w13, w2, group_sizes):
+    T, H, E, _ = _check_shapes(x, w13, w2)
+    if group_sizes.numel() != E:
+        raise ValueError("fused_moe_mlp: group_sizes must have E entries")
+    return x.new_empty((T, H))
+
+
+@torch.library.custom_op("mail_b200::fused_experts", mutates_args=())
+def _op_topk(x: torch.Tensor, w13: torch.Tensor, w2: torch.Tensor, topk_weights: torch.Tensor,
+             topk_ids: torch.Tensor, w13_scale: torch.Tensor | None, w2_scale: torch.Tensor | None) -> torch.Tensor:
+    return _topk_impl(x, w13, w2, topk_weights, topk_ids, w13_scale, w2_scale)
+
+
+@_op_topk.register_fake
+def _(x, w13, w2, topk_weights, topk_ids, w13_scale, w2_scale):
+    T, H, _, _ = _check_shapes(x, w13, w2)
+    if topk_weights.shape != topk_ids.shape or topk_ids.dim() != 2 or topk_ids.shape[0] != T:
+        raise ValueError("fused_moe_mlp: topk_weights/topk_ids must both be [T, k]")
+    return x.new_empty((T, H))
+
+
 def fused_moe_mlp(x: torch.Tensor, w13: torch.Tensor, w2: torch.Tensor, group_sizes_or_topk_weights: torch.Tensor,
                   topk_ids: torch.Tensor | None = None, scales=None, BLOCK_M: int = 128, BLOCK_N: int = 128,
                   BLOCK_N2: int = 256, BLOCK_K: int = 256) -> torch.Tensor:
@@ -253,61 +347,28 @@ def fused_moe_mlp(x: torch.Tensor, w13: torch.Tensor, w2: torch.Tensor, group_si
     Top-k form: x [T, H], topk_weights [T, k] (fp32), topk_ids [T, k]; returns
     y [T, H] = sum_j topk_weights[t, j] * MLP_{topk_ids[t, j]}(x[t]) in x.dtype.
     int8 w13/w2 select w8a8 with scales=(w13_scale [E, 2I], w2_scale [E, H])
-    and dynamic per-token activation quantisation.
+    and dynamic per-token activation quantisation. The combine adds each
+    token's k weighted rows with fp32 atomics while the [T, H] fp32
+    accumulator fits in L2 (T * H * 4 <= 80 MiB), so the order of those adds,
+    and with it the last bit of a bf16 output, can differ from run to run
+    (by at most one bf16 rounding step); larger outputs use a deterministic
+    row-store combine.
 
+    Under torch.compile the call is one operator (torch.ops.mail_b200.
+    fused_moe_mlp / fused_experts); eager calls go straight to the library.
     BLOCK_* are accepted for signature compatibility; the sm_100a kernels use
     fixed 128 x 256 tiles and results do not depend on them.
     """
     del BLOCK_M, BLOCK_N, BLOCK_N2, BLOCK_K
-    _require_cuda(x, w13, w2, group_sizes_or_topk_weights, topk_ids)
-    if x.dim() != 2 or w13.dim() != 3 or w2.dim() != 3:
-        raise ValueError("fused_moe_mlp: expected x [T, H], w13 [E, H, 2I], w2 [E, I, H]")
-    T, H = x.shape
-    E, Hw, two_i = w13.shape
-    inter = two_i // 2
-    if Hw != H or two_i != 2 * inter or tuple(w2.shape) != (E, inter, H):
-        raise ValueError(f"fused_moe_mlp: shape mismatch x{tuple(x.shape)} w13{tuple(w13.shape)} "
-                         f"w2{tuple(w2.shape)} (expected w13 [E, H, 2I], w2 [E, I, H])")
-    x = x.contiguous()
-    w13k, w2k = kmajor(w13), kmajor(w2)
-    dev = x.device
-    st = _stream(dev)
+    compiling = torch.compiler.is_compiling()
     if topk_ids is None:
-        gs = group_sizes_or_topk_weights
-        if gs.numel() != E:
-            raise ValueError("fused_moe_mlp: group_sizes must have E entries")
-        if gs.dtype not in (torch.int32, torch.int64):
-            gs = gs.to(torch.int64)
-        gs = gs.contiguous()
-        if w13.dtype != x.dtype or w2.dtype != x.dtype:
-            raise TypeError("fused_moe_mlp: x, w13 and w2 must share a dtype")
-        out = torch.empty((T, H), dtype=x.dtype, device=dev)
-        ws = _workspace(_lib.query("moe_fused_mlp_workspace_size", T, H, inter, E, _code(x), 128), dev)
-        _lib.call("moe_fused_mlp", x.data_ptr(), _code(x), T, H, w13k.data_ptr(), w2k.data_ptr(), E, inter,
-                  gs.data_ptr(), _code(gs), 128, out.data_ptr(), ws.data_ptr(), ws.numel(), st)
-        return out
-
-    topk_weights = group_sizes_or_topk_weights.to(torch.float32).contiguous()
-    ids = topk_ids.to(torch.int32).contiguous()
-    if topk_weights.shape != ids.shape or ids.dim() != 2 or ids.shape[0] != T:
-        raise ValueError("fused_moe_mlp: topk_weights/topk_ids must both be [T, k]")
-    k = ids.shape[1]
-    w_code = _code(w13)
-    s13 = s2 = None
-    if w13.dtype == torch.int8:
-        if scales is None:
-            raise ValueError("fused_moe_mlp: int8 weights need scales=(w13_scale, w2_scale)")
-        s13, s2 = (s.to(torch.float32).contiguous() for s in scales)
-        if tuple(s13.shape) != (E, 2 * inter) or tuple(s2.shape) != (E, H):
-            raise ValueError("fused_moe_mlp: scales must be w13_scale [E, 2I] and w2_scale [E, H]")
-    elif w13.dtype != x.dtype or w2.dtype != x.dtype:
-        raise TypeError("fused_moe_mlp: weights must share x's dtype or be int8")
-    y = torch.empty((T, H), dtype=x.dtype, device=dev)
-    ws = _workspace(_lib.query("moe_fused_experts_workspace_size", T, H, inter, E, k, _code(x), w_code), dev)
-    _lib.call("moe_fused_experts", x.data_ptr(), _code(x), T, H, w13k.data_ptr(), w2k.data_ptr(), w_code, E, inter,
-              topk_weights.data_ptr(), ids.data_ptr(), k, _ptr(s13), _ptr(s2), y.data_ptr(), ws.data_ptr(),
-              ws.numel(), st)
-    return y
+        if compiling:
+            return torch.ops.mail_b200.fused_moe_mlp(x, w13, w2, group_sizes_or_topk_weights)
+        return _prerouted_impl(x, w13, w2, group_sizes_or_topk_weights)
+    s13, s2 = scales if scales is not None else (None, None)
+    if compiling:
+        return torch.ops.mail_b200.fused_experts(x, w13, w2, group_sizes_or_topk_weights, topk_ids, s13, s2)
+    return _topk_impl(x, w13, w2, group_sizes_or_topk_weights, topk_ids, s13, s2)
 
 
 def fused_expert_rows(x: torch.Tensor, w13: torch.Tensor, w2: torch.Tensor, expert_ids: torch.Tensor,
