@@ -11,13 +11,29 @@ op directly every step).
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config NAME]
 
 With N > 1 (torchrun) every rank runs the expert-parallel layer on its own
-T tokens (weak scaling): experts are sharded E/N per rank and tokens travel
-to their experts and back with NCCL all-to-all (mail_b200.ep).
+T tokens (weak scaling): experts are sharded E/N per rank and token rows
+travel to their experts and back over NVLink peer memory (mail_b200.ep).
+
+One JSON line (rank 0). Besides the contract keys it carries:
+  roofline    the gate_up GEMM's achieved rate against the measured peak; its
+              per-launch time comes from the library's device-side kernel
+              clocks read over the timed region itself (CUDA-event stage
+              times from a separate replay are reported beside it)
+  sustained   the same step replayed back to back for >= 1.5 s (power-capped
+              clocks), against the sustained bf16 peak
+  configs     the other workloads at their own shapes: N=1 — Qwen3-30B-A3B
+              decode (T = 1, 8, 32, 128, 256), DeepSeek-V3 w8a8 prefill, the
+              load-imbalance stress; N>1 — DeepSeek-V3 w8a8 expert-parallel
+              with 8192 tokens per GPU (weak) and 8192 in total (strong);
+              each with its own gate_up roofline (HBM for decode, int8 tensor
+              against a measured int8 GEMM yardstick for w8a8)
 """
 from __future__ import annotations
 
 import argparse
+import ctypes
 import json
+import math
 import os
 import statistics
 import subprocess
@@ -319,238 +335,310 @@ def cpu_reference_run(cfg, steps: int, warmup: int, time_limit_s: float = 20.0):
                        f"{'w8a8 ' if cfg['quant'] else ''}fp32 numpy per-expert loop, {threads} BLAS threads")
 
 
-# --------------------------------------------------------------------------- our arm
+# --------------------------------------------------------------------------- our arm: measurement helpers
+
+DECODE_TOKENS = (1, 8, 32, 128, 256)
+L2_BYTES = 126e6
 
 
-def main():
-    ap = argparse.ArgumentParser()
-    ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--config", default="mixtral", choices=sorted(CONFIGS))
-    ap.add_argument("--tokens", type=int, default=0, help="override tokens per GPU (profiling cases)")
-    ap.add_argument("--ep", default="peer", choices=["peer", "nccl"],
-                    help="expert-parallel exchange (N > 1): fused into the kernels over NVLink peer memory, "
-                         "or NCCL all-to-all")
-    ap.add_argument("--gemm", default="auto", choices=["auto", "pair", "single"],
-                    help="grouped GEMM variant: CTA pairs (cta_group::2), one CTA per tile, or chosen by size")
-    ap.add_argument("--band", type=int, default=0, help="GEMM tile-order band width in M tiles (0: default)")
-    ap.add_argument("--pdl", type=int, default=1, choices=[0, 1],
-                    help="launch the kernels with programmatic dependent launch (1, default)")
-    ap.add_argument("--half-units", type=int, default=1, choices=[0, 1],
-                    help="CTA-pair GEMMs: each expert's odd last M tile as an M=128 pair MMA (1, default)")
-    ap.add_argument("--eager", action="store_true",
-                    help="N=1: call the op directly each step instead of replaying it from a captured CUDA graph")
-    ap.add_argument("--no-cpu-baseline", action="store_true")
-    args = ap.parse_args()
-    args.warmup = max(args.warmup, 3)
-    args.graph = not args.eager
-    cfg = dict(CONFIGS[args.config])
-    if args.tokens:
-        cfg["T"] = args.tokens
-        cfg["desc"] += f" (T={args.tokens})"
-
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
-    T, H, I, E, k = cfg["T"], cfg["H"], cfg["I"], cfg["E"], cfg["k"]
-    dtype_name = "int8" if cfg["quant"] else cfg["dtype"]
-    config_json = {"workload": cfg["desc"], "tokens_per_gpu": T, "hidden": H, "inter": I, "experts": E,
-                   "top_k": k, "routing": cfg["routing"], "dtype": cfg["dtype"] + ("+w8a8" if cfg["quant"] else ""),
-                   "parallelism": f"ep{world}" if world > 1 else "single", "gemm": args.gemm,
-                   "half_units": bool(args.half_units), "pdl": bool(args.pdl),
-                   "ep_exchange": args.ep if world > 1 else None, "cuda_graph": bool(args.graph and world == 1)}
-
-    # When one step's active expert weights fit in the L2 (decode-sized
-    # batches), consecutive steps cycle through several routings that touch
-    # different experts, so the weights stream from HBM as they would in
-    # serving instead of being L2 hits of the previous step.
-    L2_BYTES = 126e6
+def n_variants(cfg, T, world, rank):
+    """Routings a step cycles through: when one step's active expert weights
+    fit in the L2 (decode-sized batches), consecutive steps route to
+    different experts so the weights stream from HBM as in serving."""
     wbytes = 1 if cfg["quant"] else (4 if cfg["dtype"] == "fp32" else 2)
-    ids0, _ = make_routing(cfg["routing"], T, E, k, seed=rank)
-    active_bytes = len(np.unique(ids0)) * 3 * H * I * wbytes
-    n_var = 1 if world > 1 or active_bytes >= 2 * L2_BYTES else int(min(16, -(-3 * L2_BYTES // active_bytes)))
-    if n_var > 1:
-        config_json["l2"] = ("active weights of one step (%.0f MB) fit in the 126 MB L2: steps cycle through %d "
-                             "routings touching different experts" % (active_bytes / 1e6, n_var))
-    else:
-        config_json["l2"] = "active weights of one step (%.2f GB) exceed the 126 MB L2, streamed every step" % (
+    ids0, _ = make_routing(cfg["routing"], T, cfg["E"], cfg["k"], seed=rank)
+    active_bytes = len(np.unique(ids0)) * 3 * cfg["H"] * cfg["I"] * wbytes
+    if world > 1 or active_bytes >= 2 * L2_BYTES:
+        return 1, "active weights of one step (%.2f GB) exceed the 126 MB L2, streamed every step" % (
             active_bytes / 1e9)
+    n = int(min(16, -(-3 * L2_BYTES // active_bytes)))
+    return n, ("active weights of one step (%.0f MB) fit in the 126 MB L2: steps cycle through %d routings "
+               "touching different experts" % (active_bytes / 1e6, n))
 
-    if args.impl == "reference":
-        if rank != 0:
-            return 0
-        ref = cpu_reference_run(cfg, args.steps, args.warmup)
-        line = {"metric": "fused MoE MLP tokens/s", "value": ref["value"], "unit": "tokens/s", "n_gpus": world,
-                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ref["seconds_per_step"] * 1e3,
-                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-                "data": "synthetic", "config": config_json, "impl": "reference",
-                "cpu_baseline": {"value": ref["value"], "unit": "tokens/s", "cores": ref["cores"], "kind": "port",
-                                 "sample": ref["sample"]},
-                "e2e": {"value": ref["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
-                        "d2h_bytes_per_step": 0}}
-        print(json.dumps(line), flush=True)
-        return 0
 
-    import torch
-    import torch.distributed as dist
+class Ctx:
+    """Per-process handles the measurement helpers share."""
 
-    import mail_b200 as mb
-    from mail_b200 import _lib
+    def __init__(self, torch, dist, lib, device, local_rank, world, rank):
+        self.torch, self.dist, self.lib = torch, dist, lib
+        self.device, self.local_rank, self.world, self.rank = device, local_rank, world, rank
+        self.stream = torch.cuda.current_stream(device)
 
-    torch.cuda.set_device(local_rank)
-    device = torch.device("cuda", local_rank)
-    if world > 1:
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
-    lib = _lib.load()
-    lib.moe_set_option(_lib.OPT_GEMM_CTA_PAIR, {"pair": 1, "single": 0, "auto": 2}[args.gemm])
-    if args.band:
-        lib.moe_set_option(_lib.OPT_GEMM_BAND, args.band)
-    lib.moe_set_option(_lib.OPT_GEMM_HALF_UNITS, args.half_units)
-    lib.moe_set_option(_lib.OPT_PDL, args.pdl)
+    def barrier(self):
+        if self.world > 1:
+            self.dist.barrier(device_ids=[self.local_rank])
 
-    x, ids, wts, dt = make_inputs(cfg, rank, device)
-    variants = [(x, ids, wts)] + [make_inputs(cfg, rank, device, v)[:3] for v in range(1, n_var)]
+    def max_over_ranks(self, v: float) -> float:
+        if self.world == 1:
+            return v
+        t = self.torch.tensor([v], device=self.device, dtype=self.torch.float64)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return float(t.item())
 
-    def inp(i):
-        return variants[i % n_var]
+    def kernel_clocks(self, reset=True):
+        """(total_ns, launches) per kernel class since the last reset."""
+        from mail_b200 import _lib
+        tot = (ctypes.c_uint64 * _lib.NUM_CLOCKS)()
+        cnt = (ctypes.c_uint64 * _lib.NUM_CLOCKS)()
+        _lib.call("moe_kernel_clocks", tot, cnt, _lib.NUM_CLOCKS, int(reset), self.stream.cuda_stream)
+        return list(tot), list(cnt)
 
-    if world > 1:
-        from mail_b200 import ep as mep
-        assert E % world == 0, "experts must divide evenly over ranks"
-        args.graph = False  # the expert-parallel layer is called directly (host-side plan per call)
-        local = list(range(rank * E // world, (rank + 1) * E // world))
-        w13, w2, scales = make_weights(cfg, local, device, dt)
-        if args.ep == "peer":
-            layer = mep.PeerExpertParallelMoE(w13, w2, E, max_tokens=T, top_k=k, dtype=dt, scales=scales)
-        else:
-            layer = mep.ExpertParallelMoE(w13, w2, E, scales=scales)
 
-        def step(xx, ii, ww):
-            return layer(xx, ww, ii)
-    elif cfg.get("prerouted"):
-        # the reference's call: rows already grouped by expert (T*k of them),
-        # group sizes per expert (fused_moe_mlp_triton.py:121, unquant_diff.txt:13-18)
-        w13, w2, scales = make_weights(cfg, list(range(E)), device, dt)
-        args.graph = False
-        order = torch.argsort(ids.reshape(-1).to(torch.int64), stable=True)
-        x = x[order // k].contiguous()  # the step's input: T * k grouped rows
-        group_sizes = torch.bincount(ids.reshape(-1).to(torch.int64), minlength=E)
-
-        def step(xx, ii, ww):
-            return mb.fused_moe_mlp(xx, w13, w2, group_sizes)
-    else:
-        w13, w2, scales = make_weights(cfg, list(range(E)), device, dt)
-        if args.graph:
-            captured = mb.CapturedMoeMLP(w13, w2, T, k, dtype=dt, scales=scales)
-
-            def step(xx, ii, ww):
-                return captured(xx, ww, ii)
-        else:
-            def step(xx, ii, ww):
-                return mb.fused_moe_mlp(xx, w13, w2, ww, ii, scales=scales)
-
-    stream = torch.cuda.current_stream(device)
-
-    def barrier():
-        if world > 1:
-            dist.barrier(device_ids=[local_rank])
-
-    # ---- warm-up
-    for i in range(args.warmup):
-        step(*inp(i))
+def timed_region(ctx, step, inp, steps, kernels_per_step=None, sample_clocks=True):
+    """Times exactly `steps` calls of step(*inp(i)) on the device (CUDA
+    events on the launching stream, barrier + synchronize on both sides, max
+    over ranks), with NVML clocks sampled during the region and the library's
+    kernel clocks read over it."""
+    torch, lib = ctx.torch, ctx.lib
+    sampler = ClockSampler(ctx.local_rank) if sample_clocks else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    ctx.barrier()
     torch.cuda.synchronize()
-
-    # ---- timed region (device-resident inputs), per-stage events every step
-    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(STAGES)] for _ in range(args.steps)]
-    handles = [(torch.cuda.Event(enable_timing=True)) for _ in range(2)]
-    import ctypes
-    for row in ev:  # torch creates events lazily: record once so the handles exist
-        for e in row:
-            e.record(stream)
-    torch.cuda.synchronize()
-    ev_arrays = [(ctypes.c_void_p * STAGES)(*[e.cuda_event for e in row]) for row in ev]
-    assert all(e.cuda_event for row in ev for e in row)
-    sampler = ClockSampler(local_rank)
-    sampler.start()
-    time.sleep(0.3)
-    barrier()
-    torch.cuda.synchronize()
+    ctx.kernel_clocks(reset=True)
     launches0 = lib.moe_launch_count()
-    t_region0 = time.time()
-    handles[0].record(stream)
-    for i in range(args.steps):
-        if not args.graph:
-            lib.moe_set_stage_events(ev_arrays[i], STAGES)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0 = time.time()
+    e0.record(ctx.stream)
+    for i in range(steps):
         step(*inp(i))
-    lib.moe_set_stage_events(None, 0)
-    handles[1].record(stream)
+    e1.record(ctx.stream)
     torch.cuda.synchronize()
-    t_region1 = time.time()
-    barrier()
-    clocks = sampler.stop(t_region0, t_region1)
+    t1 = time.time()
+    ctx.barrier()
+    clocks = sampler.stop(t0, t1) if sampler else None
     launches = lib.moe_launch_count() - launches0
-    ms = handles[0].elapsed_time(handles[1]) / args.steps
-    stage_rows = None
-    stage_source = "eager calls, stage events recorded by the library"
-    if args.graph:
-        # replays launch the captured kernels without going through the
-        # library. Stage times: a second capture of the same op with the
-        # library's stage events as graph nodes, replayed once per timed
-        # step right after the timed region
-        launches = captured.kernels * args.steps
-        try:
-            lib.moe_set_stage_events(ev_arrays[0], STAGES)
-            try:
-                cap_ev = mb.CapturedMoeMLP(w13, w2, T, k, dtype=dt, scales=scales)
-            finally:
-                lib.moe_set_stage_events(None, 0)
-            stage_rows = []
-            for i in range(args.steps):
-                xv, iv, wv = inp(i)
-                cap_ev(xv, wv, iv)
-                torch.cuda.synchronize()
-                stage_rows.append([ev[0][j].elapsed_time(ev[0][j + 1]) for j in range(STAGES - 1)])
-            del cap_ev
-            stage_source = "graph replay with the stage events as graph nodes"
-        except Exception:
-            stage_rows = None
-        if stage_rows is None:
-            for i in range(args.steps):
-                lib.moe_set_stage_events(ev_arrays[i], STAGES)
-                xv, iv, wv = inp(i)
-                mb.fused_moe_mlp(xv, w13, w2, wv, iv, scales=scales)
-            lib.moe_set_stage_events(None, 0)
+    if kernels_per_step is not None:  # graph replays bypass the library's launch counter
+        launches = kernels_per_step * steps
+    tot, cnt = ctx.kernel_clocks(reset=True)
+    ms = ctx.max_over_ranks(e0.elapsed_time(e1) / steps)
+    kc = {}
+    for name, i in (("gate_up", 0), ("down", 1)):
+        per = tot[i] / cnt[i] / 1e6 if cnt[i] else float("nan")
+        kc[name] = {"ms_per_launch": ctx.max_over_ranks(per), "launches": int(cnt[i])}
+    return {"ms": ms, "seconds": t1 - t0, "clocks": clocks, "launches": int(launches), "kernel_clocks": kc}
+
+
+def int8_yardstick(ctx):
+    """Measured int8 tensor-core yardstick: torch._int_mm (cuBLASLt int8 x
+    int8 -> int32) on 8192^3, best of 10 launches after 3 warm-ups; None if
+    the build lacks it."""
+    torch = ctx.torch
+    n = 8192
+    try:
+        a = torch.randint(-127, 128, (n, n), dtype=torch.int8, device=ctx.device)
+        b = torch.randint(-127, 128, (n, n), dtype=torch.int8, device=ctx.device).t().contiguous().t()
+        for _ in range(3):
+            torch._int_mm(a, b)
+        best = float("inf")
+        for _ in range(10):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(ctx.stream)
+            torch._int_mm(a, b)
+            e1.record(ctx.stream)
             torch.cuda.synchronize()
-    if stage_rows is None:
-        stage_rows = [[row[j].elapsed_time(row[j + 1]) for j in range(STAGES - 1)] for row in ev]
+            best = min(best, e0.elapsed_time(e1))
+        del a, b
+        return {"tops": 2.0 * n ** 3 / (best / 1e3) / 1e12, "ms": best,
+                "how": "torch._int_mm int8 %d^3 (cuBLASLt, int32 out), best of 10" % n}
+    except Exception as exc:  # pragma: no cover - depends on the torch build
+        return {"tops": None, "error": str(exc)[:200]}
 
-    def stage_ms(a, b):
-        return statistics.mean(sum(r[a:b]) for r in stage_rows)
 
-    st_ms = {"route": stage_ms(0, 1), "gather": stage_ms(1, 2), "gemm1": stage_ms(2, 3), "pre_gemm2": stage_ms(3, 4),
-             "gemm2": stage_ms(4, 5), "finalize": stage_ms(5, 6), "source": stage_source}
-    if world > 1:
-        t = torch.tensor([ms], device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+def gate_up_roofline(cfg, T, world, id_sets, gemm1_ms, peaks, int8, sustained):
+    """Algorithmic work of one gate_up launch and its achieved rate: FLOPs
+    2 * S * H * 2I (S routed slots), bytes = w13 of the experts with slots +
+    the padded activation rows read + the h rows written; bound = the larger
+    of FLOPs / tensor peak and bytes / HBM peak (the measured peaks)."""
+    H, I, E, k = cfg["H"], cfg["I"], cfg["E"], cfg["k"]
+    wb = 1 if cfg["quant"] else (4 if cfg["dtype"] == "fp32" else 2)
+    hb = 4 if cfg["dtype"] == "fp32" else 2
+    S = T * k
+    if world == 1:
+        acts, rows = [], []
+        for ids in id_sets:
+            counts = np.bincount(ids.reshape(-1), minlength=E)
+            acts.append(int((counts > 0).sum()))
+            rows.append(int(((counts + 127) // 128 * 128).sum()))
+        active, rows_pad = float(np.mean(acts)), float(np.mean(rows))
+    else:  # this rank's experts under balanced routing
+        active = E // world
+        rows_pad = S + active * 64
+    flops = 2.0 * S * H * 2 * I
+    nbytes = active * 2.0 * I * H * wb + rows_pad * H * wb + rows_pad * I * hb
+    if cfg["quant"]:
+        if int8 and int8.get("tops"):
+            tc_peak, tc_src = int8["tops"], "measured int8 GEMM (%s)" % int8["how"]
+        else:
+            tc_peak, tc_src = 2.0 * peaks["bf16"], "2 x measured bf16 (no int8 yardstick)"
+    else:
+        tc_peak = peaks["bf16_sus"] if sustained else peaks["bf16"]
+        tc_src = "%s bf16 %s" % (peaks["source"], "sustained" if sustained else "burst")
+    s = gemm1_ms / 1e3
+    tensor_rate, hbm_rate = flops / s / 1e12, nbytes / s / 1e9
+    tensor_bound = flops / (tc_peak * 1e12) >= nbytes / (peaks["hbm"] * 1e9)
+    r = {"kernel": "moe_gemm_kernel<SWIGLU> (gate_up GEMM + SwiGLU)", "bound": "tensor" if tensor_bound else "hbm",
+         "flops_per_launch": flops, "bytes_per_launch": nbytes, "active_experts": active,
+         "ms_per_launch": gemm1_ms, "frac_tensor": tensor_rate / tc_peak, "frac_hbm": hbm_rate / peaks["hbm"]}
+    if tensor_bound:
+        r.update(achieved=tensor_rate, peak=tc_peak, unit="TOP/s" if cfg["quant"] else "TFLOP/s",
+                 frac=tensor_rate / tc_peak, peak_source=tc_src)
+        spec = 4500.0 if cfg["quant"] else 2250.0
+    else:
+        r.update(achieved=hbm_rate, peak=peaks["hbm"], unit="GB/s", frac=hbm_rate / peaks["hbm"],
+                 peak_source=f"{peaks['source']} HBM copy")
+        spec = 7700.0
+    r.update(spec_peak=spec, frac_of_spec=r["achieved"] / spec)
+    return r
 
-    # ---- end to end through the public API: every step copies its inputs
-    # from pinned host memory and its result back to pinned host memory. The
-    # copies run on their own streams (host->device, device->host) with two
-    # device buffers, so step i+1's upload and step i-1's download overlap
-    # step i's compute, as a serving loop would run them.
+
+def build_single(ctx, cfg, T, n_var, graph, weights=None):
+    """One-GPU workload: inputs (n_var routings), weights, and a step that
+    replays the op from a CUDA graph (or calls it)."""
+    import mail_b200 as mb
+
+    torch, device = ctx.torch, ctx.device
+    x, ids, wts, dt = make_inputs(cfg, ctx.rank, device)
+    variants = [(x, ids, wts)] + [make_inputs(cfg, ctx.rank, device, v)[:3] for v in range(1, n_var)]
+    if weights is None:
+        weights = make_weights(cfg, list(range(cfg["E"])), device, dt)
+    w13, w2, scales = weights
+    kernels = None
+    if cfg.get("prerouted"):
+        order = torch.argsort(ids.reshape(-1).to(torch.int64), stable=True)
+        xg = x[order // cfg["k"]].contiguous()  # T * k rows grouped by expert
+        gs = torch.bincount(ids.reshape(-1).to(torch.int64), minlength=cfg["E"])
+        variants = [(xg, ids, wts)]
+
+        def step(xx, ii, ww):
+            return mb.fused_moe_mlp(xx, w13, w2, gs)
+        captured = None
+    elif graph:
+        captured = mb.CapturedMoeMLP(w13, w2, T, cfg["k"], dtype=dt, scales=scales)
+        kernels = captured.kernels
+
+        def step(xx, ii, ww):
+            return captured(xx, ww, ii)
+    else:
+        captured = None
+
+        def step(xx, ii, ww):
+            return mb.fused_moe_mlp(xx, w13, w2, ww, ii, scales=scales)
+    return dict(step=step, variants=variants, weights=weights, captured=captured, kernels=kernels, dt=dt,
+                inp=lambda i: variants[i % len(variants)])
+
+
+def build_ep(ctx, cfg, T, ep_kind):
+    """Expert-parallel workload on this rank: its E / N experts, T tokens."""
+    from mail_b200 import ep as mep
+
+    E, world, rank = cfg["E"], ctx.world, ctx.rank
+    assert E % world == 0, "experts must divide evenly over ranks"
+    x, ids, wts, dt = make_inputs(cfg, rank, ctx.device)
+    local = list(range(rank * E // world, (rank + 1) * E // world))
+    w13, w2, scales = make_weights(cfg, local, ctx.device, dt)
+    if ep_kind == "peer":
+        layer = mep.PeerExpertParallelMoE(w13, w2, E, max_tokens=T, top_k=cfg["k"], dtype=dt, scales=scales)
+    else:
+        layer = mep.ExpertParallelMoE(w13, w2, E, scales=scales)
+
+    def step(xx, ii, ww):
+        return layer(xx, ww, ii)
+    variants = [(x, ids, wts)]
+    return dict(step=step, variants=variants, weights=(w13, w2, scales), layer=layer, kernels=None, dt=dt,
+                captured=None, inp=lambda i: variants[0])
+
+
+def close_workload(ctx, w):
+    layer = w.get("layer")
+    if layer is not None and hasattr(layer, "close"):
+        layer.close()
+    w.clear()
+    ctx.torch.cuda.synchronize()
+    ctx.torch.cuda.empty_cache()
+
+
+def run_config(ctx, name, T, args, peaks, int8, weights=None, steps=None, warmup=3, ep_kind="peer"):
+    """A sub-configuration of the line: build, warm up, time, roofline."""
+    cfg = dict(CONFIGS[name])
+    cfg["T"] = T
+    steps = steps or args.steps
+    if ctx.world > 1:
+        w = build_ep(ctx, cfg, T, ep_kind)
+        n_var, l2 = 1, "expert-parallel, weights streamed every step"
+    else:
+        n_var, l2 = n_variants(cfg, T, 1, ctx.rank)
+        w = build_single(ctx, cfg, T, n_var, graph=True, weights=weights)
+    for i in range(warmup):
+        w["step"](*w["inp"](i))
+    ctx.torch.cuda.synchronize()
+    r = timed_region(ctx, w["step"], w["inp"], steps, kernels_per_step=w["kernels"])
+    ids_sets = [v[1].cpu().numpy() for v in w["variants"]]
+    roof = gate_up_roofline(cfg, T, ctx.world, ids_sets, r["kernel_clocks"]["gate_up"]["ms_per_launch"], peaks,
+                            int8, sustained=False)
+    out = {"workload": cfg["desc"].split(" (")[0] + f" T={T}" + ("" if ctx.world == 1 else f" per GPU x {ctx.world}"),
+           "tokens_per_gpu": T, "hidden": cfg["H"], "inter": cfg["I"], "experts": cfg["E"], "top_k": cfg["k"],
+           "routing": cfg["routing"], "dtype": cfg["dtype"] + ("+w8a8" if cfg["quant"] else ""),
+           "value": ctx.world * T / (r["ms"] / 1e3), "unit": "tokens/s", "ms_per_step": r["ms"], "steps": steps,
+           "kernel_clocks": r["kernel_clocks"], "roofline": roof, "clocks": r["clocks"], "l2": l2}
+    if ctx.world == 1:
+        # the step's own weight-streaming bound: every active expert's three
+        # matrices once at the measured copy rate
+        wb = 1 if cfg["quant"] else 2
+        bound_ms = roof["active_experts"] * 3.0 * cfg["H"] * cfg["I"] * wb / (peaks["hbm"] * 1e9) * 1e3
+        out["weight_stream_bound_ms"] = bound_ms
+    keep = w.get("weights") if weights is not None else None
+    close_workload(ctx, w)
+    return out, keep
+
+
+def sub_configs(ctx, args, peaks, int8):
+    """The workloads beside the headline, at their own shapes."""
+    res = {}
+    if ctx.world == 1:
+        cfg = dict(CONFIGS["qwen3-decode"])
+        weights = None
+        for T in DECODE_TOKENS:
+            cfg["T"] = T
+            steps = max(args.steps, 200)
+            if weights is None:
+                dt = {"bf16": ctx.torch.bfloat16}[cfg["dtype"]]
+                weights = make_weights(cfg, list(range(cfg["E"])), ctx.device, dt)
+            res[f"qwen3-decode-T{T}"], _ = run_config(ctx, "qwen3-decode", T, args, peaks, int8, weights=weights,
+                                                      steps=steps)
+        del weights
+        ctx.torch.cuda.empty_cache()
+        res["dsv3-w8a8"], _ = run_config(ctx, "dsv3-w8a8", 8192, args, peaks, int8)
+        res["stress-w8a8"], _ = run_config(ctx, "stress-w8a8", 65536, args, peaks, int8, steps=max(5, args.steps // 2))
+    else:
+        res["dsv3-w8a8"], _ = run_config(ctx, "dsv3-w8a8", 8192, args, peaks, int8, ep_kind=args.ep)
+        res["dsv3-w8a8"]["scaling"] = "weak"
+        Ts = 8192 // ctx.world
+        res["dsv3-w8a8-strong"], _ = run_config(ctx, "dsv3-w8a8", Ts, args, peaks, int8, ep_kind=args.ep)
+        res["dsv3-w8a8-strong"].update(scaling="strong", tokens_total=8192)
+    return res
+
+
+def e2e_pass(ctx, w, steps):
+    """End to end through the public API: every step copies its inputs from
+    pinned host memory and its result back to pinned host memory, on their
+    own streams with two device buffers, so step i+1's upload and step i-1's
+    download overlap step i's compute, as a serving loop would run them."""
+    torch = ctx.torch
+    stream = ctx.stream
+    step, variants = w["step"], w["variants"]
+    n_var = len(variants)
     host_in = [tuple(t.cpu().pin_memory() for t in v) for v in variants]
     x_h, ids_h, wts_h = host_in[0]
     NB = 2
-    out_shape = tuple(step(x, ids, wts).shape)
-    y_h = [torch.empty(out_shape, dtype=dt).pin_memory() for _ in range(NB)]
-    x_d = [torch.empty_like(x) for _ in range(NB)]
-    ids_d = [torch.empty_like(ids) for _ in range(NB)]
-    wts_d = [torch.empty_like(wts) for _ in range(NB)]
-    up, down = torch.cuda.Stream(device), torch.cuda.Stream(device)
+    x0, ids0, wts0 = variants[0]
+    out_shape = tuple(step(x0, ids0, wts0).shape)
+    y_h = [torch.empty(out_shape, dtype=w["dt"]).pin_memory() for _ in range(NB)]
+    x_d = [torch.empty_like(x0) for _ in range(NB)]
+    ids_d = [torch.empty_like(ids0) for _ in range(NB)]
+    wts_d = [torch.empty_like(wts0) for _ in range(NB)]
+    up, down = torch.cuda.Stream(ctx.device), torch.cuda.Stream(ctx.device)
     h2d_ev = [torch.cuda.Event() for _ in range(NB)]
     comp_ev = [torch.cuda.Event() for _ in range(NB)]
     d2h_ev = torch.cuda.Event()
@@ -577,114 +665,249 @@ def main():
     for i in range(2 * NB):
         e2e_step(i)
     torch.cuda.synchronize()
-    barrier()
+    ctx.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     up.wait_event(e0)
-    for i in range(args.steps):
+    for i in range(steps):
         e2e_step(i)
     stream.wait_event(d2h_ev)  # the last result is back in host memory
     e1.record(stream)
     torch.cuda.synchronize()
-    e2e_ms = e0.elapsed_time(e1) / args.steps
-    if world > 1:
-        t = torch.tensor([e2e_ms], device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
+    ms = ctx.max_over_ranks(e0.elapsed_time(e1) / steps)
     h2d = x_h.numel() * x_h.element_size() + ids_h.numel() * 4 + wts_h.numel() * 4
     d2h = y_h[0].numel() * y_h[0].element_size()
+    return ms, int(h2d), int(d2h)
 
-    # ---- roofline of the dominant kernel (gate_up GEMM + SwiGLU)
-    peaks = load_peaks()
-    S_local = int(T * k)  # slots per rank (uniform routing keeps the per-rank load ~ T*k)
-    flops_gemm1 = 2.0 * S_local * H * 2 * I
-    gemm1_s = st_ms["gemm1"] / 1e3
-    # algorithmic bytes of one gate_up launch: the weights of the experts that
-    # received slots, the padded activation rows read, the h rows written
-    wb = 1 if cfg["quant"] else (4 if cfg["dtype"] == "fp32" else 2)
-    hb = 4 if cfg["dtype"] == "fp32" else 2
-    if world == 1:
-        counts = np.bincount(ids.cpu().numpy().reshape(-1), minlength=E)
-        active = int((counts > 0).sum())
-        rows_pad = int(((counts + 127) // 128 * 128).sum())
-    else:  # the rank's local experts, balanced routing
-        active = E // world
-        rows_pad = S_local + active * 64
-    bytes_gemm1 = active * 2.0 * I * H * wb + rows_pad * H * wb + rows_pad * I * hb
-    # a timed region shorter than ~1 s runs at boost clocks (burst peak);
-    # longer ones settle under the power cap (sustained peak)
-    region_s = ms * args.steps / 1e3
-    sustained = region_s >= 1.0
-    peak_tc = (peaks["bf16_sus"] if sustained else peaks["bf16"]) * (2.0 if cfg["quant"] else 1.0)
-    tensor_bound = flops_gemm1 / (peak_tc * 1e12) >= bytes_gemm1 / (peaks["hbm"] * 1e9)
-    roofline = {"kernel": "moe_gemm_kernel<SWIGLU> (gate_up GEMM + SwiGLU)",
-                "bound": "tensor" if tensor_bound else "hbm",
-                "flops_per_launch": flops_gemm1, "bytes_per_launch": bytes_gemm1, "active_experts": active,
-                "ms_per_launch": st_ms["gemm1"],
-                # the committed capture is of the one-GPU launch at the default size
-                "traffic": load_traffic(args.config) if not args.tokens and world == 1 else None,
-                "traffic_unit": "bytes"}
-    if tensor_bound:
-        roofline.update(achieved=flops_gemm1 / gemm1_s / 1e12, peak=peak_tc, unit="TFLOP/s",
-                        frac=flops_gemm1 / gemm1_s / 1e12 / peak_tc,
-                        peak_source=f"{peaks['source']} bf16 {'sustained' if sustained else 'burst'}"
-                                    + (" x2 (int8, spec ratio)" if cfg["quant"] else ""))
-    else:
-        roofline.update(achieved=bytes_gemm1 / gemm1_s / 1e9, peak=peaks["hbm"], unit="GB/s",
-                        frac=bytes_gemm1 / gemm1_s / 1e9 / peaks["hbm"], peak_source=f"{peaks['source']} HBM copy")
-    # the same against NVIDIA's dense spec figures (2.25 PFLOP/s bf16, 4.5 POP/s
-    # int8, 7.7 TB/s HBM3e), for context
-    spec = (4500.0 if cfg["quant"] else 2250.0) if tensor_bound else 7700.0
-    roofline.update(spec_peak=spec, frac_of_spec=roofline["achieved"] / spec)
-    flops_step = 6.0 * S_local * H * I
-    value = world * T / (ms / 1e3)
 
-    # yardsticks: cuBLAS (torch.matmul / torch.bmm) on the gate_up launch's
-    # flops, timed the same way right after: one dense GEMM [S, H] x [H, 2I]
-    # (no expert boundaries, one weight matrix), and a batched GEMM with one
-    # weight matrix per expert and S / E rows each (the MoE launch's weight
-    # bytes, no routing imbalance, no padding)
-    def time_cublas(fn):
+def stage_events_pass(ctx, w, cfg, T, steps):
+    """CUDA-event stage times (cross-check of the kernel clocks): a second
+    capture of the same op with the library's stage events as graph nodes,
+    replayed once per step (these nodes break the launch overlap between
+    stages, so the figures are slightly pessimistic)."""
+    import mail_b200 as mb
+
+    torch, lib = ctx.torch, ctx.lib
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(STAGES)]
+    for e in ev:
+        e.record(ctx.stream)
+    torch.cuda.synchronize()
+    arr = (ctypes.c_void_p * STAGES)(*[e.cuda_event for e in ev])
+    w13, w2, scales = w["weights"]
+    lib.moe_set_stage_events(arr, STAGES)
+    try:
+        cap = mb.CapturedMoeMLP(w13, w2, T, cfg["k"], dtype=w["dt"], scales=scales)
+    finally:
+        lib.moe_set_stage_events(None, 0)
+    rows = []
+    for i in range(steps):
+        xv, iv, wv = w["inp"](i)
+        cap(xv, wv, iv)
+        torch.cuda.synchronize()
+        rows.append([ev[j].elapsed_time(ev[j + 1]) for j in range(STAGES - 1)])
+    del cap
+
+    def mean(a, b):
+        return statistics.mean(sum(r[a:b]) for r in rows)
+
+    return {"route": mean(0, 1), "gather": mean(1, 2), "gemm1": mean(2, 3), "pre_gemm2": mean(3, 4),
+            "gemm2": mean(4, 5), "finalize": mean(5, 6),
+            "source": "CUDA events as graph nodes, separate replay after the timed region"}
+
+
+def cublas_yardsticks(ctx, cfg, S, gemm1_ms, steps):
+    """cuBLAS (torch.matmul / torch.bmm) on the gate_up launch's FLOPs, timed
+    the same way: one dense GEMM [S, H] x [H, 2I], and a batched GEMM with
+    one weight matrix per expert and S / E rows each."""
+    torch = ctx.torch
+    H, I, E = cfg["H"], cfg["I"], cfg["E"]
+    dt = torch.bfloat16
+    flops = 2.0 * S * H * 2 * I
+
+    def time_fn(fn):
         for _ in range(3):
             fn()
         c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        reps = max(3, args.steps)
-        c0.record(stream)
+        reps = max(3, steps)
+        c0.record(ctx.stream)
         for _ in range(reps):
             fn()
-        c1.record(stream)
+        c1.record(ctx.stream)
         torch.cuda.synchronize()
         return c0.elapsed_time(c1) / reps
 
-    if world == 1 and not cfg["quant"] and cfg["dtype"] == "bf16":
-        a = torch.randn(S_local, H, device=device, dtype=dt)
-        b = torch.randn(H, 2 * I, device=device, dtype=dt)
-        cub_ms = time_cublas(lambda: torch.matmul(a, b))
-        roofline["cublas_dense_same_shape"] = {"ms": cub_ms, "tflops": flops_gemm1 / (cub_ms / 1e3) / 1e12,
-                                               "ours_vs_cublas": cub_ms / st_ms["gemm1"]}
+    out = {}
+    a = torch.randn(S, H, device=ctx.device, dtype=dt)
+    b = torch.randn(H, 2 * I, device=ctx.device, dtype=dt)
+    ms = time_fn(lambda: torch.matmul(a, b))
+    out["cublas_dense_same_shape"] = {"ms": ms, "tflops": flops / (ms / 1e3) / 1e12, "ours_vs_cublas": ms / gemm1_ms}
+    del a, b
+    rows = S // E
+    if rows >= 128 and E * H * 2 * I * 2 <= 8 << 30:
+        a = torch.randn(E, rows, H, device=ctx.device, dtype=dt)
+        b = torch.randn(E, H, 2 * I, device=ctx.device, dtype=dt)
+        ms = time_fn(lambda: torch.bmm(a, b))
+        bflops = 2.0 * E * rows * H * 2 * I
+        out["cublas_batched_per_expert"] = {"shape": f"{E} x [{rows}, {H}] x [{H}, {2 * I}]", "ms": ms,
+                                            "tflops": bflops / (ms / 1e3) / 1e12,
+                                            "ours_vs_cublas": (flops / gemm1_ms) / (bflops / ms)}
         del a, b
-        rows = S_local // E
-        if rows >= 128 and E * H * 2 * I * 2 <= 8 << 30:
-            a = torch.randn(E, rows, H, device=device, dtype=dt)
-            b = torch.randn(E, H, 2 * I, device=device, dtype=dt)
-            bmm_ms = time_cublas(lambda: torch.bmm(a, b))
-            bmm_flops = 2.0 * E * rows * H * 2 * I
-            roofline["cublas_batched_per_expert"] = {
-                "shape": f"{E} x [{rows}, {H}] x [{H}, {2 * I}]", "ms": bmm_ms,
-                "tflops": bmm_flops / (bmm_ms / 1e3) / 1e12,
-                "ours_vs_cublas": (flops_gemm1 / st_ms["gemm1"]) / (bmm_flops / bmm_ms)}
-            del a, b
+    return out
 
-    line = {"metric": "fused MoE MLP tokens/s", "value": value, "unit": "tokens/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": dtype_name, "data": "synthetic", "config": config_json,
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", default="mixtral", choices=sorted(CONFIGS))
+    ap.add_argument("--tokens", type=int, default=0, help="override tokens per GPU (profiling cases)")
+    ap.add_argument("--ep", default="peer", choices=["peer", "nccl"],
+                    help="expert-parallel exchange (N > 1): fused into the kernels over NVLink peer memory, "
+                         "or NCCL all-to-all")
+    ap.add_argument("--gemm", default="auto", choices=["auto", "pair", "single"],
+                    help="grouped GEMM variant: CTA pairs (cta_group::2), one CTA per tile, or chosen by size")
+    ap.add_argument("--band", type=int, default=0, help="GEMM tile-order band width in M tiles (0: default)")
+    ap.add_argument("--pdl", type=int, default=1, choices=[0, 1],
+                    help="launch the kernels with programmatic dependent launch (1, default)")
+    ap.add_argument("--half-units", type=int, default=1, choices=[0, 1],
+                    help="CTA-pair GEMMs: each expert's odd last M tile as an M=128 pair MMA (1, default)")
+    ap.add_argument("--eager", action="store_true",
+                    help="N=1: call the op directly each step instead of replaying it from a captured CUDA graph")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-configs", action="store_true", help="skip the other workloads (the configs key)")
+    ap.add_argument("--sustain-s", type=float, default=1.5,
+                    help="seconds of back-to-back steps in the sustained pass (0: skip)")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    args.graph = not args.eager
+    cfg = dict(CONFIGS[args.config])
+    if args.tokens:
+        cfg["T"] = args.tokens
+        cfg["desc"] += f" (T={args.tokens})"
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    T, H, I, E, k = cfg["T"], cfg["H"], cfg["I"], cfg["E"], cfg["k"]
+    dtype_name = "int8" if cfg["quant"] else cfg["dtype"]
+    config_json = {"workload": cfg["desc"], "tokens_per_gpu": T, "hidden": H, "inter": I, "experts": E,
+                   "top_k": k, "routing": cfg["routing"], "dtype": cfg["dtype"] + ("+w8a8" if cfg["quant"] else ""),
+                   "parallelism": f"ep{world}" if world > 1 else "single", "gemm": args.gemm,
+                   "half_units": bool(args.half_units), "pdl": bool(args.pdl),
+                   "ep_exchange": args.ep if world > 1 else None, "cuda_graph": bool(args.graph and world == 1)}
+    n_var, l2_note = n_variants(cfg, T, world, rank)
+    config_json["l2"] = l2_note
+
+    if args.impl == "reference":
+        if rank != 0:
+            return 0
+        ref = cpu_reference_run(cfg, args.steps, args.warmup)
+        line = {"metric": "fused MoE MLP tokens/s", "value": ref["value"], "unit": "tokens/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ref["seconds_per_step"] * 1e3,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+                "data": "synthetic", "config": config_json, "impl": "reference",
+                "cpu_baseline": {"value": ref["value"], "unit": "tokens/s", "cores": ref["cores"], "kind": "port",
+                                 "sample": ref["sample"]},
+                "e2e": {"value": ref["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return 0
+
+    import torch
+    import torch.distributed as dist
+
+    from mail_b200 import _lib
+
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+    lib = _lib.load()
+    lib.moe_set_option(_lib.OPT_GEMM_CTA_PAIR, {"pair": 1, "single": 0, "auto": 2}[args.gemm])
+    if args.band:
+        lib.moe_set_option(_lib.OPT_GEMM_BAND, args.band)
+    lib.moe_set_option(_lib.OPT_GEMM_HALF_UNITS, args.half_units)
+    lib.moe_set_option(_lib.OPT_PDL, args.pdl)
+    lib.moe_set_option(_lib.OPT_KERNEL_CLOCKS, 1)  # before any capture: GEMM launches time themselves
+    ctx = Ctx(torch, dist, lib, device, local_rank, world, rank)
+    peaks = load_peaks()
+
+    # ---- the headline workload
+    if world > 1:
+        w = build_ep(ctx, cfg, T, args.ep)
+        args.graph = False
+    else:
+        w = build_single(ctx, cfg, T, n_var, graph=args.graph and not cfg.get("prerouted"))
+    for i in range(args.warmup):
+        w["step"](*w["inp"](i))
+    torch.cuda.synchronize()
+    reg = timed_region(ctx, w["step"], w["inp"], args.steps, kernels_per_step=w["kernels"])
+    ms = reg["ms"]
+    gemm1_ms = reg["kernel_clocks"]["gate_up"]["ms_per_launch"]
+    gemm2_ms = reg["kernel_clocks"]["down"]["ms_per_launch"]
+
+    # ---- sustained: the same step back to back for >= sustain_s seconds
+    sustained = None
+    if args.sustain_s > 0:
+        n_sus = max(args.steps, int(math.ceil(args.sustain_s * 1e3 / ms)))
+        sreg = timed_region(ctx, w["step"], w["inp"], n_sus, kernels_per_step=w["kernels"])
+        sroof = gate_up_roofline(cfg, T, world, [v[1].cpu().numpy() for v in w["variants"]],
+                                 sreg["kernel_clocks"]["gate_up"]["ms_per_launch"], peaks, None, sustained=True)
+        sustained = {"value": world * T / (sreg["ms"] / 1e3), "unit": "tokens/s", "ms_per_step": sreg["ms"],
+                     "steps": n_sus, "seconds": sreg["seconds"], "clocks": sreg["clocks"],
+                     "kernel_clocks": sreg["kernel_clocks"],
+                     "roofline": {k2: sroof[k2] for k2 in ("achieved", "peak", "unit", "frac", "peak_source",
+                                                           "ms_per_launch", "bound")}}
+
+    # ---- CUDA-event stage times (cross-check), e2e through the public API
+    stage = None
+    if world == 1 and args.graph and not cfg.get("prerouted"):
+        try:
+            stage = stage_events_pass(ctx, w, cfg, T, args.steps)
+        except Exception as exc:  # the cross-check is optional
+            stage = {"error": str(exc)[:200]}
+    e2e_ms, h2d, d2h = e2e_pass(ctx, w, args.steps)
+
+    # ---- roofline of the dominant kernel (gate_up GEMM + SwiGLU)
+    int8 = int8_yardstick(ctx) if (world == 1 and (cfg["quant"] or not args.no_configs)) else None
+    id_sets = [v[1].cpu().numpy() for v in w["variants"]]
+    region_s = ms * args.steps / 1e3
+    roofline = gate_up_roofline(cfg, T, world, id_sets, gemm1_ms, peaks, int8, sustained=region_s >= 1.0)
+    roofline["ms_per_launch_source"] = ("library kernel clocks (device %globaltimer, first CTA past its wait on "
+                                        "the previous kernel to last CTA end) over the timed region, %d launches"
+                                        % reg["kernel_clocks"]["gate_up"]["launches"])
+    roofline["down_ms_per_launch"] = gemm2_ms
+    if stage and "gemm1" in stage:
+        roofline["ms_per_launch_events"] = stage["gemm1"]
+    roofline["traffic"] = load_traffic(args.config) if not args.tokens and world == 1 else None
+    roofline["traffic_unit"] = "bytes"
+    if world == 1 and not cfg["quant"] and cfg["dtype"] == "bf16" and not cfg.get("prerouted"):
+        roofline.update(cublas_yardsticks(ctx, cfg, T * k, gemm1_ms, args.steps))
+    flops_step = 6.0 * T * k * H * I
+    peak_tc = roofline["peak"] if roofline["bound"] == "tensor" else peaks["bf16"]
+
+    line = {"metric": "fused MoE MLP tokens/s", "value": world * T / (ms / 1e3), "unit": "tokens/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": dtype_name,
+            "data": "synthetic", "config": config_json,
             "tflops_per_gpu": flops_step / (ms / 1e3) / 1e12,
             "frac_of_tensor_peak": flops_step / (ms / 1e3) / 1e12 / peak_tc,
-            "stage_ms": st_ms, "roofline": roofline,
-            "e2e": {"value": world * T / (e2e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": int(h2d),
-                    "d2h_bytes_per_step": int(d2h), "ms_per_step": e2e_ms,
+            "kernel_clocks": reg["kernel_clocks"], "stage_ms": stage, "roofline": roofline,
+            "sustained": sustained,
+            "e2e": {"value": world * T / (e2e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
                     "copies": "pinned host memory, own H2D / D2H streams, double-buffered"},
-            "gpu_launches": int(launches), "clocks": clocks}
+            "gpu_launches": reg["launches"], "clocks": reg["clocks"]}
+    if int8:
+        line["int8_yardstick"] = int8
+    close_workload(ctx, w)
+
+    # ---- the other workloads
+    if not args.no_configs and args.config == "mixtral" and not args.tokens:
+        line["configs"] = sub_configs(ctx, args, peaks, int8)
 
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         ref = cpu_reference_run(cfg, steps=3, warmup=1, time_limit_s=20.0)
@@ -693,8 +916,6 @@ def main():
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
-        if hasattr(layer, "close"):
-            layer.close()
         dist.barrier(device_ids=[local_rank])
         dist.destroy_process_group()
     return 0

@@ -106,9 +106,12 @@ typedef enum {
   MOE_OPT_GEMM_HALF_UNITS = 4 /* CTA pairs only. 1 (default): an expert's odd last M tile runs as one
                                M=128 pair MMA, 64 of its rows on each CTA; 0: as an M=256 pair MMA
                                whose second CTA's rows are idle */,
-  MOE_OPT_PDL = 5             /* 1 (default): kernels are launched with programmatic dependent launch,
+  MOE_OPT_PDL = 5,            /* 1 (default): kernels are launched with programmatic dependent launch,
                                so each one's launch and prologue overlap the kernel before it in the
                                stream (every kernel first waits for its predecessors' results); 0: off */
+  MOE_OPT_KERNEL_CLOCKS = 6   /* 1: the grouped GEMM kernels time every launch on the device (read with
+                               moe_kernel_clocks); launches are captured with the setting in force when
+                               they are issued, so set it before capturing a CUDA graph. 0 (default): off */
 } moe_option_t;
 MOE_API int moe_set_option(int option, int value);
 /* Current value of an option, or -1 for an unknown option. */
@@ -117,6 +120,17 @@ MOE_API int moe_get_option(int option);
 /* Number of CUDA kernels this library has launched in this process
  * (monotonic, all threads). */
 MOE_API int64_t moe_launch_count(void);
+
+/* Device-side kernel clocks (MOE_OPT_KERNEL_CLOCKS): for each kernel class,
+ * the summed busy time of its launches on the current device — from the
+ * first CTA past its wait on the preceding kernels to the last CTA's end, so
+ * a launch's prologue overlapped with its predecessor is not counted — and
+ * the number of launches. Classes: MOE_CLOCK_GATE_UP (gate_up GEMM +
+ * SwiGLU), MOE_CLOCK_DOWN (down GEMM + its epilogue). Copies the first n
+ * classes into total_ns[] / launches[] (host arrays), clears them if reset
+ * != 0, and synchronises `stream`. */
+typedef enum { MOE_CLOCK_GATE_UP = 0, MOE_CLOCK_DOWN = 1, MOE_NUM_CLOCKS = 2 } moe_clock_t;
+MOE_API int moe_kernel_clocks(uint64_t* total_ns, uint64_t* launches, int n, int reset, void* stream);
 
 /* Stage boundaries at which the all-in-one entry points record profiling
  * events (moe_set_stage_events). */

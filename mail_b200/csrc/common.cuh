@@ -107,6 +107,49 @@ __device__ __forceinline__ void pdl_begin() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+// Kernel clocks (MOE_OPT_KERNEL_CLOCKS): per kernel class, the busy time of
+// every launch measured on the device with the global nanosecond timer —
+// from the moment the first CTA is past its wait on the preceding grids to
+// the moment the last CTA finishes — summed over launches. The first CTA to
+// arrive stamps the start; the last to finish (a completion count over the
+// grid) adds end - start and re-arms the record for the next launch. Two
+// atomics per CTA; launches of one class never overlap (stream order).
+struct KernelClock {
+  unsigned long long start;
+  unsigned long long total_ns;
+  unsigned long long launches;
+  unsigned int started;
+  unsigned int finished;
+};
+
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Call after pdl_begin(), from every CTA.
+__device__ __forceinline__ void clock_begin(KernelClock* c) {
+  if (c != nullptr && threadIdx.x == 0 && atomicAdd(&c->started, 1u) == 0u) atomicExch(&c->start, global_ns());
+}
+
+// Call at the very end, after a __syncthreads(), from every CTA.
+__device__ __forceinline__ void clock_end(KernelClock* c) {
+  if (c == nullptr || threadIdx.x != 0) return;
+  __threadfence();
+  const unsigned int nblocks = gridDim.x * gridDim.y * gridDim.z;
+  if (atomicAdd(&c->finished, 1u) == nblocks - 1u) {
+    __threadfence();
+    const unsigned long long t = global_ns();
+    const unsigned long long s = atomicAdd(&c->start, 0ull);
+    atomicAdd(&c->total_ns, t - s);
+    atomicAdd(&c->launches, 1ull);
+    atomicExch(&c->started, 0u);
+    atomicExch(&c->finished, 0u);
+    __threadfence();
+  }
+}
+
 // Whether launches carry the programmatic-serialisation attribute
 // (MOE_OPT_PDL, default on). Defined in moe_gemm.cu.
 bool pdl_enabled();

@@ -22,8 +22,14 @@ thread_local int g_num_stage_events = 0;
 }  // namespace
 
 int record_stage(int stage, cudaStream_t st) {
-  if (g_stage_events && stage < g_num_stage_events && g_stage_events[stage])
-    MOE_CUDA_TRY(cudaEventRecord(static_cast<cudaEvent_t>(g_stage_events[stage]), st));
+  if (g_stage_events && stage < g_num_stage_events && g_stage_events[stage]) {
+    // under stream capture an event record becomes a graph node only with
+    // cudaEventRecordExternal (a plain record would only order the capture)
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    MOE_CUDA_TRY(cudaStreamIsCapturing(st, &cs));
+    const unsigned flags = cs == cudaStreamCaptureStatusActive ? cudaEventRecordExternal : cudaEventRecordDefault;
+    MOE_CUDA_TRY(cudaEventRecordWithFlags(static_cast<cudaEvent_t>(g_stage_events[stage]), st, flags));
+  }
   return MOE_OK;
 }
 

@@ -34,6 +34,7 @@
 namespace moe {
 
 __device__ int g_moe_device_error = 0;
+__device__ KernelClock g_kernel_clocks[MOE_NUM_CLOCKS];
 
 namespace {
 
@@ -79,6 +80,7 @@ struct Params {
   int num_peers;
   int band_tiles;         // M tiles per band of the expert-major raster
   int stream_k;           // split the (unit, K block) space evenly (additive epilogues only)
+  int clock_slot;         // kernel clock class (MOE_OPT_KERNEL_CLOCKS), -1 = off
 };
 
 // The work of one CTA (or CTA pair): whole units t = gid, gid + n, ... in
@@ -281,6 +283,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     if (SWIGLU && PAIR && p.half_units) ptx::prefetch_tmap(&tmap_b64);
   }
   pdl_begin();  // the tile table and operands come from the grids before this one
+  KernelClock* const clk = p.clock_slot >= 0 ? &g_kernel_clocks[p.clock_slot] : nullptr;
+  clock_begin(clk);
   for (int i = threadIdx.x; i <= E; i += blockDim.x) s_cum[i] = p.table[TileTable::cum_off() + i];
   if constexpr (PAIR) {
     __syncthreads();
@@ -654,6 +658,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   }
 
   __syncthreads();
+  clock_end(clk);
   if constexpr (PAIR) ptx::cluster_sync();  // no CTA leaves while its peer may still signal it
   if (warp == 1) {
     __syncwarp();
@@ -757,6 +762,8 @@ std::atomic<int> g_gemm_stream_k{0};
 std::atomic<int> g_gemm_half_units{1};
 // Programmatic dependent launch for every kernel of the library.
 std::atomic<int> g_pdl{1};
+// Device-side timing of the GEMM launches (MOE_OPT_KERNEL_CLOCKS).
+std::atomic<int> g_kernel_clocks_on{0};
 
 bool use_pair(int64_t max_tiles, int E, int64_t n_tiles) {
   const int v = g_gemm_cta_pair.load();
@@ -898,6 +905,7 @@ extern "C" int moe_gemm1_swiglu(const void* a, int dtype, int64_t a_rows, int64_
   p.a_scale = a_scale;
   p.b_scale = w13_scale;
   p.top_k = 1;
+  p.clock_slot = g_kernel_clocks_on.load() ? MOE_CLOCK_GATE_UP : -1;
   return pair ? launch<true, true>(dtype, ta, tb, ta64, tb64, p, as_stream(stream))
               : launch<true, false>(dtype, ta, tb, ta64, tb64, p, as_stream(stream));
 }
@@ -963,6 +971,7 @@ int gemm2_impl(const void* h, int dtype, int64_t h_rows, int64_t inter, const vo
   // the weighted combine adds partial sums, so its work can be split along K
   // evenly over the grid (no partly idle last wave)
   p.stream_k = epilogue == MOE_EPI_COMBINE_ADD && g_gemm_stream_k.load() != 0;
+  p.clock_slot = g_kernel_clocks_on.load() ? MOE_CLOCK_DOWN : -1;
   return pair ? launch<false, true>(dtype, ta, tb, ta64, tb, p, stream)
               : launch<false, false>(dtype, ta, tb, ta64, tb, p, stream);
 }
@@ -1015,6 +1024,10 @@ extern "C" int moe_set_option(int option, int value) {
     g_pdl.store(value != 0);
     return MOE_OK;
   }
+  if (option == MOE_OPT_KERNEL_CLOCKS) {
+    g_kernel_clocks_on.store(value != 0);
+    return MOE_OK;
+  }
   return set_error(MOE_ERR_INVALID_ARG, "moe_set_option: unknown option %d", option);
 }
 
@@ -1024,7 +1037,26 @@ extern "C" int moe_get_option(int option) {
   if (option == MOE_OPT_GEMM_STREAM_K) return g_gemm_stream_k.load();
   if (option == MOE_OPT_GEMM_HALF_UNITS) return g_gemm_half_units.load();
   if (option == MOE_OPT_PDL) return g_pdl.load();
+  if (option == MOE_OPT_KERNEL_CLOCKS) return g_kernel_clocks_on.load();
   return -1;
+}
+
+extern "C" int moe_kernel_clocks(uint64_t* total_ns, uint64_t* launches, int n, int reset, void* stream) {
+  MOE_CHECK_ARG(n >= 0 && n <= MOE_NUM_CLOCKS, "moe_kernel_clocks: n must be in [0, %d]", MOE_NUM_CLOCKS);
+  MOE_CHECK_ARG(n == 0 || (total_ns && launches), "moe_kernel_clocks: NULL output");
+  cudaStream_t st = as_stream(stream);
+  KernelClock host[MOE_NUM_CLOCKS];
+  MOE_CUDA_TRY(cudaMemcpyFromSymbolAsync(host, g_kernel_clocks, sizeof(host), 0, cudaMemcpyDeviceToHost, st));
+  if (reset) {
+    static const KernelClock zero[MOE_NUM_CLOCKS] = {};
+    MOE_CUDA_TRY(cudaMemcpyToSymbolAsync(g_kernel_clocks, zero, sizeof(zero), 0, cudaMemcpyHostToDevice, st));
+  }
+  MOE_CUDA_TRY(cudaStreamSynchronize(st));
+  for (int i = 0; i < n; ++i) {
+    total_ns[i] = host[i].total_ns;
+    launches[i] = host[i].launches;
+  }
+  return MOE_OK;
 }
 
 extern "C" int moe_selftest_wait_timeout(uint64_t timeout_ns, void* stream) {

@@ -345,16 +345,22 @@ def test_mixtral_full_size_sampled_and_properties():
     ids_t, wts_t = torch.from_numpy(ids).to(dev()), torch.from_numpy(wts).to(dev())
     y = mb.fused_moe_mlp(x, w13.transpose(1, 2), w2.transpose(1, 2), wts_t, ids_t)
     torch.cuda.synchronize()
+    # 512 sampled tokens (every expert among them), against a torch fp32
+    # reference of the same op computed expert by expert
     rng = np.random.default_rng(1)
-    sample = rng.choice(T, size=24, replace=False)
+    sample = np.sort(rng.choice(T, size=512, replace=False))
+    assert len(np.unique(ids[sample])) == E
     ref = torch.zeros(len(sample), H, device=dev())
-    for i, t in enumerate(sample):
-        for j in range(k):
-            e = int(ids[t, j])
-            gu = x[t].float() @ w13[e].float().t()
-            h = torch.nn.functional.silu(gu[:I]) * gu[I:]
-            h = h.to(torch.bfloat16).float()
-            ref[i] += float(wts[t, j]) * (h @ w2[e].float().t())
+    xs = x[torch.from_numpy(sample).to(dev())].float()
+    for e in range(E):
+        rows, js = np.nonzero(ids[sample] == e)
+        if rows.size == 0:
+            continue
+        gu = xs[torch.from_numpy(rows).to(dev())] @ w13[e].float().t()
+        h = (torch.nn.functional.silu(gu[:, :I]) * gu[:, I:]).to(torch.bfloat16).float()
+        o = h @ w2[e].float().t()
+        wv = torch.from_numpy(wts[sample][rows, js]).to(dev())[:, None]
+        ref.index_add_(0, torch.from_numpy(rows).to(dev()), wv * o)
     err = max_abs_rel(npf(y[torch.from_numpy(sample).to(dev())]), npf(ref))
     assert err < TOL, err
     # linearity in the routing weights
@@ -528,4 +534,35 @@ def test_stream_k_combine_matches_whole_tiles(pair):
     assert max_abs_rel(npf(y_sk), npf(y_tiles)) <= 2.0 ** -7
     ref = O.moe_mlp_topk(npf(x), npf(w13), npf(w2), wts, ids, round_hidden=O.round_bf16)
     assert max_abs_rel(npf(y_sk), ref) < TOL
+    assert_no_device_error()
+
+
+def test_kernel_clocks_time_each_gemm_launch():
+    """MOE_OPT_KERNEL_CLOCKS: every gate_up and down launch is timed on the
+    device; the summed busy time fits inside the CUDA-event time of the calls
+    and each class counts exactly its launches."""
+    import ctypes
+    lib = _lib.load()
+    x, w13, w2, ids, wts = topk_case(512, 1024, 1024, 8, 2, "uniform-softmax", torch.bfloat16, seed=21)
+    tot = (ctypes.c_uint64 * _lib.NUM_CLOCKS)()
+    cnt = (ctypes.c_uint64 * _lib.NUM_CLOCKS)()
+    st = torch.cuda.current_stream().cuda_stream
+    lib.moe_set_option(_lib.OPT_KERNEL_CLOCKS, 1)
+    try:
+        run_topk(x, w13, w2, ids, wts)
+        _lib.call("moe_kernel_clocks", tot, cnt, _lib.NUM_CLOCKS, 1, st)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(3):
+            run_topk(x, w13, w2, ids, wts)
+        e1.record()
+        torch.cuda.synchronize()
+        _lib.call("moe_kernel_clocks", tot, cnt, _lib.NUM_CLOCKS, 1, st)
+    finally:
+        lib.moe_set_option(_lib.OPT_KERNEL_CLOCKS, 0)
+    assert list(cnt) == [3, 3]
+    assert all(t > 0 for t in tot)
+    assert (tot[0] + tot[1]) / 1e6 <= e0.elapsed_time(e1) * 1.02
+    _lib.call("moe_kernel_clocks", tot, cnt, _lib.NUM_CLOCKS, 0, st)
+    assert list(cnt) == [0, 0]  # the read above cleared them; clocks off since
     assert_no_device_error()
