@@ -876,9 +876,9 @@ def main():
     id_sets = [v[1].cpu().numpy() for v in w["variants"]]
     region_s = ms * args.steps / 1e3
     roofline = gate_up_roofline(cfg, T, world, id_sets, gemm1_ms, peaks, int8, sustained=region_s >= 1.0)
-    roofline["ms_per_launch_source"] = ("library kernel clocks (device %globaltimer, first CTA past its wait on "
-                                        "the previous kernel to last CTA end) over the timed region, %d launches"
-                                        % reg["kernel_clocks"]["gate_up"]["launches"])
+    roofline["ms_per_launch_source"] = ("library kernel clocks (device global timer, first CTA past its wait on "
+                                        "the previous kernel to last CTA end) over the timed region, "
+                                        f"{reg['kernel_clocks']['gate_up']['launches']} launches")
     roofline["down_ms_per_launch"] = gemm2_ms
     if stage and "gemm1" in stage:
         roofline["ms_per_launch_events"] = stage["gemm1"]

@@ -72,7 +72,7 @@ def test_align_static_matches_align_on_two_calls_in_a_row():
 
 @pytest.mark.parametrize("T,k,E", [
     (16288, 8, 256),   # scratch 1,047,808 B: the last tail region ends just below the 1 MiB array
-    (2000, 8, 4096),   # more than 1024 experts: the multi-kernel path even for a small batch
+    (990, 8, 4096),    # more than 1024 experts: the multi-kernel path, scratch just under 1 MiB
     (60, 8, 4096),     # the same with fewer slots than experts
     (2048, 8, 128),    # 16384 slots: the one-CTA align, no scratch
 ])
