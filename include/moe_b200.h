@@ -109,9 +109,16 @@ typedef enum {
   MOE_OPT_PDL = 5,            /* 1 (default): kernels are launched with programmatic dependent launch,
                                so each one's launch and prologue overlap the kernel before it in the
                                stream (every kernel first waits for its predecessors' results); 0: off */
-  MOE_OPT_KERNEL_CLOCKS = 6   /* 1: the grouped GEMM kernels time every launch on the device (read with
+  MOE_OPT_KERNEL_CLOCKS = 6,  /* 1: the grouped GEMM kernels time every launch on the device (read with
                                moe_kernel_clocks); launches are captured with the setting in force when
                                they are issued, so set it before capturing a CUDA graph. 0 (default): off */
+  MOE_OPT_GEMM_SWAP_AB = 7    /* operand roles of the grouped GEMMs. 2 (default): the all-in-one entry points
+                               swap them when the routed rows average at most 64 per expert that receives
+                               any (decode): the 128 weight rows of an output-feature tile are the MMA's M
+                               operand and the expert's token rows (rounded up to 16) its N operand, with
+                               the K dimension split over more CTAs when a launch has few work items; the
+                               stand-alone GEMM entry points keep rows as M. 1: always swap (stand-alone
+                               GEMMs included, without K splits). 0: never */
 } moe_option_t;
 MOE_API int moe_set_option(int option, int value);
 /* Current value of an option, or -1 for an unknown option. */

@@ -89,6 +89,35 @@ inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s
 // to peer_out[meta >> 24] at row meta & 0xFFFFFF, meta = row_map[r] (< 0: skip).
 constexpr int kEpiScatterPeer = 3;
 
+// Operand roles and K splits of one MoE layer's two grouped GEMMs
+// (moe_gemm.cu). swap: few token rows per expert, so the weights are the
+// MMA's 128-row operand and the tokens its N operand (moe_gemm_swap.cuh).
+struct GemmPlan {
+  bool swap = false;
+  int nmax = 128;            // token rows per swapped work item (32 or 128)
+  int splits1 = 1;           // K splits of the gate_up GEMM (swapped)
+  int splits2 = 1;           // K splits of the down GEMM (swapped, combine epilogue only)
+  size_t partial_bytes = 0;  // gate_up split-K slots
+  size_t counter_bytes = 0;  // gate_up split-K counts (zeroed before the launch)
+};
+
+// Plan for `slots` routed rows over `num_experts` experts (max_tiles M tiles of
+// 128 rows); combine: the down GEMM uses the additive combine epilogue.
+GemmPlan gemm_plan(int64_t slots, int num_experts, int64_t max_tiles, int64_t hidden, int64_t inter, int dtype,
+                   bool combine);
+
+// moe_gemm1_swiglu / moe_gemm2 with an explicit plan (nullptr: the row-major
+// kernels, or the swapped one when MOE_OPT_GEMM_SWAP_AB forces it) and, for a
+// gate_up split, its workspace (partial slots and zeroed counters).
+int gemm1_swiglu_planned(const void* a, int dtype, int64_t a_rows, int64_t hidden, const void* w13, int num_experts,
+                         int64_t inter, const float* a_scale, const float* w13_scale, const int32_t* tile_table,
+                         int64_t max_tiles, void* h, int h_dtype, const GemmPlan* plan, void* partial,
+                         int32_t* counters, cudaStream_t stream);
+int gemm2_planned(const void* h, int dtype, int64_t h_rows, int64_t inter, const void* w2, int num_experts,
+                  int64_t hidden, const float* h_scale, const float* w2_scale, const int32_t* tile_table,
+                  int64_t max_tiles, int epilogue, const int32_t* row_map, const float* row_weight, int top_k,
+                  void* out, int out_dtype, int64_t out_rows, const GemmPlan* plan, cudaStream_t stream);
+
 // Down GEMM whose epilogue stores each output row into the buffer of the rank
 // that sent the row (peer pointers, NVLink stores). Defined in moe_gemm.cu.
 int gemm2_scatter_peer(const void* h, int dtype, int64_t h_rows, int64_t inter, const void* w2, int num_experts,

@@ -91,7 +91,8 @@ ExpertsOut combine_mode(int64_t T, int64_t H) {
 struct FusedExpertsWs {
   int64_t S, cap, max_tiles;
   size_t align_bytes;
-  size_t align, sorted, slot_pos, gs, poff, table, xp, xs, h, hq, hs, y32, o, bytes;
+  GemmPlan plan;
+  size_t align, sorted, slot_pos, gs, poff, table, xp, xs, h, hq, hs, y32, o, partial, counters, bytes;
 };
 FusedExpertsWs fused_experts_ws(int64_t T, int64_t H, int64_t I, int E, int k, int x_dtype, int w_dtype,
                                 ExpertsOut mode) {
@@ -117,6 +118,9 @@ FusedExpertsWs fused_experts_ws(int64_t T, int64_t H, int64_t I, int E, int k, i
   const bool atomic_acc = mode == ExpertsOut::kCombineAtomic && x_dtype != MOE_F32;
   w.y32 = c.take(atomic_acc ? (size_t)T * H * sizeof(float) : 0);
   w.o = c.take(mode == ExpertsOut::kCombineRows ? (size_t)w.cap * H * dtype_size(x_dtype) : 0);
+  w.plan = gemm_plan(w.S, E, w.max_tiles, H, I, q ? MOE_I8 : x_dtype, mode == ExpertsOut::kCombineAtomic);
+  w.partial = c.take(w.plan.partial_bytes);
+  w.counters = c.take(w.plan.counter_bytes);
   w.bytes = c.off;
   return w;
 }
@@ -186,8 +190,13 @@ int run_experts(const ExpertsArgs& a) {
                       stream));
   MOE_TRY(record_stage(MOE_STAGE_GATHERED, st));
   void* h = ws + w.h;
-  MOE_TRY(moe_gemm1_swiglu(xp, q ? MOE_I8 : a.x_dtype, w.cap, a.H, a.w13, a.E, a.I, xs, a.w13_scale, table,
-                           w.max_tiles, h, h_dtype, stream));
+  int32_t* counters = nullptr;
+  if (w.plan.counter_bytes) {  // split-K counts of the gate_up GEMM start at zero
+    counters = reinterpret_cast<int32_t*>(ws + w.counters);
+    MOE_TRY(zero_fill(counters, w.plan.counter_bytes, st));
+  }
+  MOE_TRY(gemm1_swiglu_planned(xp, q ? MOE_I8 : a.x_dtype, w.cap, a.H, a.w13, a.E, a.I, xs, a.w13_scale, table,
+                               w.max_tiles, h, h_dtype, &w.plan, ws + w.partial, counters, st));
   MOE_TRY(record_stage(MOE_STAGE_GEMM1, st));
   const void* a2 = h;
   float* hs = nullptr;
@@ -202,21 +211,21 @@ int run_experts(const ExpertsArgs& a) {
     float* acc = (a.x_dtype == MOE_F32) ? static_cast<float*>(a.y) : reinterpret_cast<float*>(ws + w.y32);
     MOE_TRY(zero_fill(acc, (size_t)a.T * a.H * sizeof(float), st));
     MOE_TRY(record_stage(MOE_STAGE_PRE_GEMM2, st));
-    MOE_TRY(moe_gemm2(a2, g2_dtype, w.cap, a.I, a.w2, a.E, a.H, hs, a.w2_scale, table, w.max_tiles,
-                      MOE_EPI_COMBINE_ADD, sorted, a.topk_weights, a.k, acc, MOE_F32, a.T, stream));
+    MOE_TRY(gemm2_planned(a2, g2_dtype, w.cap, a.I, a.w2, a.E, a.H, hs, a.w2_scale, table, w.max_tiles,
+                          MOE_EPI_COMBINE_ADD, sorted, a.topk_weights, a.k, acc, MOE_F32, a.T, &w.plan, st));
     MOE_TRY(record_stage(MOE_STAGE_GEMM2, st));
     if (a.x_dtype != MOE_F32) MOE_TRY(moe_convert_f32(acc, a.T * a.H, a.y, a.x_dtype, stream));
   } else if (a.mode == ExpertsOut::kCombineRows) {
     void* o = ws + w.o;
     MOE_TRY(record_stage(MOE_STAGE_PRE_GEMM2, st));
-    MOE_TRY(moe_gemm2(a2, g2_dtype, w.cap, a.I, a.w2, a.E, a.H, hs, a.w2_scale, table, w.max_tiles,
-                      MOE_EPI_STORE_ROWS, nullptr, nullptr, 1, o, a.x_dtype, w.cap, stream));
+    MOE_TRY(gemm2_planned(a2, g2_dtype, w.cap, a.I, a.w2, a.E, a.H, hs, a.w2_scale, table, w.max_tiles,
+                          MOE_EPI_STORE_ROWS, nullptr, nullptr, 1, o, a.x_dtype, w.cap, &w.plan, st));
     MOE_TRY(record_stage(MOE_STAGE_GEMM2, st));
     MOE_TRY(moe_combine_rows(o, a.x_dtype, a.H, slot_pos, a.topk_weights, a.T, a.k, a.y, a.x_dtype, stream));
   } else {
     MOE_TRY(record_stage(MOE_STAGE_PRE_GEMM2, st));
-    MOE_TRY(moe_gemm2(a2, g2_dtype, w.cap, a.I, a.w2, a.E, a.H, hs, a.w2_scale, table, w.max_tiles,
-                      MOE_EPI_SCATTER_ROWS, sorted, nullptr, 1, a.y, a.x_dtype, a.T, stream));
+    MOE_TRY(gemm2_planned(a2, g2_dtype, w.cap, a.I, a.w2, a.E, a.H, hs, a.w2_scale, table, w.max_tiles,
+                          MOE_EPI_SCATTER_ROWS, sorted, nullptr, 1, a.y, a.x_dtype, a.T, &w.plan, st));
     MOE_TRY(record_stage(MOE_STAGE_GEMM2, st));
   }
   MOE_TRY(record_stage(MOE_STAGE_DONE, st));

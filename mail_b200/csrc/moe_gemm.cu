@@ -764,6 +764,11 @@ std::atomic<int> g_gemm_half_units{1};
 std::atomic<int> g_pdl{1};
 // Device-side timing of the GEMM launches (MOE_OPT_KERNEL_CLOCKS).
 std::atomic<int> g_kernel_clocks_on{0};
+// Swapped operand roles for few rows per expert (MOE_OPT_GEMM_SWAP_AB).
+std::atomic<int> g_gemm_swap{2};
+// Auto rule: swap when the routed rows average at most this many per expert
+// that receives any.
+constexpr int64_t kSwapRowsPerExpert = 64;
 
 bool use_pair(int64_t max_tiles, int E, int64_t n_tiles) {
   const int v = g_gemm_cta_pair.load();
@@ -845,6 +850,8 @@ int check_gemm_common(const char* fn, int dtype, int64_t k, int E, const int32_t
 }  // namespace
 }  // namespace moe
 
+#include "moe_gemm_swap.cuh"
+
 using namespace moe;
 
 extern "C" int moe_get_device_error(int* host_code, void* stream) {
@@ -857,9 +864,49 @@ extern "C" int moe_get_device_error(int* host_code, void* stream) {
   return MOE_OK;
 }
 
-extern "C" int moe_gemm1_swiglu(const void* a, int dtype, int64_t a_rows, int64_t hidden, const void* w13,
-                                int num_experts, int64_t inter, const float* a_scale, const float* w13_scale,
-                                const int32_t* tile_table, int64_t max_tiles, void* h, int h_dtype, void* stream) {
+namespace moe {
+
+GemmPlan gemm_plan(int64_t slots, int num_experts, int64_t max_tiles, int64_t hidden, int64_t inter, int dtype,
+                   bool combine) {
+  GemmPlan p;
+  const int opt = g_gemm_swap.load();
+  const int64_t nonempty = std::min<int64_t>(num_experts, slots);
+  p.swap = opt == 1 || (opt == 2 && slots > 0 && slots <= kSwapRowsPerExpert * nonempty);
+  if (!p.swap) return p;
+  p.nmax = (slots > 0 && slots <= 32) ? 32 : 128;
+  const int64_t sms = num_sms();
+  const int es = dtype_size(dtype);
+  const int64_t nf1 = ceil_div(inter, SW_FEAT), nf2 = ceil_div(hidden, SW_FEAT);
+  const int64_t kb1 = ceil_div(hidden * es, ROW_BYTES), kb2 = ceil_div(inter * es, ROW_BYTES);
+  // fewer work items than half the SMs: split K so about one wave of items
+  // runs, each split keeping at least 4 K blocks
+  auto split = [&](int64_t units, int64_t kb) -> int {
+    if (units <= 0 || 2 * units > sms) return 1;
+    return (int)std::max<int64_t>(1, std::min<int64_t>(sms / units, kb / 4));
+  };
+  p.splits1 = split(max_tiles * nf1, kb1);
+  p.splits2 = combine ? split(max_tiles * nf2, kb2) : 1;
+  if (p.splits1 > 1) {
+    p.partial_bytes = (size_t)max_tiles * nf1 * p.splits1 * 2 * SW_FEAT * p.nmax * 4;
+    p.counter_bytes = (size_t)max_tiles * nf1 * 4 * sizeof(int32_t);
+  }
+  return p;
+}
+
+namespace {
+// The swapped-operand plan a stand-alone GEMM call runs with: forced by
+// MOE_OPT_GEMM_SWAP_AB = 1 only, 128 token rows per item, no K split.
+const GemmPlan* standalone_plan(GemmPlan* storage) {
+  if (g_gemm_swap.load() != 1) return nullptr;
+  storage->swap = true;
+  return storage;
+}
+}  // namespace
+
+int gemm1_swiglu_planned(const void* a, int dtype, int64_t a_rows, int64_t hidden, const void* w13, int num_experts,
+                         int64_t inter, const float* a_scale, const float* w13_scale, const int32_t* tile_table,
+                         int64_t max_tiles, void* h, int h_dtype, const GemmPlan* plan, void* partial,
+                         int32_t* counters, cudaStream_t stream) {
   MOE_TRY(check_gemm_common("moe_gemm1_swiglu", dtype, hidden, num_experts, tile_table, max_tiles));
   MOE_CHECK_ARG(a && w13 && h, "moe_gemm1_swiglu: NULL pointer");
   MOE_CHECK_ARG(inter > 0 && inter % 8 == 0, "moe_gemm1_swiglu: inter (%lld) must be a positive multiple of 8",
@@ -871,6 +918,39 @@ extern "C" int moe_gemm1_swiglu(const void* a, int dtype, int64_t a_rows, int64_
   MOE_CHECK_ARG((uintptr_t)a % 16 == 0 && (uintptr_t)w13 % 16 == 0 && (uintptr_t)h % 16 == 0,
                 "moe_gemm1_swiglu: pointers must be 16-byte aligned");
   if (a_rows == 0 || max_tiles == 0) return MOE_OK;
+  if (plan && plan->swap) {
+    const int splits = plan->splits1;
+    if (splits > 1) MOE_CHECK_ARG(partial && counters, "moe_gemm1_swiglu: a K split needs its workspace");
+    CUtensorMap tw, tx;
+    MOE_TRY(make_tmap(&tw, w13, dtype, hidden, (uint64_t)num_experts * 2 * inter, SW_FEAT));
+    MOE_TRY(make_tmap(&tx, a, dtype, hidden, a_rows, SW_BOX));
+    SwapParams p{};
+    p.E = num_experts;
+    p.num_kb = (int)ceil_div(hidden * dtype_size(dtype), ROW_BYTES);
+    p.splits = splits;
+    p.nf = (int)ceil_div(inter, SW_FEAT);
+    p.n_valid = (int)inter;
+    p.w_rows_per_expert = (int)(2 * inter);
+    p.inter = (int)inter;
+    p.nmax = plan->nmax;
+    p.stages = swap_stages(true, p.nmax, num_experts);
+    p.idesc_m = make_idesc(dtype, SW_FEAT) & ~(0x3Fu << 17);
+    p.table = tile_table;
+    p.max_tiles = (int)max_tiles;
+    p.a_rows = a_rows;
+    p.epi = MOE_EPI_STORE_ROWS;
+    p.out = h;
+    p.out_dtype = h_dtype;
+    p.ldo = inter;
+    p.out_rows = a_rows;
+    p.a_scale = a_scale;
+    p.w_scale = w13_scale;
+    p.top_k = 1;
+    p.partial = partial;
+    p.counters = counters;
+    p.clock_slot = g_kernel_clocks_on.load() ? MOE_CLOCK_GATE_UP : -1;
+    return launch_swap<true>(dtype, tw, tx, p, stream);
+  }
   CUtensorMap ta, tb, ta64, tb64;
   const bool pair = use_pair(max_tiles, num_experts, ceil_div(inter, BN / 2));
   const bool half_units = pair && g_gemm_half_units.load() != 0;
@@ -906,8 +986,17 @@ extern "C" int moe_gemm1_swiglu(const void* a, int dtype, int64_t a_rows, int64_
   p.b_scale = w13_scale;
   p.top_k = 1;
   p.clock_slot = g_kernel_clocks_on.load() ? MOE_CLOCK_GATE_UP : -1;
-  return pair ? launch<true, true>(dtype, ta, tb, ta64, tb64, p, as_stream(stream))
-              : launch<true, false>(dtype, ta, tb, ta64, tb64, p, as_stream(stream));
+  return pair ? launch<true, true>(dtype, ta, tb, ta64, tb64, p, stream)
+              : launch<true, false>(dtype, ta, tb, ta64, tb64, p, stream);
+}
+}  // namespace moe
+
+extern "C" int moe_gemm1_swiglu(const void* a, int dtype, int64_t a_rows, int64_t hidden, const void* w13,
+                                int num_experts, int64_t inter, const float* a_scale, const float* w13_scale,
+                                const int32_t* tile_table, int64_t max_tiles, void* h, int h_dtype, void* stream) {
+  GemmPlan storage;
+  return gemm1_swiglu_planned(a, dtype, a_rows, hidden, w13, num_experts, inter, a_scale, w13_scale, tile_table,
+                              max_tiles, h, h_dtype, standalone_plan(&storage), nullptr, nullptr, as_stream(stream));
 }
 
 namespace moe {
@@ -916,7 +1005,7 @@ int gemm2_impl(const void* h, int dtype, int64_t h_rows, int64_t inter, const vo
                int64_t hidden, const float* h_scale, const float* w2_scale, const int32_t* tile_table,
                int64_t max_tiles, int epilogue, const int32_t* row_map, const float* row_weight, int top_k,
                void* out, int out_dtype, int64_t out_rows, void* const* peer_out, int num_peers,
-               cudaStream_t stream) {
+               const GemmPlan* plan, cudaStream_t stream) {
   MOE_TRY(check_gemm_common("moe_gemm2", dtype, inter, num_experts, tile_table, max_tiles));
   MOE_CHECK_ARG(h && w2 && (out || peer_out), "moe_gemm2: NULL pointer");
   MOE_CHECK_ARG(hidden > 0 && hidden % 8 == 0, "moe_gemm2: hidden (%lld) must be a positive multiple of 8",
@@ -935,6 +1024,37 @@ int gemm2_impl(const void* h, int dtype, int64_t h_rows, int64_t inter, const vo
   MOE_CHECK_ARG((uintptr_t)h % 16 == 0 && (uintptr_t)w2 % 16 == 0 && (uintptr_t)out % 16 == 0,
                 "moe_gemm2: pointers must be 16-byte aligned");
   if (h_rows == 0 || max_tiles == 0) return MOE_OK;
+  if (plan && plan->swap && epilogue != kEpiScatterPeer) {
+    CUtensorMap tw, tx;
+    MOE_TRY(make_tmap(&tw, w2, dtype, inter, (uint64_t)num_experts * hidden, SW_FEAT));
+    MOE_TRY(make_tmap(&tx, h, dtype, inter, h_rows, SW_BOX));
+    SwapParams p{};
+    p.E = num_experts;
+    p.num_kb = (int)ceil_div(inter * dtype_size(dtype), ROW_BYTES);
+    p.splits = epilogue == MOE_EPI_COMBINE_ADD ? plan->splits2 : 1;  // partial sums add only in the combine
+    p.nf = (int)ceil_div(hidden, SW_FEAT);
+    p.n_valid = (int)hidden;
+    p.w_rows_per_expert = (int)hidden;
+    p.inter = (int)inter;
+    p.nmax = plan->nmax;
+    p.stages = swap_stages(false, p.nmax, num_experts);
+    p.idesc_m = make_idesc(dtype, SW_FEAT) & ~(0x3Fu << 17);
+    p.table = tile_table;
+    p.max_tiles = (int)max_tiles;
+    p.a_rows = h_rows;
+    p.epi = epilogue;
+    p.out = out;
+    p.out_dtype = out_dtype;
+    p.ldo = hidden;
+    p.out_rows = out_rows;
+    p.a_scale = h_scale;
+    p.w_scale = w2_scale;
+    p.row_map = row_map;
+    p.row_weight = row_weight;
+    p.top_k = top_k > 0 ? top_k : 1;
+    p.clock_slot = g_kernel_clocks_on.load() ? MOE_CLOCK_DOWN : -1;
+    return launch_swap<false>(dtype, tw, tx, p, stream);
+  }
   CUtensorMap ta, tb, ta64;
   const bool pair = use_pair(max_tiles, num_experts, ceil_div(hidden, BN));
   const bool half_units = pair && g_gemm_half_units.load() != 0;  // read once: the maps must match
@@ -986,7 +1106,16 @@ int gemm2_scatter_peer(const void* h, int dtype, int64_t h_rows, int64_t inter, 
   MOE_CHECK_ARG(peer_out && num_peers > 0 && num_peers <= 256, "ep: bad peer output table");
   return gemm2_impl(h, dtype, h_rows, inter, w2, num_experts, hidden, h_scale, w2_scale, tile_table, max_tiles,
                     kEpiScatterPeer, row_meta, nullptr, 1, nullptr, out_dtype, peer_rows, peer_out, num_peers,
-                    stream);
+                    nullptr, stream);
+}
+
+int gemm2_planned(const void* h, int dtype, int64_t h_rows, int64_t inter, const void* w2, int num_experts,
+                  int64_t hidden, const float* h_scale, const float* w2_scale, const int32_t* tile_table,
+                  int64_t max_tiles, int epilogue, const int32_t* row_map, const float* row_weight, int top_k,
+                  void* out, int out_dtype, int64_t out_rows, const GemmPlan* plan, cudaStream_t stream) {
+  MOE_CHECK_ARG(out != nullptr, "moe_gemm2: NULL pointer");
+  return gemm2_impl(h, dtype, h_rows, inter, w2, num_experts, hidden, h_scale, w2_scale, tile_table, max_tiles,
+                    epilogue, row_map, row_weight, top_k, out, out_dtype, out_rows, nullptr, 0, plan, stream);
 }
 }  // namespace moe
 
@@ -997,8 +1126,10 @@ extern "C" int moe_gemm2(const void* h, int dtype, int64_t h_rows, int64_t inter
   MOE_CHECK_ARG(epilogue == MOE_EPI_STORE_ROWS || epilogue == MOE_EPI_COMBINE_ADD || epilogue == MOE_EPI_SCATTER_ROWS,
                 "moe_gemm2: bad epilogue %d", epilogue);
   MOE_CHECK_ARG(out != nullptr, "moe_gemm2: NULL pointer");
+  GemmPlan storage;
   return gemm2_impl(h, dtype, h_rows, inter, w2, num_experts, hidden, h_scale, w2_scale, tile_table, max_tiles,
-                    epilogue, row_map, row_weight, top_k, out, out_dtype, out_rows, nullptr, 0, as_stream(stream));
+                    epilogue, row_map, row_weight, top_k, out, out_dtype, out_rows, nullptr, 0,
+                    standalone_plan(&storage), as_stream(stream));
 }
 
 extern "C" int moe_set_option(int option, int value) {
@@ -1028,6 +1159,11 @@ extern "C" int moe_set_option(int option, int value) {
     g_kernel_clocks_on.store(value != 0);
     return MOE_OK;
   }
+  if (option == MOE_OPT_GEMM_SWAP_AB) {
+    MOE_CHECK_ARG(value >= 0 && value <= 2, "moe_set_option: GEMM_SWAP_AB takes 0, 1 or 2");
+    g_gemm_swap.store(value);
+    return MOE_OK;
+  }
   return set_error(MOE_ERR_INVALID_ARG, "moe_set_option: unknown option %d", option);
 }
 
@@ -1038,6 +1174,7 @@ extern "C" int moe_get_option(int option) {
   if (option == MOE_OPT_GEMM_HALF_UNITS) return g_gemm_half_units.load();
   if (option == MOE_OPT_PDL) return g_pdl.load();
   if (option == MOE_OPT_KERNEL_CLOCKS) return g_kernel_clocks_on.load();
+  if (option == MOE_OPT_GEMM_SWAP_AB) return g_gemm_swap.load();
   return -1;
 }
 

@@ -38,15 +38,19 @@ def max_abs_rel(y, ref):
     return float(np.abs(y - ref).max() / max(np.abs(ref).max(), 1e-30))
 
 
-@pytest.fixture(params=[(1, 1), (1, 0), (0, 1)], ids=["cta_pair", "cta_pair_no_half_units", "single_cta"])
+@pytest.fixture(params=[(1, 1, 0), (1, 0, 0), (0, 1, 0), (2, 1, 1)],
+                ids=["cta_pair", "cta_pair_no_half_units", "single_cta", "swapped_operands"])
 def gemm_variant(request):
+    """CTA pairs (with and without M=128 half units), one CTA per tile, and
+    the swapped-operand kernel (forced on the stand-alone GEMM calls)."""
     lib = _lib.load()
-    old = lib.moe_get_option(_lib.OPT_GEMM_CTA_PAIR), lib.moe_get_option(_lib.OPT_GEMM_HALF_UNITS)
-    lib.moe_set_option(_lib.OPT_GEMM_CTA_PAIR, request.param[0])
-    lib.moe_set_option(_lib.OPT_GEMM_HALF_UNITS, request.param[1])
+    opts = (_lib.OPT_GEMM_CTA_PAIR, _lib.OPT_GEMM_HALF_UNITS, _lib.OPT_GEMM_SWAP_AB)
+    old = [lib.moe_get_option(o) for o in opts]
+    for o, v in zip(opts, request.param):
+        assert lib.moe_set_option(o, v) == 0
     yield request.param
-    lib.moe_set_option(_lib.OPT_GEMM_CTA_PAIR, old[0])
-    lib.moe_set_option(_lib.OPT_GEMM_HALF_UNITS, old[1])
+    for o, v in zip(opts, old):
+        lib.moe_set_option(o, v)
 
 
 def tile_table(group_sizes):
