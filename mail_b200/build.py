@@ -17,7 +17,7 @@ CSRC = os.path.join(HERE, "csrc")
 BUILD_DIR = os.path.join(HERE, "_build")
 LIB_NAME = "libmoe_b200.so"
 LIB_PATH = os.path.join(HERE, LIB_NAME)
-SOURCES = ["moe_route.cu", "moe_rows.cu", "moe_gemm.cu", "moe_api.cu", "moe_ep.cu"]
+SOURCES = ["moe_route.cu", "moe_rows.cu", "moe_prep.cu", "moe_gemm.cu", "moe_api.cu", "moe_ep.cu"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 COMMON_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden"]
 

@@ -1,6 +1,7 @@
 // Internal helpers shared by the MoE translation units: status/error
 // reporting, dtype sizes, the compact tile table, and the device error flag.
 #pragma once
+#include <algorithm>
 #include <atomic>
 #include <cstdarg>
 #include <cstdint>
@@ -208,6 +209,15 @@ int zero_fill(void* dst, size_t bytes, cudaStream_t st);
 // moe_gather_rows, with padding rows zero-filled or left untouched (moe_rows.cu).
 int gather_rows(const void* src, int src_dtype, int64_t cols, const int32_t* sorted_slots, int top_k, int64_t rows,
                 const int32_t* rows_dev, void* dst, int dst_dtype, float* dst_scale, bool zero_pad, void* stream);
+
+// Decode-sized layer prep in one launch (moe_prep.cu): the align, the
+// permuting gather (+ int8 quantisation), and zero fills of two buffers.
+constexpr int64_t kPrepMaxSlots = 4096;
+bool prep_small_fits(int64_t slots, int num_experts);
+int prep_small(const int32_t* topk_ids, int64_t num_tokens, int top_k, int num_experts, int block_m,
+               const void* x, int x_dtype, int64_t hidden, void* xp, bool quant, float* xs, int32_t* sorted_slots,
+               int32_t* slot_pos, int32_t* group_sizes, int32_t* padded_offsets, int32_t* tile_table,
+               void* zero_a, size_t zero_a_bytes, void* zero_b, size_t zero_b_bytes, cudaStream_t st);
 
 // SM count of the current device (queried once per device; threads may race
 // to fill the cache with the same value).

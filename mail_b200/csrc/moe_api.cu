@@ -179,21 +179,30 @@ int run_experts(const ExpertsArgs& a) {
   cudaStream_t st = as_stream(stream);
 
   MOE_TRY(record_stage(MOE_STAGE_ENTRY, st));
-  MOE_TRY(moe_align(a.topk_ids, a.T, a.k, a.E, kBlockM, sorted, slot_pos, gs, poff, table, ws + w.align,
-                    w.align_bytes, stream));
-  MOE_TRY(record_stage(MOE_STAGE_ROUTED, st));
   const int32_t* rows_dev = table + 1;  // padded rows in use
   void* xp = ws + w.xp;
   float* xs = q ? reinterpret_cast<float*>(ws + w.xs) : nullptr;
-  // padding rows are left as they are: the GEMMs never store their results
-  MOE_TRY(gather_rows(a.x, a.x_dtype, a.H, sorted, a.k, w.cap, rows_dev, xp, q ? MOE_I8 : a.x_dtype, xs, false,
-                      stream));
-  MOE_TRY(record_stage(MOE_STAGE_GATHERED, st));
   void* h = ws + w.h;
-  int32_t* counters = nullptr;
-  if (w.plan.counter_bytes) {  // split-K counts of the gate_up GEMM start at zero
-    counters = reinterpret_cast<int32_t*>(ws + w.counters);
-    MOE_TRY(zero_fill(counters, w.plan.counter_bytes, st));
+  int32_t* counters = w.plan.counter_bytes ? reinterpret_cast<int32_t*>(ws + w.counters) : nullptr;
+  float* acc = nullptr;
+  if (a.mode == ExpertsOut::kCombineAtomic)
+    acc = (a.x_dtype == MOE_F32) ? static_cast<float*>(a.y) : reinterpret_cast<float*>(ws + w.y32);
+  // decode-sized batches: align, gather (+ quant) and both zero fills in one launch
+  const bool small = a.mode == ExpertsOut::kCombineAtomic && prep_small_fits(w.S, a.E);
+  if (small) {
+    MOE_TRY(prep_small(a.topk_ids, a.T, a.k, a.E, kBlockM, a.x, a.x_dtype, a.H, xp, q, xs, sorted, slot_pos, gs,
+                       poff, table, acc, (size_t)a.T * a.H * sizeof(float), counters, w.plan.counter_bytes, st));
+    MOE_TRY(record_stage(MOE_STAGE_ROUTED, st));
+    MOE_TRY(record_stage(MOE_STAGE_GATHERED, st));
+  } else {
+    MOE_TRY(moe_align(a.topk_ids, a.T, a.k, a.E, kBlockM, sorted, slot_pos, gs, poff, table, ws + w.align,
+                      w.align_bytes, stream));
+    MOE_TRY(record_stage(MOE_STAGE_ROUTED, st));
+    // padding rows are left as they are: the GEMMs never store their results
+    MOE_TRY(gather_rows(a.x, a.x_dtype, a.H, sorted, a.k, w.cap, rows_dev, xp, q ? MOE_I8 : a.x_dtype, xs, false,
+                        stream));
+    MOE_TRY(record_stage(MOE_STAGE_GATHERED, st));
+    if (counters) MOE_TRY(zero_fill(counters, w.plan.counter_bytes, st));  // split-K counts start at zero
   }
   MOE_TRY(gemm1_swiglu_planned(xp, q ? MOE_I8 : a.x_dtype, w.cap, a.H, a.w13, a.E, a.I, xs, a.w13_scale, table,
                                w.max_tiles, h, h_dtype, &w.plan, ws + w.partial, counters, st));
@@ -208,8 +217,7 @@ int run_experts(const ExpertsArgs& a) {
   }
   const int g2_dtype = q ? MOE_I8 : h_dtype;
   if (a.mode == ExpertsOut::kCombineAtomic) {
-    float* acc = (a.x_dtype == MOE_F32) ? static_cast<float*>(a.y) : reinterpret_cast<float*>(ws + w.y32);
-    MOE_TRY(zero_fill(acc, (size_t)a.T * a.H * sizeof(float), st));
+    if (!small) MOE_TRY(zero_fill(acc, (size_t)a.T * a.H * sizeof(float), st));
     MOE_TRY(record_stage(MOE_STAGE_PRE_GEMM2, st));
     MOE_TRY(gemm2_planned(a2, g2_dtype, w.cap, a.I, a.w2, a.E, a.H, hs, a.w2_scale, table, w.max_tiles,
                           MOE_EPI_COMBINE_ADD, sorted, a.topk_weights, a.k, acc, MOE_F32, a.T, &w.plan, st));

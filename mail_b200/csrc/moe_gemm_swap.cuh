@@ -353,31 +353,42 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         uint32_t g[16], u[16];
         ptx::tmem_ld16(tbase + c * 16, g);
         if constexpr (SWIGLU) ptx::tmem_ld16(tbase + p.nmax + c * 16, u);
+        // this chunk's per-token metadata, one token per lane (lanes 0-15),
+        // loaded in parallel and broadcast below
+        const int my_tok = c * 16 + (lane & 15);
+        const int64_t my_row = (int64_t)rstart + my_tok;
+        float m_sa = 1.f, m_w = 1.f;
+        int m_slot = -1;
+        if (my_tok < rcount) {
+          if constexpr (KIND == 2) m_sa = p.a_scale[my_row];
+          if (!SWIGLU && p.epi != MOE_EPI_STORE_ROWS) {
+            m_slot = p.row_map[my_row];
+            if (m_slot >= 0 && p.row_weight) m_w = p.row_weight[m_slot];
+          }
+        }
         ptx::tmem_ld_wait();
-        if (!feat_ok) continue;
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
           const int tok = c * 16 + j;
-          if (tok >= rcount) break;
+          if (tok >= rcount) break;  // uniform across the warp
           const int64_t row = (int64_t)rstart + tok;
-          float sa = 1.f;
-          if constexpr (KIND == 2) sa = p.a_scale[row];
+          const float sa = __shfl_sync(0xffffffffu, m_sa, j);
           if constexpr (SWIGLU) {
             const float gv = acc_value<KIND>(g[j]) * sa * ws_g;
             const float uv = acc_value<KIND>(u[j]) * sa * ws_u;
-            store1_out(p.out, p.out_dtype, row * p.ldo + feat, silu_mul(gv, uv));
+            if (feat_ok) store1_out(p.out, p.out_dtype, row * p.ldo + feat, silu_mul(gv, uv));
           } else {
+            const int32_t slot = __shfl_sync(0xffffffffu, m_slot, j);
+            const float w = __shfl_sync(0xffffffffu, m_w, j);
             const float v = acc_value<KIND>(g[j]) * sa * ws_g;
+            if (!feat_ok) continue;
             if (p.epi == MOE_EPI_STORE_ROWS) {
               if (row < p.out_rows) store1_out(p.out, p.out_dtype, row * p.ldo + feat, v);
-            } else {
-              const int32_t slot = p.row_map[row];
-              if (slot < 0) continue;
+            } else if (slot >= 0) {
               if (p.epi == MOE_EPI_COMBINE_ADD) {
                 const int64_t t = slot / p.top_k;
-                if (t < p.out_rows) red_add1(static_cast<float*>(p.out) + t * p.ldo + feat, v * p.row_weight[slot]);
+                if (t < p.out_rows) red_add1(static_cast<float*>(p.out) + t * p.ldo + feat, v * w);
               } else if (slot < p.out_rows) {  // MOE_EPI_SCATTER_ROWS
-                const float w = p.row_weight ? p.row_weight[slot] : 1.f;
                 store1_out(p.out, p.out_dtype, (int64_t)slot * p.ldo + feat, v * w);
               }
             }

@@ -44,6 +44,8 @@ CASES = [
     (64, 1024, 512, 8, 2, "uniform-softmax", torch.float32, False),  # tiny fp32 layer (tf32)
     (5, 512, 136, 16, 4, "sigmoid", torch.float16, False),        # ragged I: a partial feature tile
     (300, 256, 384, 64, 6, "hot25-zipf1.0", torch.bfloat16, False),  # a hot expert with several token tiles
+    (512, 1024, 256, 128, 8, "zipf1.2", torch.bfloat16, False),   # 4096 slots: the largest one-launch prep
+    (513, 1024, 256, 128, 8, "zipf1.2", torch.bfloat16, False),   # 4104 slots: align + gather launches
 ]
 
 
