@@ -515,11 +515,23 @@ def build_single(ctx, cfg, T, n_var, graph, weights=None):
             return mb.fused_moe_mlp(xx, w13, w2, gs)
         captured = None
     elif graph:
-        captured = mb.CapturedMoeMLP(w13, w2, T, cfg["k"], dtype=dt, scales=scales)
+        # one graph per set of input buffers, bound to them (a replay reads the
+        # resident inputs, no copies); the end-to-end pass's buffers get theirs
+        # on first use, in its warm-up
+        graphs = {}
+
+        def graph_for(xx, ii, ww):
+            key = (xx.data_ptr(), ii.data_ptr(), ww.data_ptr())
+            if key not in graphs:
+                graphs[key] = mb.CapturedMoeMLP(w13, w2, T, cfg["k"], dtype=dt, scales=scales, inputs=(xx, ww, ii))
+            return graphs[key]
+
+        for v in variants:
+            captured = graph_for(*v)
         kernels = captured.kernels
 
         def step(xx, ii, ww):
-            return captured(xx, ww, ii)
+            return graph_for(xx, ii, ww)(xx, ww, ii)
     else:
         captured = None
 

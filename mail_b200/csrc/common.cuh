@@ -107,6 +107,17 @@ struct GemmPlan {
 GemmPlan gemm_plan(int64_t slots, int num_experts, int64_t max_tiles, int64_t hidden, int64_t inter, int dtype,
                    bool combine);
 
+// Output conversion fused into the swapped down GEMM's combine epilogue: when
+// the last contribution to a (token, 32-output-feature group) of the fp32
+// accumulator has been added (a count per group reaching the token's routed
+// slots x K splits), the warp that added it converts the group to `out`.
+struct FusedConvert {
+  void* out;               // [T, H] in dtype
+  int dtype;
+  int32_t* counters;       // [T][H / 32 rounded up to 4 per 128], zero on entry
+  const int32_t* kvalid;   // [T] routed slots per token
+};
+
 // moe_gemm1_swiglu / moe_gemm2 with an explicit plan (nullptr: the row-major
 // kernels, or the swapped one when MOE_OPT_GEMM_SWAP_AB forces it) and, for a
 // gate_up split, its workspace (partial slots and zeroed counters).
@@ -117,7 +128,8 @@ int gemm1_swiglu_planned(const void* a, int dtype, int64_t a_rows, int64_t hidde
 int gemm2_planned(const void* h, int dtype, int64_t h_rows, int64_t inter, const void* w2, int num_experts,
                   int64_t hidden, const float* h_scale, const float* w2_scale, const int32_t* tile_table,
                   int64_t max_tiles, int epilogue, const int32_t* row_map, const float* row_weight, int top_k,
-                  void* out, int out_dtype, int64_t out_rows, const GemmPlan* plan, cudaStream_t stream);
+                  void* out, int out_dtype, int64_t out_rows, const GemmPlan* plan, cudaStream_t stream,
+                  const FusedConvert* convert = nullptr);
 
 // Down GEMM whose epilogue stores each output row into the buffer of the rank
 // that sent the row (peer pointers, NVLink stores). Defined in moe_gemm.cu.
@@ -217,7 +229,9 @@ bool prep_small_fits(int64_t slots, int num_experts);
 int prep_small(const int32_t* topk_ids, int64_t num_tokens, int top_k, int num_experts, int block_m,
                const void* x, int x_dtype, int64_t hidden, void* xp, bool quant, float* xs, int32_t* sorted_slots,
                int32_t* slot_pos, int32_t* group_sizes, int32_t* padded_offsets, int32_t* tile_table,
-               void* zero_a, size_t zero_a_bytes, void* zero_b, size_t zero_b_bytes, cudaStream_t st);
+               void* zero_a, size_t zero_a_bytes, void* zero_b, size_t zero_b_bytes, int32_t* kvalid, void* y,
+               cudaStream_t st);
+
 
 // SM count of the current device (queried once per device; threads may race
 // to fill the cache with the same value).

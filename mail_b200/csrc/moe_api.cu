@@ -92,7 +92,10 @@ struct FusedExpertsWs {
   int64_t S, cap, max_tiles;
   size_t align_bytes;
   GemmPlan plan;
-  size_t align, sorted, slot_pos, gs, poff, table, xp, xs, h, hq, hs, y32, o, partial, counters, bytes;
+  bool small;         // decode-sized: one prep launch, output conversion fused into the down GEMM
+  bool fused_convert;
+  size_t align, sorted, slot_pos, gs, poff, table, xp, xs, h, hq, hs, y32, o, partial, counters, conv_cnt, kvalid,
+      zero_end, bytes;
 };
 FusedExpertsWs fused_experts_ws(int64_t T, int64_t H, int64_t I, int E, int k, int x_dtype, int w_dtype,
                                 ExpertsOut mode) {
@@ -119,8 +122,14 @@ FusedExpertsWs fused_experts_ws(int64_t T, int64_t H, int64_t I, int E, int k, i
   w.y32 = c.take(atomic_acc ? (size_t)T * H * sizeof(float) : 0);
   w.o = c.take(mode == ExpertsOut::kCombineRows ? (size_t)w.cap * H * dtype_size(x_dtype) : 0);
   w.plan = gemm_plan(w.S, E, w.max_tiles, H, I, q ? MOE_I8 : x_dtype, mode == ExpertsOut::kCombineAtomic);
+  w.small = mode == ExpertsOut::kCombineAtomic && prep_small_fits(w.S, E);
+  w.fused_convert = w.small && w.plan.swap && x_dtype != MOE_F32;
   w.partial = c.take(w.plan.partial_bytes);
+  // zero-filled together by the prep launch: split-K counts, conversion counts
   w.counters = c.take(w.plan.counter_bytes);
+  w.conv_cnt = c.take(w.fused_convert ? (size_t)T * ceil_div(H, 128) * 4 * sizeof(int32_t) : 0);
+  w.zero_end = c.off;
+  w.kvalid = c.take(w.fused_convert ? (size_t)T * sizeof(int32_t) : 0);
   w.bytes = c.off;
   return w;
 }
@@ -187,11 +196,13 @@ int run_experts(const ExpertsArgs& a) {
   float* acc = nullptr;
   if (a.mode == ExpertsOut::kCombineAtomic)
     acc = (a.x_dtype == MOE_F32) ? static_cast<float*>(a.y) : reinterpret_cast<float*>(ws + w.y32);
-  // decode-sized batches: align, gather (+ quant) and both zero fills in one launch
-  const bool small = a.mode == ExpertsOut::kCombineAtomic && prep_small_fits(w.S, a.E);
+  // decode-sized batches: align, gather (+ quant) and the zero fills in one launch
+  const bool small = w.small;
+  int32_t* kvalid = w.fused_convert ? reinterpret_cast<int32_t*>(ws + w.kvalid) : nullptr;
   if (small) {
     MOE_TRY(prep_small(a.topk_ids, a.T, a.k, a.E, kBlockM, a.x, a.x_dtype, a.H, xp, q, xs, sorted, slot_pos, gs,
-                       poff, table, acc, (size_t)a.T * a.H * sizeof(float), counters, w.plan.counter_bytes, st));
+                       poff, table, acc, (size_t)a.T * a.H * sizeof(float), ws + w.counters,
+                       w.zero_end - w.counters, kvalid, a.y, st));
     MOE_TRY(record_stage(MOE_STAGE_ROUTED, st));
     MOE_TRY(record_stage(MOE_STAGE_GATHERED, st));
   } else {
@@ -219,10 +230,12 @@ int run_experts(const ExpertsArgs& a) {
   if (a.mode == ExpertsOut::kCombineAtomic) {
     if (!small) MOE_TRY(zero_fill(acc, (size_t)a.T * a.H * sizeof(float), st));
     MOE_TRY(record_stage(MOE_STAGE_PRE_GEMM2, st));
+    FusedConvert conv{a.y, a.x_dtype, reinterpret_cast<int32_t*>(ws + w.conv_cnt), kvalid};
     MOE_TRY(gemm2_planned(a2, g2_dtype, w.cap, a.I, a.w2, a.E, a.H, hs, a.w2_scale, table, w.max_tiles,
-                          MOE_EPI_COMBINE_ADD, sorted, a.topk_weights, a.k, acc, MOE_F32, a.T, &w.plan, st));
+                          MOE_EPI_COMBINE_ADD, sorted, a.topk_weights, a.k, acc, MOE_F32, a.T, &w.plan, st,
+                          w.fused_convert ? &conv : nullptr));
     MOE_TRY(record_stage(MOE_STAGE_GEMM2, st));
-    if (a.x_dtype != MOE_F32) MOE_TRY(moe_convert_f32(acc, a.T * a.H, a.y, a.x_dtype, stream));
+    if (a.x_dtype != MOE_F32 && !w.fused_convert) MOE_TRY(moe_convert_f32(acc, a.T * a.H, a.y, a.x_dtype, stream));
   } else if (a.mode == ExpertsOut::kCombineRows) {
     void* o = ws + w.o;
     MOE_TRY(record_stage(MOE_STAGE_PRE_GEMM2, st));

@@ -1005,7 +1005,7 @@ int gemm2_impl(const void* h, int dtype, int64_t h_rows, int64_t inter, const vo
                int64_t hidden, const float* h_scale, const float* w2_scale, const int32_t* tile_table,
                int64_t max_tiles, int epilogue, const int32_t* row_map, const float* row_weight, int top_k,
                void* out, int out_dtype, int64_t out_rows, void* const* peer_out, int num_peers,
-               const GemmPlan* plan, cudaStream_t stream) {
+               const GemmPlan* plan, cudaStream_t stream, const FusedConvert* convert = nullptr) {
   MOE_TRY(check_gemm_common("moe_gemm2", dtype, inter, num_experts, tile_table, max_tiles));
   MOE_CHECK_ARG(h && w2 && (out || peer_out), "moe_gemm2: NULL pointer");
   MOE_CHECK_ARG(hidden > 0 && hidden % 8 == 0, "moe_gemm2: hidden (%lld) must be a positive multiple of 8",
@@ -1053,6 +1053,13 @@ int gemm2_impl(const void* h, int dtype, int64_t h_rows, int64_t inter, const vo
     p.row_weight = row_weight;
     p.top_k = top_k > 0 ? top_k : 1;
     p.clock_slot = g_kernel_clocks_on.load() ? MOE_CLOCK_DOWN : -1;
+    if (convert && epilogue == MOE_EPI_COMBINE_ADD) {
+      MOE_CHECK_ARG(convert->out && convert->counters && convert->kvalid, "moe_gemm2: incomplete fused conversion");
+      p.conv_out = convert->out;
+      p.conv_dtype = convert->dtype;
+      p.conv_cnt = convert->counters;
+      p.conv_kvalid = convert->kvalid;
+    }
     return launch_swap<false>(dtype, tw, tx, p, stream);
   }
   CUtensorMap ta, tb, ta64;
@@ -1112,10 +1119,12 @@ int gemm2_scatter_peer(const void* h, int dtype, int64_t h_rows, int64_t inter, 
 int gemm2_planned(const void* h, int dtype, int64_t h_rows, int64_t inter, const void* w2, int num_experts,
                   int64_t hidden, const float* h_scale, const float* w2_scale, const int32_t* tile_table,
                   int64_t max_tiles, int epilogue, const int32_t* row_map, const float* row_weight, int top_k,
-                  void* out, int out_dtype, int64_t out_rows, const GemmPlan* plan, cudaStream_t stream) {
+                  void* out, int out_dtype, int64_t out_rows, const GemmPlan* plan, cudaStream_t stream,
+                  const FusedConvert* convert) {
   MOE_CHECK_ARG(out != nullptr, "moe_gemm2: NULL pointer");
   return gemm2_impl(h, dtype, h_rows, inter, w2, num_experts, hidden, h_scale, w2_scale, tile_table, max_tiles,
-                    epilogue, row_map, row_weight, top_k, out, out_dtype, out_rows, nullptr, 0, plan, stream);
+                    epilogue, row_map, row_weight, top_k, out, out_dtype, out_rows, nullptr, 0, plan, stream,
+                    convert);
 }
 }  // namespace moe
 

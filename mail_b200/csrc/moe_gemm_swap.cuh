@@ -63,6 +63,13 @@ struct SwapParams {
   void* partial;         // gate_up with splits > 1: [units][splits][2][128][nmax] 32-bit
   int32_t* counters;     // gate_up with splits > 1: [units][4], zero on entry, left zero
   int clock_slot;
+  // down GEMM, combine epilogue: fused conversion of the fp32 accumulator
+  // (out) to conv_out, per (token, 32-feature group), by the warp whose add
+  // completes the group: conv_cnt [T][nf * 4] zero on entry, conv_kvalid [T]
+  void* conv_out;
+  int conv_dtype;
+  int32_t* conv_cnt;
+  const int32_t* conv_kvalid;
 };
 
 __host__ __device__ constexpr int swap_na(bool swiglu) { return swiglu ? 2 : 1; }
@@ -397,6 +404,37 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
       ptx::tc_fence_before();
       ptx::mbar_arrive(&tempty[buf]);
+      if (!SWIGLU && p.conv_out != nullptr) {
+        // this warp's adds for its 32 features of the item's tokens are done:
+        // count them per token; the warp completing a (token, group) converts it
+        __threadfence();
+        __syncwarp();
+        const int ngroups = p.nf * 4;
+        const int group = f * 4 + q;
+        for (int t0 = 0; t0 < rcount; t0 += 32) {
+          const int tok = t0 + lane;
+          int64_t t = -1;
+          bool done = false;
+          if (tok < rcount) {
+            const int32_t slot = p.row_map[(int64_t)rstart + tok];
+            if (slot >= 0 && slot / p.top_k < p.out_rows) {
+              t = slot / p.top_k;
+              const int old = atomicAdd(&p.conv_cnt[t * ngroups + group], 1);
+              done = old == p.conv_kvalid[t] * p.splits - 1;
+            }
+          }
+          unsigned todo = __ballot_sync(0xffffffffu, done);
+          if (todo) __threadfence();
+          while (todo) {
+            const int j = __ffs(todo) - 1;
+            todo &= todo - 1;
+            const int64_t tt = __shfl_sync(0xffffffffu, t, j);
+            if (feat_ok)
+              store1_out(p.conv_out, p.conv_dtype, tt * p.ldo + feat,
+                         __ldcg(static_cast<const float*>(p.out) + tt * p.ldo + feat));
+          }
+        }
+      }
     }
     if (!ok) {
       if (lane == 0) raise_device_error(3);

@@ -17,7 +17,10 @@
 //     of sorted_slots are not written, the GEMMs never read them);
 //   * every CTA gathers its share of the routed rows (one warp per slot,
 //     16-byte accesses; int8 rows get absmax / 127 scales) and clears its
-//     share of the two zero-filled buffers.
+//     share of the two zero-filled buffers;
+//   * optionally (kvalid != NULL) the routed-slot count of every token, which
+//     the down GEMM's fused output conversion waits for, with a zero output
+//     row written here for a token whose slots were all dropped.
 #include "common.cuh"
 #include "rows.cuh"
 #include "scan.cuh"
@@ -35,7 +38,7 @@ __global__ void __launch_bounds__(kPrepThreads) prep_small_kernel(
     int64_t H, void* __restrict__ xp, float* __restrict__ xs, int32_t* __restrict__ sorted,
     int32_t* __restrict__ slot_pos, int32_t* __restrict__ gs, int32_t* __restrict__ poff_out,
     int32_t* __restrict__ table, uint4* __restrict__ zero_a, int64_t zero_a16, uint4* __restrict__ zero_b,
-    int64_t zero_b16) {
+    int64_t zero_b16, int32_t* __restrict__ kvalid, Tin* __restrict__ y) {
   pdl_begin();
   extern __shared__ int32_t sm[];
   const int E1 = E + 1;
@@ -170,6 +173,19 @@ __global__ void __launch_bounds__(kPrepThreads) prep_small_kernel(
 
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+  if (kvalid) {  // routed slots per token; a token with none gets a zero output row here
+    const int64_t T = S / k;
+    for (int64_t t = (int64_t)blockIdx.x * blockDim.x + tid; t < T; t += stride) {
+      int c = 0;
+      for (int j = 0; j < k; ++j) {
+        const int id = s_ids[t * k + j];
+        c += (id >= 0 && id < E);
+      }
+      kvalid[t] = c;
+      if (c == 0)
+        for (int64_t col = 0; col < H; col += 8) zero8(y + t * H + col);
+    }
+  }
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + tid; i < zero_a16; i += stride) zero_a[i] = z;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + tid; i < zero_b16; i += stride) zero_b[i] = z;
 }
@@ -183,7 +199,8 @@ bool prep_small_fits(int64_t slots, int num_experts) {
 int prep_small(const int32_t* topk_ids, int64_t num_tokens, int top_k, int num_experts, int block_m,
                const void* x, int x_dtype, int64_t hidden, void* xp, bool quant, float* xs, int32_t* sorted_slots,
                int32_t* slot_pos, int32_t* group_sizes, int32_t* padded_offsets, int32_t* tile_table,
-               void* zero_a, size_t zero_a_bytes, void* zero_b, size_t zero_b_bytes, cudaStream_t st) {
+               void* zero_a, size_t zero_a_bytes, void* zero_b, size_t zero_b_bytes, int32_t* kvalid, void* y,
+               cudaStream_t st) {
   const int64_t S = num_tokens * top_k;
   MOE_CHECK_ARG(prep_small_fits(S, num_experts), "prep_small: batch too large");
   MOE_CHECK_ARG(hidden % 8 == 0 && zero_a_bytes % 16 == 0 && zero_b_bytes % 16 == 0, "prep_small: bad sizes");
@@ -201,7 +218,8 @@ int prep_small(const int32_t* topk_ids, int64_t num_tokens, int top_k, int num_e
                                num_experts, block_m, max_tiles, static_cast<const TT*>(x), hidden, xp, xs,         \
                                sorted_slots, slot_pos, group_sizes, padded_offsets, tile_table,                    \
                                static_cast<uint4*>(zero_a), (int64_t)(zero_a_bytes / 16),                          \
-                               static_cast<uint4*>(zero_b), (int64_t)(zero_b_bytes / 16)));                        \
+                               static_cast<uint4*>(zero_b), (int64_t)(zero_b_bytes / 16), kvalid,                  \
+                               static_cast<TT*>(y)));                                                              \
   } while (0)
   if (x_dtype == MOE_BF16) {
     if (quant) PREP(__nv_bfloat16, true);

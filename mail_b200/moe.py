@@ -404,18 +404,29 @@ class CapturedMoeMLP:
     """The top-k fused_moe_mlp for one batch shape, captured in a CUDA graph.
 
     At decode sizes launching the op's kernels costs about as much as running
-    them; a replay launches the whole captured sequence at once. Inputs are
-    copied into static buffers and every replay writes the same output
-    tensor (copy it if it must outlive the next call).
+    them; a replay launches the whole captured sequence at once. By default
+    the graph reads static input buffers that each call fills by copying;
+    `inputs=(x, topk_weights, topk_ids)` binds the graph to those tensors
+    instead (a caller that writes them in place, e.g. the previous layer,
+    then calls with the same tensors and no copy happens). Every replay
+    writes the same output tensor (copy it if it must outlive the next call).
     """
 
     def __init__(self, w13: torch.Tensor, w2: torch.Tensor, num_tokens: int, top_k: int, dtype=torch.bfloat16,
-                 scales=None):
+                 scales=None, inputs=None):
         dev = w13.device
         H = w13.shape[1]
-        self.x = torch.zeros((num_tokens, H), dtype=dtype, device=dev)
-        self.ids = torch.zeros((num_tokens, top_k), dtype=torch.int32, device=dev)
-        self.w = torch.zeros((num_tokens, top_k), dtype=torch.float32, device=dev)
+        if inputs is None:
+            self.x = torch.zeros((num_tokens, H), dtype=dtype, device=dev)
+            self.w = torch.zeros((num_tokens, top_k), dtype=torch.float32, device=dev)
+            self.ids = torch.zeros((num_tokens, top_k), dtype=torch.int32, device=dev)
+        else:
+            self.x, self.w, self.ids = inputs
+            if (tuple(self.x.shape) != (num_tokens, H) or self.x.dtype != dtype or not self.x.is_contiguous()
+                    or tuple(self.ids.shape) != (num_tokens, top_k) or self.ids.dtype != torch.int32
+                    or self.w.dtype != torch.float32 or not self.ids.is_contiguous() or not self.w.is_contiguous()):
+                raise ValueError("CapturedMoeMLP: bound inputs must be contiguous x [T, H] (dtype), "
+                                 "topk_weights fp32 [T, k] and topk_ids int32 [T, k]")
         side = torch.cuda.Stream(dev)
         side.wait_stream(torch.cuda.current_stream(dev))
         with torch.cuda.stream(side):  # first call outside the capture (kernel attributes, caches)
@@ -428,9 +439,9 @@ class CapturedMoeMLP:
         self.kernels = int(_lib.load().moe_launch_count() - before)  # library kernels per replay
 
     def __call__(self, x: torch.Tensor, topk_weights: torch.Tensor, topk_ids: torch.Tensor) -> torch.Tensor:
-        self.x.copy_(x)
-        self.w.copy_(topk_weights)
-        self.ids.copy_(topk_ids)
+        for src, dst in ((x, self.x), (topk_weights, self.w), (topk_ids, self.ids)):
+            if src.data_ptr() != dst.data_ptr():
+                dst.copy_(src)
         self.graph.replay()
         return self.y
 

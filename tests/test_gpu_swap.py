@@ -118,3 +118,59 @@ def test_swapped_graph_replay_matches_eager():
         got = cap(x, wts_t, ids_t).float()
         assert max_abs_rel(got.cpu().numpy(), ref.cpu().numpy()) < 1e-2
     assert mb.device_error(dev()) == 0
+
+
+@pytest.mark.parametrize("quant", [False, True])
+def test_fused_conversion_with_dropped_tokens(quant):
+    """Decode-sized batch where some tokens have every slot dropped (ids
+    outside [0, E)) and others some: the down GEMM converts each output group
+    once all of its token's routed slots have been added, and the tokens with
+    none get zero rows."""
+    T, H, I, E, k = 24, 1024, 512, 64, 6
+    rng = np.random.default_rng(17)
+    x = torch.from_numpy(rng.standard_normal((T, H), dtype=np.float32)).to(dev(), torch.bfloat16)
+    w13 = (torch.randn(E, 2 * I, H, device=dev()) * 0.03).to(torch.bfloat16).transpose(1, 2)
+    w2 = (torch.randn(E, H, I, device=dev()) * 0.03).to(torch.bfloat16).transpose(1, 2)
+    ids, wts = O.synthetic_routing("zipf1.2", T, E, k, 4)
+    ids = ids.copy()
+    ids[[0, 7, 23]] = -1            # tokens with every slot dropped
+    ids[3, :4] = E + 5              # a token with two slots left
+    scales = None
+    if quant:
+        w13, w2, scales = mb.quantize_weights_int8(w13, w2)
+    y = mb.fused_moe_mlp(x, w13, w2, torch.from_numpy(wts).to(dev()), torch.from_numpy(ids).to(dev()),
+                         scales=scales)
+    yf = y.float().cpu().numpy()
+    assert (yf[[0, 7, 23]] == 0).all()
+    xf = x.float().cpu().numpy()
+    if quant:
+        ref = O.moe_mlp_w8a8(xf, w13.transpose(1, 2).cpu().numpy(), scales[0].cpu().numpy(),
+                             w2.transpose(1, 2).cpu().numpy(), scales[1].cpu().numpy(), wts, ids,
+                             round_hidden=O.round_bf16)
+    else:
+        ref = O.moe_mlp_topk(xf, w13.float().cpu().numpy(), w2.float().cpu().numpy(), wts, ids,
+                             round_hidden=O.round_bf16)
+    assert max_abs_rel(yf, ref) < TOL
+    assert mb.device_error(dev()) == 0
+
+
+def test_graph_bound_to_resident_inputs():
+    """CapturedMoeMLP with inputs=(x, w, ids): replays read those tensors
+    directly; rewriting them in place changes the next result."""
+    T, H, I, E, k = 8, 2048, 768, 128, 8
+    w13 = (torch.randn(E, 2 * I, H, device=dev()) * 0.02).to(torch.bfloat16).transpose(1, 2)
+    w2 = (torch.randn(E, H, I, device=dev()) * 0.02).to(torch.bfloat16).transpose(1, 2)
+    x = torch.randn(T, H, device=dev()).to(torch.bfloat16)
+    ids0, wts0 = O.synthetic_routing("zipf1.2", T, E, k, 1)
+    ids = torch.from_numpy(ids0).to(dev())
+    wts = torch.from_numpy(wts0).to(dev())
+    cap = mb.CapturedMoeMLP(w13, w2, T, k, dtype=torch.bfloat16, inputs=(x, wts, ids))
+    for seed in range(3):
+        ids_n, wts_n = O.synthetic_routing("zipf1.2", T, E, k, 10 + seed)
+        x.copy_(torch.randn(T, H, device=dev()))
+        ids.copy_(torch.from_numpy(ids_n))
+        wts.copy_(torch.from_numpy(wts_n))
+        got = cap(x, wts, ids).float()
+        ref = mb.fused_moe_mlp(x, w13, w2, wts, ids).float()
+        assert max_abs_rel(got.cpu().numpy(), ref.cpu().numpy()) < 1e-2
+    assert mb.device_error(dev()) == 0
