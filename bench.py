@@ -384,10 +384,24 @@ class Ctx:
         return list(tot), list(cnt)
 
 
-def timed_region(ctx, step, inp, steps, kernels_per_step=None, sample_clocks=True):
-    """Times exactly `steps` calls of step(*inp(i)) on the device (CUDA
-    events on the launching stream, barrier + synchronize on both sides, max
-    over ranks), with NVML clocks sampled during the region and the library's
+def run_steps(w, n):
+    """Runs steps 0 .. n-1 of a workload: from its chained graph (several
+    consecutive steps per replay) where one fits, else one step at a time."""
+    chain, G = w.get("chain"), w.get("chain_steps", 1)
+    i = 0
+    while i < n:
+        if chain is not None and n - i >= G:
+            chain.replay()
+            i += G
+        else:
+            w["step"](*w["inp"](i))
+            i += 1
+
+
+def timed_region(ctx, w, steps, kernels_per_step=None, sample_clocks=True):
+    """Times exactly `steps` steps of workload w on the device (CUDA events
+    on the launching stream, barrier + synchronize on both sides, max over
+    ranks), with NVML clocks sampled during the region and the library's
     kernel clocks read over it."""
     torch, lib = ctx.torch, ctx.lib
     sampler = ClockSampler(ctx.local_rank) if sample_clocks else None
@@ -401,8 +415,7 @@ def timed_region(ctx, step, inp, steps, kernels_per_step=None, sample_clocks=Tru
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0 = time.time()
     e0.record(ctx.stream)
-    for i in range(steps):
-        step(*inp(i))
+    run_steps(w, steps)
     e1.record(ctx.stream)
     torch.cuda.synchronize()
     t1 = time.time()
@@ -532,13 +545,30 @@ def build_single(ctx, cfg, T, n_var, graph, weights=None):
 
         def step(xx, ii, ww):
             return graph_for(xx, ii, ww)(xx, ww, ii)
+
+        if T <= 512:
+            # decode-sized steps take microseconds, as long as a graph launch:
+            # chain several consecutive steps (cycling the routings) in one
+            # graph, as a model's decode graph holds consecutive layers
+            G = len(variants) * -(-8 // len(variants))
+            chain = ctx.torch.cuda.CUDAGraph()
+            with ctx.torch.cuda.graph(chain):
+                for j in range(G):
+                    xx, ii, ww = variants[j % len(variants)]
+                    mb.fused_moe_mlp(xx, w13, w2, ww, ii, scales=scales)
+            extra = dict(chain=chain, chain_steps=G)
+        else:
+            extra = {}
     else:
         captured = None
 
         def step(xx, ii, ww):
             return mb.fused_moe_mlp(xx, w13, w2, ww, ii, scales=scales)
-    return dict(step=step, variants=variants, weights=weights, captured=captured, kernels=kernels, dt=dt,
-                inp=lambda i: variants[i % len(variants)])
+    out = dict(step=step, variants=variants, weights=weights, captured=captured, kernels=kernels, dt=dt,
+               inp=lambda i: variants[i % len(variants)])
+    if graph and not cfg.get("prerouted"):
+        out.update(extra)
+    return out
 
 
 def build_ep(ctx, cfg, T, ep_kind):
@@ -582,10 +612,9 @@ def run_config(ctx, name, T, args, peaks, int8, weights=None, steps=None, warmup
     else:
         n_var, l2 = n_variants(cfg, T, 1, ctx.rank)
         w = build_single(ctx, cfg, T, n_var, graph=True, weights=weights)
-    for i in range(warmup):
-        w["step"](*w["inp"](i))
+    run_steps(w, max(warmup, w.get("chain_steps", 1)))
     ctx.torch.cuda.synchronize()
-    r = timed_region(ctx, w["step"], w["inp"], steps, kernels_per_step=w["kernels"])
+    r = timed_region(ctx, w, steps, kernels_per_step=w["kernels"])
     ids_sets = [v[1].cpu().numpy() for v in w["variants"]]
     roof = gate_up_roofline(cfg, T, ctx.world, ids_sets, r["kernel_clocks"]["gate_up"]["ms_per_launch"], peaks,
                             int8, sustained=False)
@@ -593,7 +622,8 @@ def run_config(ctx, name, T, args, peaks, int8, weights=None, steps=None, warmup
            "tokens_per_gpu": T, "hidden": cfg["H"], "inter": cfg["I"], "experts": cfg["E"], "top_k": cfg["k"],
            "routing": cfg["routing"], "dtype": cfg["dtype"] + ("+w8a8" if cfg["quant"] else ""),
            "value": ctx.world * T / (r["ms"] / 1e3), "unit": "tokens/s", "ms_per_step": r["ms"], "steps": steps,
-           "kernel_clocks": r["kernel_clocks"], "roofline": roof, "clocks": r["clocks"], "l2": l2}
+           "kernel_clocks": r["kernel_clocks"], "roofline": roof, "clocks": r["clocks"], "l2": l2,
+           "graph_steps": w.get("chain_steps", 1)}
     if ctx.world == 1:
         # the step's own weight-streaming bound: every active expert's three
         # matrices once at the measured copy rate
@@ -811,6 +841,8 @@ def main():
                    "ep_exchange": args.ep if world > 1 else None, "cuda_graph": bool(args.graph and world == 1)}
     n_var, l2_note = n_variants(cfg, T, world, rank)
     config_json["l2"] = l2_note
+    if world == 1 and args.graph and T <= 512 and not cfg.get("prerouted"):
+        config_json["graph_steps"] = n_var * -(-8 // n_var)
 
     if args.impl == "reference":
         if rank != 0:
@@ -853,10 +885,9 @@ def main():
         args.graph = False
     else:
         w = build_single(ctx, cfg, T, n_var, graph=args.graph and not cfg.get("prerouted"))
-    for i in range(args.warmup):
-        w["step"](*w["inp"](i))
+    run_steps(w, max(args.warmup, w.get("chain_steps", 1)))
     torch.cuda.synchronize()
-    reg = timed_region(ctx, w["step"], w["inp"], args.steps, kernels_per_step=w["kernels"])
+    reg = timed_region(ctx, w, args.steps, kernels_per_step=w["kernels"])
     ms = reg["ms"]
     gemm1_ms = reg["kernel_clocks"]["gate_up"]["ms_per_launch"]
     gemm2_ms = reg["kernel_clocks"]["down"]["ms_per_launch"]
@@ -865,7 +896,7 @@ def main():
     sustained = None
     if args.sustain_s > 0:
         n_sus = max(args.steps, int(math.ceil(args.sustain_s * 1e3 / ms)))
-        sreg = timed_region(ctx, w["step"], w["inp"], n_sus, kernels_per_step=w["kernels"])
+        sreg = timed_region(ctx, w, n_sus, kernels_per_step=w["kernels"])
         sroof = gate_up_roofline(cfg, T, world, [v[1].cpu().numpy() for v in w["variants"]],
                                  sreg["kernel_clocks"]["gate_up"]["ms_per_launch"], peaks, None, sustained=True)
         sustained = {"value": world * T / (sreg["ms"] / 1e3), "unit": "tokens/s", "ms_per_step": sreg["ms"],

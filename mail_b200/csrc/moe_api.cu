@@ -83,6 +83,9 @@ enum class ExpertsOut {
 // read-modify-writes reach HBM and a row store + separate combine is cheaper.
 constexpr size_t kAtomicCombineMaxBytes = size_t(80) << 20;
 
+// Largest batch whose output conversion runs inside the down GEMM.
+constexpr int64_t kFusedConvertMaxTokens = 32;
+
 ExpertsOut combine_mode(int64_t T, int64_t H) {
   return (size_t)T * H * sizeof(float) <= kAtomicCombineMaxBytes ? ExpertsOut::kCombineAtomic
                                                                   : ExpertsOut::kCombineRows;
@@ -123,7 +126,9 @@ FusedExpertsWs fused_experts_ws(int64_t T, int64_t H, int64_t I, int E, int k, i
   w.o = c.take(mode == ExpertsOut::kCombineRows ? (size_t)w.cap * H * dtype_size(x_dtype) : 0);
   w.plan = gemm_plan(w.S, E, w.max_tiles, H, I, q ? MOE_I8 : x_dtype, mode == ExpertsOut::kCombineAtomic);
   w.small = mode == ExpertsOut::kCombineAtomic && prep_small_fits(w.S, E);
-  w.fused_convert = w.small && w.plan.swap && x_dtype != MOE_F32;
+  // fused conversion: saves the convert launch where it is a sizeable share of
+  // the step (a few tokens); per-token completion counts cost more above that
+  w.fused_convert = w.small && w.plan.swap && x_dtype != MOE_F32 && T <= kFusedConvertMaxTokens;
   w.partial = c.take(w.plan.partial_bytes);
   // zero-filled together by the prep launch: split-K counts, conversion counts
   w.counters = c.take(w.plan.counter_bytes);

@@ -355,38 +355,47 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
         continue;
       }
-#pragma unroll 1
-      for (int c = 0; c < nchunks; ++c) {
+      // the item's per-token metadata (activation scale, slot, routing
+      // weight), token 32 i + lane in register i: all loads issued at once
+      float m_sa[4], m_w[4];
+      int m_slot[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int tok = 32 * i + lane;
+        m_sa[i] = 1.f;
+        m_w[i] = 1.f;
+        m_slot[i] = -1;
+        if (tok < rcount) {
+          if constexpr (KIND == 2) m_sa[i] = p.a_scale[(int64_t)rstart + tok];
+          if (!SWIGLU && p.epi != MOE_EPI_STORE_ROWS) m_slot[i] = p.row_map[(int64_t)rstart + tok];
+        }
+      }
+      if (!SWIGLU && p.epi != MOE_EPI_STORE_ROWS && p.row_weight) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          if (m_slot[i] >= 0) m_w[i] = p.row_weight[m_slot[i]];
+      }
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {  // 16-token chunks (at most 128 tokens per item)
+        if (c >= nchunks) break;
         uint32_t g[16], u[16];
         ptx::tmem_ld16(tbase + c * 16, g);
         if constexpr (SWIGLU) ptx::tmem_ld16(tbase + p.nmax + c * 16, u);
-        // this chunk's per-token metadata, one token per lane (lanes 0-15),
-        // loaded in parallel and broadcast below
-        const int my_tok = c * 16 + (lane & 15);
-        const int64_t my_row = (int64_t)rstart + my_tok;
-        float m_sa = 1.f, m_w = 1.f;
-        int m_slot = -1;
-        if (my_tok < rcount) {
-          if constexpr (KIND == 2) m_sa = p.a_scale[my_row];
-          if (!SWIGLU && p.epi != MOE_EPI_STORE_ROWS) {
-            m_slot = p.row_map[my_row];
-            if (m_slot >= 0 && p.row_weight) m_w = p.row_weight[m_slot];
-          }
-        }
         ptx::tmem_ld_wait();
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
           const int tok = c * 16 + j;
           if (tok >= rcount) break;  // uniform across the warp
+          const int src_lane = (c & 1) * 16 + j;
           const int64_t row = (int64_t)rstart + tok;
-          const float sa = __shfl_sync(0xffffffffu, m_sa, j);
+          const float sa = __shfl_sync(0xffffffffu, m_sa[c >> 1], src_lane);
           if constexpr (SWIGLU) {
             const float gv = acc_value<KIND>(g[j]) * sa * ws_g;
             const float uv = acc_value<KIND>(u[j]) * sa * ws_u;
             if (feat_ok) store1_out(p.out, p.out_dtype, row * p.ldo + feat, silu_mul(gv, uv));
           } else {
-            const int32_t slot = __shfl_sync(0xffffffffu, m_slot, j);
-            const float w = __shfl_sync(0xffffffffu, m_w, j);
+            const int32_t slot = __shfl_sync(0xffffffffu, m_slot[c >> 1], src_lane);
+            const float w = __shfl_sync(0xffffffffu, m_w[c >> 1], src_lane);
             const float v = acc_value<KIND>(g[j]) * sa * ws_g;
             if (!feat_ok) continue;
             if (p.epi == MOE_EPI_STORE_ROWS) {
