@@ -815,6 +815,9 @@ def main():
                     help="launch the kernels with programmatic dependent launch (1, default)")
     ap.add_argument("--half-units", type=int, default=1, choices=[0, 1],
                     help="CTA-pair GEMMs: each expert's odd last M tile as an M=128 pair MMA (1, default)")
+    ap.add_argument("--swap", default="auto", choices=["auto", "on", "off"],
+                    help="grouped GEMM operand roles: weights as the MMA's 128-row operand for few rows per "
+                         "expert (auto), always (on), never (off)")
     ap.add_argument("--eager", action="store_true",
                     help="N=1: call the op directly each step instead of replaying it from a captured CUDA graph")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -838,7 +841,8 @@ def main():
                    "top_k": k, "routing": cfg["routing"], "dtype": cfg["dtype"] + ("+w8a8" if cfg["quant"] else ""),
                    "parallelism": f"ep{world}" if world > 1 else "single", "gemm": args.gemm,
                    "half_units": bool(args.half_units), "pdl": bool(args.pdl),
-                   "ep_exchange": args.ep if world > 1 else None, "cuda_graph": bool(args.graph and world == 1)}
+                   "ep_exchange": args.ep if world > 1 else None, "cuda_graph": bool(args.graph and world == 1),
+                   "swap_ab": args.swap}
     n_var, l2_note = n_variants(cfg, T, world, rank)
     config_json["l2"] = l2_note
     if world == 1 and args.graph and T <= 512 and not cfg.get("prerouted"):
@@ -875,6 +879,7 @@ def main():
         lib.moe_set_option(_lib.OPT_GEMM_BAND, args.band)
     lib.moe_set_option(_lib.OPT_GEMM_HALF_UNITS, args.half_units)
     lib.moe_set_option(_lib.OPT_PDL, args.pdl)
+    lib.moe_set_option(_lib.OPT_GEMM_SWAP_AB, {"auto": 2, "on": 1, "off": 0}[args.swap])
     lib.moe_set_option(_lib.OPT_KERNEL_CLOCKS, 1)  # before any capture: GEMM launches time themselves
     ctx = Ctx(torch, dist, lib, device, local_rank, world, rank)
     peaks = load_peaks()

@@ -129,6 +129,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   int32_t* s_cum = reinterpret_cast<int32_t*>(smem + (size_t)S * stage_bytes + BAR_BYTES);
+  // per epilogue warp: the current item's token slots, routing weights and
+  // activation scales (staged once per item, read back as broadcasts)
+  int32_t* s_meta = s_cum + align_up16((p.E + 1) * 4) / 4;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -355,57 +358,52 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
         continue;
       }
-      // the item's per-token metadata (activation scale, slot, routing
-      // weight), token 32 i + lane in register i: all loads issued at once
-      float m_sa[4], m_w[4];
-      int m_slot[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int tok = 32 * i + lane;
-        m_sa[i] = 1.f;
-        m_w[i] = 1.f;
-        m_slot[i] = -1;
-        if (tok < rcount) {
-          if constexpr (KIND == 2) m_sa[i] = p.a_scale[(int64_t)rstart + tok];
-          if (!SWIGLU && p.epi != MOE_EPI_STORE_ROWS) m_slot[i] = p.row_map[(int64_t)rstart + tok];
+      int32_t* m_slot = s_meta + (warp - 2) * 3 * SW_FEAT;
+      float* m_w = reinterpret_cast<float*>(m_slot + SW_FEAT);
+      float* m_sa = m_w + SW_FEAT;
+      const bool need_slot = !SWIGLU && p.epi != MOE_EPI_STORE_ROWS;
+      if (KIND == 2 || need_slot) {
+        __syncwarp();  // the previous item's reads of the staging area are done
+        for (int tok = lane; tok < rcount; tok += 32) {
+          const int64_t row = (int64_t)rstart + tok;
+          if constexpr (KIND == 2) m_sa[tok] = p.a_scale[row];
+          if (need_slot) {
+            const int32_t slot = p.row_map[row];
+            m_slot[tok] = slot;
+            m_w[tok] = (slot >= 0 && p.row_weight) ? p.row_weight[slot] : 1.f;
+          }
         }
+        __syncwarp();
       }
-      if (!SWIGLU && p.epi != MOE_EPI_STORE_ROWS && p.row_weight) {
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-          if (m_slot[i] >= 0) m_w[i] = p.row_weight[m_slot[i]];
-      }
-#pragma unroll
-      for (int c = 0; c < 8; ++c) {  // 16-token chunks (at most 128 tokens per item)
-        if (c >= nchunks) break;
+#pragma unroll 1
+      for (int c = 0; c < nchunks; ++c) {
         uint32_t g[16], u[16];
         ptx::tmem_ld16(tbase + c * 16, g);
         if constexpr (SWIGLU) ptx::tmem_ld16(tbase + p.nmax + c * 16, u);
         ptx::tmem_ld_wait();
+        if (!feat_ok) continue;
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
           const int tok = c * 16 + j;
-          if (tok >= rcount) break;  // uniform across the warp
-          const int src_lane = (c & 1) * 16 + j;
+          if (tok >= rcount) break;
           const int64_t row = (int64_t)rstart + tok;
-          const float sa = __shfl_sync(0xffffffffu, m_sa[c >> 1], src_lane);
+          const float sa = KIND == 2 ? m_sa[tok] : 1.f;
           if constexpr (SWIGLU) {
             const float gv = acc_value<KIND>(g[j]) * sa * ws_g;
             const float uv = acc_value<KIND>(u[j]) * sa * ws_u;
-            if (feat_ok) store1_out(p.out, p.out_dtype, row * p.ldo + feat, silu_mul(gv, uv));
+            store1_out(p.out, p.out_dtype, row * p.ldo + feat, silu_mul(gv, uv));
           } else {
-            const int32_t slot = __shfl_sync(0xffffffffu, m_slot[c >> 1], src_lane);
-            const float w = __shfl_sync(0xffffffffu, m_w[c >> 1], src_lane);
             const float v = acc_value<KIND>(g[j]) * sa * ws_g;
-            if (!feat_ok) continue;
             if (p.epi == MOE_EPI_STORE_ROWS) {
               if (row < p.out_rows) store1_out(p.out, p.out_dtype, row * p.ldo + feat, v);
-            } else if (slot >= 0) {
+            } else {
+              const int32_t slot = m_slot[tok];
+              if (slot < 0) continue;
               if (p.epi == MOE_EPI_COMBINE_ADD) {
                 const int64_t t = slot / p.top_k;
-                if (t < p.out_rows) red_add1(static_cast<float*>(p.out) + t * p.ldo + feat, v * w);
+                if (t < p.out_rows) red_add1(static_cast<float*>(p.out) + t * p.ldo + feat, v * m_w[tok]);
               } else if (slot < p.out_rows) {  // MOE_EPI_SCATTER_ROWS
-                store1_out(p.out, p.out_dtype, (int64_t)slot * p.ldo + feat, v * w);
+                store1_out(p.out, p.out_dtype, (int64_t)slot * p.ldo + feat, v * m_w[tok]);
               }
             }
           }
@@ -462,14 +460,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
 // ---------------------------------------------------------------- host side
 
+constexpr size_t SW_META_BYTES = 4 * 3 * SW_FEAT * 4;  // epilogue warps' token metadata staging
+
 size_t swap_smem_bytes(bool swiglu, int nmax, int stages, int E) {
   return 1024 + (size_t)stages * (swap_na(swiglu) * SW_A_TILE + (size_t)nmax * ROW_BYTES) + BAR_BYTES +
-         align_up16((E + 1) * 4);
+         align_up16((E + 1) * 4) + SW_META_BYTES;
 }
 
 int swap_stages(bool swiglu, int nmax, int E) {
   const size_t stage = swap_na(swiglu) * SW_A_TILE + (size_t)nmax * ROW_BYTES;
-  const size_t fixed = 1024 + BAR_BYTES + align_up16((E + 1) * 4);
+  const size_t fixed = 1024 + BAR_BYTES + align_up16((E + 1) * 4) + SW_META_BYTES;
   return (int)std::min<size_t>(SW_MAX_STAGES, (SW_SMEM_BUDGET - fixed) / stage);
 }
 
