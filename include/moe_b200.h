@@ -113,8 +113,9 @@ typedef enum {
                                moe_kernel_clocks); launches are captured with the setting in force when
                                they are issued, so set it before capturing a CUDA graph. 0 (default): off */
   MOE_OPT_GEMM_SWAP_AB = 7    /* operand roles of the grouped GEMMs. 2 (default): the all-in-one entry points
-                               swap them when the routed rows average at most 64 per expert that receives
-                               any (decode): the 128 weight rows of an output-feature tile are the MMA's M
+                               swap them in the gate_up GEMM when the routed rows average at most 64 per
+                               expert that receives any (decode), and in the down GEMM as well for at most
+                               32 routed slots: the 128 weight rows of an output-feature tile are the MMA's M
                                operand and the expert's token rows (rounded up to 16) its N operand, with
                                the K dimension split over more CTAs when a launch has few work items; the
                                stand-alone GEMM entry points keep rows as M. 1: always swap (stand-alone

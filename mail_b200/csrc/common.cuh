@@ -94,7 +94,8 @@ constexpr int kEpiScatterPeer = 3;
 // (moe_gemm.cu). swap: few token rows per expert, so the weights are the
 // MMA's 128-row operand and the tokens its N operand (moe_gemm_swap.cuh).
 struct GemmPlan {
-  bool swap = false;
+  bool swap = false;         // gate_up GEMM swapped
+  bool swap2 = false;        // down GEMM swapped as well
   int nmax = 128;            // token rows per swapped work item (32 or 128)
   int splits1 = 1;           // K splits of the gate_up GEMM (swapped)
   int splits2 = 1;           // K splits of the down GEMM (swapped, combine epilogue only)

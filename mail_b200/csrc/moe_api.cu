@@ -128,7 +128,7 @@ FusedExpertsWs fused_experts_ws(int64_t T, int64_t H, int64_t I, int E, int k, i
   w.small = mode == ExpertsOut::kCombineAtomic && prep_small_fits(w.S, E);
   // fused conversion: saves the convert launch where it is a sizeable share of
   // the step (a few tokens); per-token completion counts cost more above that
-  w.fused_convert = w.small && w.plan.swap && x_dtype != MOE_F32 && T <= kFusedConvertMaxTokens;
+  w.fused_convert = w.small && w.plan.swap2 && x_dtype != MOE_F32 && T <= kFusedConvertMaxTokens;
   w.partial = c.take(w.plan.partial_bytes);
   // zero-filled together by the prep launch: split-K counts, conversion counts
   w.counters = c.take(w.plan.counter_bytes);

@@ -874,6 +874,12 @@ GemmPlan gemm_plan(int64_t slots, int num_experts, int64_t max_tiles, int64_t hi
   p.swap = opt == 1 || (opt == 2 && slots > 0 && slots <= kSwapRowsPerExpert * nonempty);
   if (!p.swap) return p;
   p.nmax = (slots > 0 && slots <= 32) ? 32 : 128;
+  // the swapped down GEMM streams 16 KB of weights per stage next to the token
+  // rows and adds its combine one element at a time: measured against the
+  // row-major kernel on Qwen3-30B-A3B decode shapes it ties at 8 routed slots
+  // and loses from 64 on (T = 8: 30.2 vs 24.5 us; T = 256: 156 vs 71 us), so
+  // it runs only for the smallest batches, where it also converts the output
+  p.swap2 = opt == 1 || p.nmax == 32;
   const int64_t sms = num_sms();
   const int es = dtype_size(dtype);
   const int64_t nf1 = ceil_div(inter, SW_FEAT), nf2 = ceil_div(hidden, SW_FEAT);
@@ -885,7 +891,7 @@ GemmPlan gemm_plan(int64_t slots, int num_experts, int64_t max_tiles, int64_t hi
     return (int)std::max<int64_t>(1, std::min<int64_t>(sms / units, kb / 4));
   };
   p.splits1 = split(max_tiles * nf1, kb1);
-  p.splits2 = combine ? split(max_tiles * nf2, kb2) : 1;
+  p.splits2 = (combine && p.swap2) ? split(max_tiles * nf2, kb2) : 1;
   if (p.splits1 > 1) {
     p.partial_bytes = (size_t)max_tiles * nf1 * p.splits1 * 2 * SW_FEAT * p.nmax * 4;
     p.counter_bytes = (size_t)max_tiles * nf1 * 4 * sizeof(int32_t);
@@ -898,7 +904,7 @@ namespace {
 // MOE_OPT_GEMM_SWAP_AB = 1 only, 128 token rows per item, no K split.
 const GemmPlan* standalone_plan(GemmPlan* storage) {
   if (g_gemm_swap.load() != 1) return nullptr;
-  storage->swap = true;
+  storage->swap = storage->swap2 = true;
   return storage;
 }
 }  // namespace
@@ -1024,7 +1030,7 @@ int gemm2_impl(const void* h, int dtype, int64_t h_rows, int64_t inter, const vo
   MOE_CHECK_ARG((uintptr_t)h % 16 == 0 && (uintptr_t)w2 % 16 == 0 && (uintptr_t)out % 16 == 0,
                 "moe_gemm2: pointers must be 16-byte aligned");
   if (h_rows == 0 || max_tiles == 0) return MOE_OK;
-  if (plan && plan->swap && epilogue != kEpiScatterPeer) {
+  if (plan && plan->swap2 && epilogue != kEpiScatterPeer) {
     CUtensorMap tw, tx;
     MOE_TRY(make_tmap(&tw, w2, dtype, inter, (uint64_t)num_experts * hidden, SW_FEAT));
     MOE_TRY(make_tmap(&tx, h, dtype, inter, h_rows, SW_BOX));
