@@ -234,6 +234,12 @@ int prep_small(const int32_t* topk_ids, int64_t num_tokens, int top_k, int num_e
                cudaStream_t st);
 
 
+// Token-order scatter of the routed rows (+ per-token int8 quantisation):
+// dst[slot_pos[t * k + j]] = row t of src, each row read once (moe_rows.cu).
+bool scatter_rows_fits(int64_t cols);
+int scatter_rows(const void* src, int src_dtype, int64_t cols, const int32_t* slot_pos, int top_k, int64_t T,
+                 void* dst, int dst_dtype, float* dst_scale, cudaStream_t st);
+
 // SM count of the current device (queried once per device; threads may race
 // to fill the cache with the same value).
 inline int num_sms() {

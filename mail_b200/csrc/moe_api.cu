@@ -214,9 +214,14 @@ int run_experts(const ExpertsArgs& a) {
     MOE_TRY(moe_align(a.topk_ids, a.T, a.k, a.E, kBlockM, sorted, slot_pos, gs, poff, table, ws + w.align,
                       w.align_bytes, stream));
     MOE_TRY(record_stage(MOE_STAGE_ROUTED, st));
-    // padding rows are left as they are: the GEMMs never store their results
-    MOE_TRY(gather_rows(a.x, a.x_dtype, a.H, sorted, a.k, w.cap, rows_dev, xp, q ? MOE_I8 : a.x_dtype, xs, false,
-                        stream));
+    // padding rows are left as they are: the GEMMs never store their results.
+    // Token order: each activation row is read (and quantised) once and
+    // stored to its k padded rows
+    if (scatter_rows_fits(a.H))
+      MOE_TRY(scatter_rows(a.x, a.x_dtype, a.H, slot_pos, a.k, a.T, xp, q ? MOE_I8 : a.x_dtype, xs, st));
+    else
+      MOE_TRY(gather_rows(a.x, a.x_dtype, a.H, sorted, a.k, w.cap, rows_dev, xp, q ? MOE_I8 : a.x_dtype, xs, false,
+                          stream));
     MOE_TRY(record_stage(MOE_STAGE_GATHERED, st));
     if (counters) MOE_TRY(zero_fill(counters, w.plan.counter_bytes, st));  // split-K counts start at zero
   }

@@ -129,6 +129,75 @@ __global__ void __launch_bounds__(kQuantThreads) gather_quant_kernel(const Tin* 
   }
 }
 
+// Token-order scatter of the routed rows, the inverse of the gather: each
+// token's row is read once (RT threads per row, kept in registers), quantised
+// once when Tout is int8 (the quantisation is per token, so all k copies
+// share it), and stored to each of its k padded rows slot_pos[t * k + j]
+// (skipped where < 0). Reads T x H instead of the gather's T x k x H, which
+// comes from DRAM once the activations outgrow the L2.
+template <typename Tin, typename Tout, int RT>
+__global__ void __launch_bounds__(kQuantThreads) scatter_rows_kernel(const Tin* __restrict__ src, int64_t cols,
+                                                                     const int32_t* __restrict__ slot_pos,
+                                                                     int top_k, int64_t T,
+                                                                     Tout* __restrict__ dst,
+                                                                     float* __restrict__ dst_scale) {
+  pdl_begin();
+  constexpr bool QUANT = sizeof(Tout) == 1;
+  constexpr int kRowsPerPass = kQuantThreads / RT;
+  constexpr int kWarpsPerRow = RT / 32;
+  __shared__ float red[kQuantThreads / 32];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int grp = tid / RT, gt = tid % RT;
+  for (int64_t base = (int64_t)blockIdx.x * kRowsPerPass; base < T; base += (int64_t)gridDim.x * kRowsPerPass) {
+    const int64_t t = base + grp;
+    const bool active = t < T;
+    const Tin* s = active ? src + t * cols : nullptr;
+    float v[kQuantVecs][8];
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < kQuantVecs; ++i) {
+      const int64_t c = ((int64_t)i * RT + gt) * 8;
+      if (s && c < cols) {
+        load8(s + c, v[i]);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(v[i][j]));
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[i][j] = 0.f;
+      }
+    }
+    float scale = 0.f, inv = 0.f;
+    if constexpr (QUANT) {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+      if constexpr (kWarpsPerRow > 1) {
+        if (lane == 0) red[warp] = amax;
+        __syncthreads();
+        const int w0 = grp * kWarpsPerRow;
+        amax = red[w0];
+#pragma unroll
+        for (int w = 1; w < kWarpsPerRow; ++w) amax = fmaxf(amax, red[w0 + w]);
+        __syncthreads();
+      }
+      row_scales(amax, scale, inv);
+    }
+    if (!active) continue;
+    for (int j = 0; j < top_k; ++j) {
+      const int32_t pos = slot_pos[t * top_k + j];
+      if (pos < 0) continue;
+      Tout* d = dst + (int64_t)pos * cols;
+#pragma unroll
+      for (int i = 0; i < kQuantVecs; ++i) {
+        const int64_t c = ((int64_t)i * RT + gt) * 8;
+        if (c >= cols) continue;
+        if constexpr (QUANT) *reinterpret_cast<uint2*>(d + c) = quant8(v[i], inv);
+        else store8(d + c, v[i]);
+      }
+      if (QUANT && gt == 0 && dst_scale) dst_scale[pos] = scale;
+    }
+  }
+}
+
 template <typename To, typename Tacc>
 __global__ void __launch_bounds__(256) combine_rows_kernel(const To* __restrict__ o, int64_t hidden,
                                                            const int32_t* __restrict__ slot_pos,
@@ -203,6 +272,45 @@ int zero_fill(void* dst, size_t bytes, cudaStream_t st) {
 using namespace moe;
 
 namespace moe {
+bool scatter_rows_fits(int64_t cols) { return cols > 0 && cols % 8 == 0 && cols <= kQuantMaxCols; }
+
+int scatter_rows(const void* src, int src_dtype, int64_t cols, const int32_t* slot_pos, int top_k, int64_t T,
+                 void* dst, int dst_dtype, float* dst_scale, cudaStream_t st) {
+  MOE_CHECK_ARG(src && dst && slot_pos, "scatter_rows: NULL pointer");
+  MOE_CHECK_ARG(scatter_rows_fits(cols), "scatter_rows: cols %lld unsupported", (long long)cols);
+  MOE_CHECK_ARG(((uintptr_t)src % 16 == 0) && ((uintptr_t)dst % 16 == 0), "scatter_rows: pointers must be 16-byte aligned");
+  if (T == 0) return MOE_OK;
+  const int rt = cols <= 2048 ? 32 : (cols <= 4096 ? 64 : 128);
+  int64_t blocks = ceil_div(T, kQuantThreads / rt);
+  const int64_t cap = (int64_t)num_sms() * 16;
+  if (blocks > cap) blocks = cap;
+#define SCATTER(TI, TO, RT)                                                                                        \
+  MOE_CUDA_TRY(launch_kernel(scatter_rows_kernel<TI, TO, RT>, dim3((unsigned)blocks), dim3(kQuantThreads), 0, st, \
+                             static_cast<const TI*>(src), cols, slot_pos, top_k, T, static_cast<TO*>(dst),         \
+                             dst_scale))
+#define SCATTER_RT(TI, TO)           \
+  if (rt == 32) SCATTER(TI, TO, 32);  \
+  else if (rt == 64) SCATTER(TI, TO, 64); \
+  else SCATTER(TI, TO, 128);
+  if (dst_dtype == MOE_I8) {
+    MOE_CHECK_ARG(dst_scale != nullptr, "scatter_rows: int8 output needs dst_scale");
+    if (src_dtype == MOE_BF16) { SCATTER_RT(__nv_bfloat16, int8_t) }
+    else if (src_dtype == MOE_F16) { SCATTER_RT(__half, int8_t) }
+    else if (src_dtype == MOE_F32) { SCATTER_RT(float, int8_t) }
+    else return set_error(MOE_ERR_UNSUPPORTED, "scatter_rows: dtype %d not supported", src_dtype);
+  } else {
+    MOE_CHECK_ARG(dst_dtype == src_dtype, "scatter_rows: output dtype must be int8 or the input's");
+    if (src_dtype == MOE_BF16) { SCATTER_RT(__nv_bfloat16, __nv_bfloat16) }
+    else if (src_dtype == MOE_F16) { SCATTER_RT(__half, __half) }
+    else if (src_dtype == MOE_F32) { SCATTER_RT(float, float) }
+    else return set_error(MOE_ERR_UNSUPPORTED, "scatter_rows: dtype %d not supported", src_dtype);
+  }
+#undef SCATTER_RT
+#undef SCATTER
+  MOE_LAUNCH_CHECK("scatter_rows_kernel");
+  return MOE_OK;
+}
+
 // moe_gather_rows with a choice for padding rows (slot < 0): zero-filled
 // (zero_pad), or left as they are. The fused top-k pass leaves them: the
 // GEMMs compute padding rows but never store their results, so their content
