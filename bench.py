@@ -811,6 +811,8 @@ def main():
     ap.add_argument("--gemm", default="auto", choices=["auto", "pair", "single"],
                     help="grouped GEMM variant: CTA pairs (cta_group::2), one CTA per tile, or chosen by size")
     ap.add_argument("--band", type=int, default=0, help="GEMM tile-order band width in M tiles (0: default)")
+    ap.add_argument("--band-down", type=int, default=0,
+                    help="the down GEMM's band width in M tiles (0: the --band value)")
     ap.add_argument("--pdl", type=int, default=1, choices=[0, 1],
                     help="launch the kernels with programmatic dependent launch (1, default)")
     ap.add_argument("--half-units", type=int, default=1, choices=[0, 1],
@@ -877,6 +879,7 @@ def main():
     lib.moe_set_option(_lib.OPT_GEMM_CTA_PAIR, {"pair": 1, "single": 0, "auto": 2}[args.gemm])
     if args.band:
         lib.moe_set_option(_lib.OPT_GEMM_BAND, args.band)
+    lib.moe_set_option(_lib.OPT_GEMM_BAND_DOWN, args.band_down)
     lib.moe_set_option(_lib.OPT_GEMM_HALF_UNITS, args.half_units)
     lib.moe_set_option(_lib.OPT_PDL, args.pdl)
     lib.moe_set_option(_lib.OPT_GEMM_SWAP_AB, {"auto": 2, "on": 1, "off": 0}[args.swap])

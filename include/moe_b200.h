@@ -119,7 +119,9 @@ typedef enum {
                                operand and the expert's token rows (rounded up to 16) its N operand, with
                                the K dimension split over more CTAs when a launch has few work items; the
                                stand-alone GEMM entry points keep rows as M. 1: always swap (stand-alone
-                               GEMMs included, without K splits). 0: never */
+                               GEMMs included, without K splits). 0: never */,
+  MOE_OPT_GEMM_BAND_DOWN = 8  /* the down GEMM's band of M tiles (MOE_OPT_GEMM_BAND); 0 (default): the same
+                               band as the gate_up GEMM */
 } moe_option_t;
 MOE_API int moe_set_option(int option, int value);
 /* Current value of an option, or -1 for an unknown option. */

@@ -752,6 +752,7 @@ int kind_of(int dtype) { return dtype == MOE_F32 ? 1 : (dtype == MOE_I8 ? 2 : 0)
 // 0.277 vs 0.290 ms).
 std::atomic<int> g_gemm_cta_pair{2};
 std::atomic<int> g_gemm_band{GROUP_M};  // M tiles per band of the tile raster
+std::atomic<int> g_gemm_band_down{0};   // the down GEMM's band (0: g_gemm_band)
 // Stream-K split of the partial last wave for the additive combine epilogue.
 // Off by default: on the Mixtral layer the down GEMM measured 0.760 ms with it
 // and 0.745 ms without (the persistent grid's tail costs less than the extra
@@ -1085,7 +1086,7 @@ int gemm2_impl(const void* h, int dtype, int64_t h_rows, int64_t inter, const vo
   p.idesc = make_idesc(dtype, pair ? 2 * BM : BM);
   p.idesc_half = make_idesc(dtype, BM);
   p.half_units = half_units;
-  p.band_tiles = g_gemm_band.load();
+  p.band_tiles = g_gemm_band_down.load() ? g_gemm_band_down.load() : g_gemm_band.load();
   p.table = tile_table;
   p.max_tiles = (int)max_tiles;
   p.a_rows = h_rows;
@@ -1158,6 +1159,11 @@ extern "C" int moe_set_option(int option, int value) {
     g_gemm_band.store(value);
     return MOE_OK;
   }
+  if (option == MOE_OPT_GEMM_BAND_DOWN) {
+    MOE_CHECK_ARG(value >= 0 && value <= 1 << 20, "moe_set_option: GEMM_BAND_DOWN takes 0 .. 2^20 tiles");
+    g_gemm_band_down.store(value);
+    return MOE_OK;
+  }
   if (option == MOE_OPT_GEMM_STREAM_K) {
     g_gemm_stream_k.store(value != 0);
     return MOE_OK;
@@ -1185,6 +1191,7 @@ extern "C" int moe_set_option(int option, int value) {
 extern "C" int moe_get_option(int option) {
   if (option == MOE_OPT_GEMM_CTA_PAIR) return g_gemm_cta_pair.load();
   if (option == MOE_OPT_GEMM_BAND) return g_gemm_band.load();
+  if (option == MOE_OPT_GEMM_BAND_DOWN) return g_gemm_band_down.load();
   if (option == MOE_OPT_GEMM_STREAM_K) return g_gemm_stream_k.load();
   if (option == MOE_OPT_GEMM_HALF_UNITS) return g_gemm_half_units.load();
   if (option == MOE_OPT_PDL) return g_pdl.load();
