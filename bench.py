@@ -683,6 +683,7 @@ def e2e_pass(ctx, w, steps):
     up, down = torch.cuda.Stream(ctx.device), torch.cuda.Stream(ctx.device)
     h2d_ev = [torch.cuda.Event() for _ in range(NB)]
     comp_ev = [torch.cuda.Event() for _ in range(NB)]
+    d2h_buf_ev = [torch.cuda.Event() for _ in range(NB)]  # result of buffer b copied out
     d2h_ev = torch.cuda.Event()
 
     def e2e_step(i):
@@ -696,12 +697,15 @@ def e2e_pass(ctx, w, steps):
             wts_d[b].copy_(wh, non_blocking=True)
             h2d_ev[b].record(up)
         stream.wait_event(h2d_ev[b])
+        if i >= NB:
+            stream.wait_event(d2h_buf_ev[b])  # a replay rewrites the output step i-NB's copy reads
         y = step(x_d[b], ids_d[b], wts_d[b])
         comp_ev[b].record(stream)
         with torch.cuda.stream(down):
             down.wait_event(comp_ev[b])
             y.record_stream(down)
             y_h[b].copy_(y, non_blocking=True)
+            d2h_buf_ev[b].record(down)
             d2h_ev.record(down)
 
     for i in range(2 * NB):

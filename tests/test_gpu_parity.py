@@ -424,14 +424,17 @@ def test_fused_expert_rows_matches_oracle(dtype, quant, gemm_variant):
     assert_no_device_error()
 
 
-def test_launch_counter_counts_kernels():
-    x, w13, w2, ids, wts = topk_case(64, 256, 128, 4, 2, "uniform-softmax", torch.bfloat16)
+@pytest.mark.parametrize("T,k,E,kernels", [
+    (2, 8, 64, 3),      # <= 32 slots: prep + gate_up + down converting the output itself
+    (64, 2, 4, 4),      # <= 4096 slots: prep + gate_up + down + convert
+    (2100, 2, 4, 6),    # align + scatter + gate_up + output clear + down + convert
+])
+def test_launch_counter_counts_kernels(T, k, E, kernels):
+    x, w13, w2, ids, wts = topk_case(T, 256, 128, E, k, "uniform-softmax", torch.bfloat16)
     lib = _lib.load()
     before = lib.moe_launch_count()
     run_topk(x, w13, w2, ids, wts)
-    # align (one kernel for up to 16384 slots) + gather + gemm1 + output clear
-    # + gemm2 + convert
-    assert lib.moe_launch_count() - before == 6
+    assert lib.moe_launch_count() - before == kernels
 
 
 @pytest.mark.parametrize("T", [1, 256])
