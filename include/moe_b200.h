@@ -84,7 +84,9 @@ MOE_API int moe_version(void);
 MOE_API const char* moe_last_error(void);
 /* Copies the device error flag (0 = none, else a code identifying the stalled
  * pipeline role: 1 TMA producer, 2 MMA issuer, 3 epilogue, 4 drain,
- * 6 self-test) into *host_code and clears it. Synchronises `stream`. */
+ * 6 self-test, 7 device-wide barrier of the one-launch decode kernel) into
+ * *host_code and clears it (after code 7 it also re-arms that barrier).
+ * Synchronises `stream`. */
 MOE_API int moe_get_device_error(int* host_code, void* stream);
 /* Self-test of the bounded waits: one CTA waits on an mbarrier that nothing
  * completes; the wait gives up after timeout_ns (at most 2 s), the kernel
@@ -120,8 +122,14 @@ typedef enum {
                                the K dimension split over more CTAs when a launch has few work items; the
                                stand-alone GEMM entry points keep rows as M. 1: always swap (stand-alone
                                GEMMs included, without K splits). 0: never */,
-  MOE_OPT_GEMM_BAND_DOWN = 8  /* the down GEMM's band of M tiles (MOE_OPT_GEMM_BAND); 0 (default): the same
+  MOE_OPT_GEMM_BAND_DOWN = 8, /* the down GEMM's band of M tiles (MOE_OPT_GEMM_BAND); 0 (default): the same
                                band as the gate_up GEMM */
+  MOE_OPT_DECODE_FUSED = 9    /* 1 (default): moe_fused_experts runs a batch of at most 16 tokens and 128 routed
+                               slots (bf16/fp16, no int8) as one persistent kernel — routing, gate_up GEMM +
+                               SwiGLU, down GEMM + combine and output conversion as phases separated by
+                               device-wide barriers. Its barrier lives in the library's device memory, so
+                               two such calls must not run concurrently on one GPU (different streams);
+                               callers that overlap MoE calls on several streams set 0 */
 } moe_option_t;
 MOE_API int moe_set_option(int option, int value);
 /* Current value of an option, or -1 for an unknown option. */

@@ -16,7 +16,7 @@ LIB_PATH = os.path.join(_HERE, "libmoe_b200.so")
 F32, F16, BF16, I8, I32, I64 = 0, 1, 2, 3, 4, 5
 EPI_STORE_ROWS, EPI_COMBINE_ADD, EPI_SCATTER_ROWS = 0, 1, 2
 OPT_GEMM_CTA_PAIR, OPT_GEMM_BAND, OPT_GEMM_STREAM_K, OPT_GEMM_HALF_UNITS, OPT_PDL, OPT_KERNEL_CLOCKS = 1, 2, 3, 4, 5, 6
-OPT_GEMM_SWAP_AB, OPT_GEMM_BAND_DOWN = 7, 8
+OPT_GEMM_SWAP_AB, OPT_GEMM_BAND_DOWN, OPT_DECODE_FUSED = 7, 8, 9
 CLOCK_GATE_UP, CLOCK_DOWN, NUM_CLOCKS = 0, 1, 2
 STATUS = {0: "MOE_OK", 1: "MOE_ERR_INVALID_ARG", 2: "MOE_ERR_UNSUPPORTED", 3: "MOE_ERR_CUDA",
           4: "MOE_ERR_WORKSPACE", 5: "MOE_ERR_DEVICE"}

@@ -234,6 +234,15 @@ int prep_small(const int32_t* topk_ids, int64_t num_tokens, int top_k, int num_e
                cudaStream_t st);
 
 
+// The whole top-k layer for at most 16 tokens (and 128 routed slots) in one
+// persistent launch (moe_decode.cuh): routing, gate_up, down + combine,
+// conversion, separated by device-wide barriers (MOE_OPT_DECODE_FUSED).
+bool decode_fused_fits(int64_t T, int k, int E, int64_t H, int64_t I, int x_dtype, int w_dtype);
+size_t decode_fused_workspace(int64_t T, int k, int E, int64_t H, int64_t I, int dtype);
+int decode_fused(const void* x, int dtype, int64_t T, int64_t H, const void* w13, const void* w2, int E, int64_t I,
+                 const float* topk_weights, const int32_t* topk_ids, int k, void* y, void* workspace,
+                 size_t workspace_bytes, cudaStream_t st);
+
 // Token-order scatter of the routed rows (+ per-token int8 quantisation):
 // dst[slot_pos[t * k + j]] = row t of src, each row read once (moe_rows.cu).
 bool scatter_rows_fits(int64_t cols);

@@ -172,12 +172,24 @@ int check_experts(const ExpertsArgs& a) {
   return MOE_OK;
 }
 
+bool one_launch(const ExpertsArgs& a) {
+  return a.mode == ExpertsOut::kCombineAtomic && decode_fused_fits(a.T, a.k, a.E, a.H, a.I, a.x_dtype, a.w_dtype);
+}
+
 // align -> gather (+int8 quant) -> GEMM1 + SwiGLU -> (int8 quant of h) ->
-// GEMM2 with the output handling of a.mode.
+// GEMM2 with the output handling of a.mode; a decode-sized batch as one launch.
 int run_experts(const ExpertsArgs& a) {
   if (a.T == 0) return MOE_OK;
   MOE_CHECK_ARG(a.x && a.w13 && a.w2 && a.topk_ids && (a.topk_weights || a.mode == ExpertsOut::kScatterRows),
                 "%s: NULL input", a.name);
+  if (one_launch(a)) {
+    cudaStream_t st = as_stream(a.stream);
+    MOE_TRY(record_stage(MOE_STAGE_ENTRY, st));
+    MOE_TRY(decode_fused(a.x, a.x_dtype, a.T, a.H, a.w13, a.w2, a.E, a.I, a.topk_weights, a.topk_ids, a.k, a.y,
+                         a.workspace, a.workspace_bytes, st));
+    for (int s = MOE_STAGE_ROUTED; s <= MOE_STAGE_DONE; ++s) MOE_TRY(record_stage(s, st));
+    return MOE_OK;
+  }
   const FusedExpertsWs w = fused_experts_ws(a.T, a.H, a.I, a.E, a.k, a.x_dtype, a.w_dtype, a.mode);
   if (a.workspace_bytes < w.bytes || !a.workspace)
     return set_error(MOE_ERR_WORKSPACE, "%s: workspace %zu < %zu bytes", a.name, a.workspace_bytes, w.bytes);
@@ -326,9 +338,11 @@ extern "C" size_t moe_fused_experts_workspace_size(int64_t num_tokens, int64_t h
                                                    int num_experts, int top_k, int x_dtype, int w_dtype) {
   if (num_tokens < 0 || hidden <= 0 || inter <= 0 || num_experts <= 0 || top_k <= 0) return 0;
   if (dtype_size(x_dtype) == 0 || dtype_size(w_dtype) == 0) return 0;
-  return fused_experts_ws(num_tokens, hidden, inter, num_experts, top_k, x_dtype, w_dtype,
-                          combine_mode(num_tokens, hidden))
-      .bytes;
+  const ExpertsOut mode = combine_mode(num_tokens, hidden);
+  if (mode == ExpertsOut::kCombineAtomic &&
+      decode_fused_fits(num_tokens, top_k, num_experts, hidden, inter, x_dtype, w_dtype))
+    return decode_fused_workspace(num_tokens, top_k, num_experts, hidden, inter, x_dtype);
+  return fused_experts_ws(num_tokens, hidden, inter, num_experts, top_k, x_dtype, w_dtype, mode).bytes;
 }
 
 extern "C" int moe_fused_experts(const void* x, int x_dtype, int64_t num_tokens, int64_t hidden, const void* w13,

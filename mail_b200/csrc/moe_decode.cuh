@@ -1,0 +1,652 @@
+// The whole top-k MoE layer for a decode-sized batch in one launch.
+//
+// Included by moe_gemm.cu (same translation unit: device error flag, kernel
+// clocks, tensor maps, PTX wrappers). For at most kDecodeMaxTokens tokens
+// (the MMA's N = 16) and kDecodeMaxSlots routed slots, the layer's stages —
+// routing align, gate_up GEMM + SwiGLU, down GEMM + weighted combine, output
+// conversion — run as phases of one persistent kernel, one CTA per SM,
+// separated by device-wide barriers:
+//
+//   phase 0  every CTA reads the top-k ids and weights (at most 128 slots)
+//            and derives the active experts (distinct valid ids in increasing
+//            order; expert tile m = the m-th of them) and, per (tile, token),
+//            the token's summed routing weight for that expert; the fp32
+//            output accumulator is cleared
+//   phase 1  gate_up work items (tile m, 128-feature tile f, K split s):
+//            weights as the MMA's 128-row operand (gate and up rows, two
+//            accumulators), the N = 16 operand is x itself — the first 16 rows
+//            of x, rows past T zero-filled by TMA — so there is no gather.
+//            SwiGLU output h[m][t][i] for all T tokens of the tile (tokens not
+//            routed to the expert are computed and never used); with K split,
+//            each split stores fp32 partial sums instead
+//   barrier  (with K split: all CTAs add the partial sums in split order and
+//            apply SwiGLU, then a second barrier)
+//   phase 2  down work items (tile m, 128-output-feature tile): the N operand
+//            is h[m] (16 rows), the epilogue adds weight(m, t) * acc into the
+//            fp32 accumulator row of token t
+//   barrier, phase 3  the fp32 accumulator is converted to the output dtype
+//
+// The producer starts loading its first phase-2 weight tiles as soon as ring
+// stages free up after its last phase-1 stage, before the barrier (the
+// weights do not depend on h); only the h rows wait for the barrier. At one
+// token a phase-2 item's weights (128 rows x I) fit in the ring, so the down
+// projection's weight stream overlaps the gate_up phase's tail.
+//
+// Device-wide barrier: a count and a generation word in static device memory,
+// self-resetting (the last CTA to arrive clears the count and advances the
+// generation). All CTAs are resident at once (grid <= SM count, one CTA per
+// SM by its shared memory). Every wait is bounded; a barrier that times out
+// latches device error 7, and moe_get_device_error() also resets the barrier.
+// Two such launches must not overlap on one GPU (different streams).
+namespace moe {
+namespace {
+
+constexpr int kDecodeMaxTokens = 16;
+constexpr int kDecodeMaxSlots = 128;
+constexpr int DK_STAGE_A = 2 * SW_A_TILE;                  // 32 KB: gate + up tiles, or two w2 K blocks
+constexpr int DK_STAGE_B = 2 * kDecodeMaxTokens * ROW_BYTES;  // 4 KB: token boxes for the A tiles
+constexpr int DK_STAGE = DK_STAGE_A + DK_STAGE_B;
+constexpr int DK_STAGES = 6;
+constexpr int DK_TMEM_COLS = 64;                           // 2 buffers x (gate 16 + up 16) columns
+
+__device__ unsigned int g_decode_bar_count = 0;
+__device__ unsigned int g_decode_bar_gen = 0;
+
+// Device-wide barrier (one thread per CTA). Returns false after the time
+// limit or when *abort is raised.
+__device__ bool decode_grid_barrier(unsigned int nblocks, volatile int* abort) {
+  volatile unsigned int* gen_p = &g_decode_bar_gen;
+  const unsigned int gen = *gen_p;
+  __threadfence();
+  if (atomicAdd(&g_decode_bar_count, 1u) == nblocks - 1u) {
+    atomicExch(&g_decode_bar_count, 0u);
+    __threadfence();
+    atomicAdd(&g_decode_bar_gen, 1u);
+    return true;
+  }
+  const uint64_t t0 = ptx::globaltimer();
+  while (*gen_p == gen) {
+    if (*abort) return false;
+    if (ptx::globaltimer() - t0 > MOE_WAIT_TIMEOUT_NS) return false;
+    __nanosleep(64);
+  }
+  __threadfence();
+  return true;
+}
+
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+struct DecodeParams {
+  int T, k, E, I, H;
+  int nf1, nf2;          // feature tiles of 128: ceil(I / 128), ceil(H / 128)
+  int kb1, kb2;          // K blocks of 128 bytes: gate_up (H), down (I)
+  int splits1;           // K splits of the gate_up phase
+  int max_tiles;         // tiles reserved in h: min(E, T * k)
+  uint32_t idesc;        // M = 128, N = 16
+  const int32_t* ids;    // [T, k]
+  const float* wts;      // [T, k]
+  void* h;               // [max_tiles][16][I], x dtype
+  float* partial;        // splits1 > 1: [max_tiles * nf1][splits1][2][128][16]
+  float* y32;            // [T, H]
+  void* y;               // [T, H], x dtype
+  int dtype;             // MOE_BF16 or MOE_F16
+  int clock_slot;
+};
+
+template <int KIND>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    moe_decode_kernel(const __grid_constant__ CUtensorMap tmap_w13, const __grid_constant__ CUtensorMap tmap_w2,
+                      const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_h,
+                      const DecodeParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* ring = smem;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + DK_STAGES * DK_STAGE);
+  uint64_t* empty = full + DK_STAGES;
+  uint64_t* tfull = empty + DK_STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint64_t* epi_done = drain + 1;   // epilogue warps: a phase's global stores are done
+  uint64_t* grid_pass = epi_done + 1;  // producer: the device-wide barrier was passed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(grid_pass + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* s_A = reinterpret_cast<int*>(tmem_slot + 2);  // number of active experts
+  // routing tables (phase 0)
+  int32_t* s_act = reinterpret_cast<int32_t*>(smem + DK_STAGES * DK_STAGE + 256);  // [128] expert of tile m
+  int32_t* s_ids = s_act + kDecodeMaxSlots;                                          // [128] slot ids
+  float* s_w = reinterpret_cast<float*>(s_ids + kDecodeMaxSlots);                    // [128] slot weights
+  int* s_first = reinterpret_cast<int*>(s_w + kDecodeMaxSlots);                      // [128] first slot of its id
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int S = p.T * p.k;
+  constexpr int kElems = ROW_BYTES / (KIND == 0 ? 2 : 4);
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < DK_STAGES; ++i) {
+      ptx::mbar_init(&full[i], 1);
+      ptx::mbar_init(&empty[i], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      ptx::mbar_init(&tfull[a], 1);
+      ptx::mbar_init(&tempty[a], 4 * 32);
+    }
+    ptx::mbar_init(drain, 1);
+    ptx::mbar_init(epi_done, 4 * 32);
+    ptx::mbar_init(grid_pass, 1);
+    *abort_flag = 0;
+    ptx::fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    ptx::prefetch_tmap(&tmap_w13);
+    ptx::prefetch_tmap(&tmap_w2);
+    ptx::prefetch_tmap(&tmap_x);
+    ptx::prefetch_tmap(&tmap_h);
+  }
+  pdl_begin();
+  KernelClock* const clk = p.clock_slot >= 0 ? &g_kernel_clocks[p.clock_slot] : nullptr;
+  clock_begin(clk);
+  if (warp == 1) {
+    ptx::tmem_alloc(tmem_slot, DK_TMEM_COLS);
+    ptx::tmem_relinquish();
+  }
+
+  // ---------------------------------------------------------------- phase 0: routing
+  for (int s = threadIdx.x; s < kDecodeMaxSlots; s += blockDim.x) {
+    s_ids[s] = s < S ? p.ids[s] : -1;
+    s_w[s] = s < S ? p.wts[s] : 0.f;
+  }
+  __syncthreads();
+  // slot s is the first of its expert if no earlier slot has the same valid
+  // id; its tile = number of distinct valid ids smaller than its id
+  if (threadIdx.x < kDecodeMaxSlots) {
+    const int s = threadIdx.x, id = s_ids[s];
+    bool first = id >= 0 && id < p.E;
+    for (int j = 0; first && j < s; ++j) first = s_ids[j] != id;
+    s_first[s] = first;
+  }
+  __syncthreads();
+  if (threadIdx.x < S && s_first[threadIdx.x]) {
+    const int id = s_ids[threadIdx.x];
+    int rank = 0;
+    for (int j = 0; j < S; ++j) rank += s_first[j] && s_ids[j] < id;
+    s_act[rank] = id;
+  }
+  if (threadIdx.x == 0) {
+    int a = 0;
+    for (int j = 0; j < S; ++j) a += s_first[j];
+    *s_A = a;
+  }
+  __syncthreads();
+  // clear the fp32 accumulator (before the first barrier, so before any add)
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < (int64_t)p.T * p.H;
+       i += (int64_t)gridDim.x * blockDim.x)
+    p.y32[i] = 0.f;
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int A = *s_A;
+  const int items1 = A * p.nf1 * p.splits1;
+  const int items2 = A * p.nf2;
+  const int split_kb = (p.kb1 + p.splits1 - 1) / p.splits1;  // K blocks per split (last may be shorter)
+  const int stages2 = (p.kb2 + 1) / 2;                        // two w2 K blocks per stage
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int last_par[DK_STAGES];
+      for (int i = 0; i < DK_STAGES; ++i) last_par[i] = -1;
+      bool ok = true;
+      auto advance = [&]() {
+        last_par[stage] = (int)phase;
+        if (++stage == DK_STAGES) {
+          stage = 0;
+          phase ^= 1;
+        }
+      };
+      // phase 1: gate + up weight tiles and the x box of each K block
+      for (int it = blockIdx.x; ok && it < items1; it += gridDim.x) {
+        const int m = it / (p.nf1 * p.splits1), rem = it % (p.nf1 * p.splits1);
+        const int f = rem / p.splits1, s = rem % p.splits1;
+        const int e = s_act[m];
+        const int kb0 = s * split_kb, kb1 = min(p.kb1, kb0 + split_kb);
+        const int wrow = e * 2 * p.I + f * SW_FEAT;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!ptx::mbar_wait(&empty[stage], phase ^ 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          uint8_t* st = ring + stage * DK_STAGE;
+          const int kx = kb * kElems;
+          ptx::mbar_arrive_expect_tx(&full[stage], DK_STAGE_A + kDecodeMaxTokens * ROW_BYTES);
+          ptx::tma_load_2d(st, &tmap_w13, &full[stage], kx, wrow);
+          ptx::tma_load_2d(st + SW_A_TILE, &tmap_w13, &full[stage], kx, wrow + p.I);
+          ptx::tma_load_2d(st + DK_STAGE_A, &tmap_x, &full[stage], kx, 0);
+          advance();
+        }
+      }
+      // the first phase-2 stages' weights ahead of the barrier (they do not
+      // depend on h); a slot is free once its phase-1 MMAs are done, so these
+      // waits never depend on the barrier. At most one ring's worth.
+      int pend_stage[DK_STAGES], pend_kb[DK_STAGES], pend_m[DK_STAGES], npend = 0;
+      int it2 = blockIdx.x, kb2 = 0;  // next phase-2 stage: item it2, K blocks kb2, kb2 + 1
+      while (ok && it2 < items2 && npend < DK_STAGES) {
+        if (!ptx::mbar_wait(&empty[stage], phase ^ 1, abort_flag)) {
+          ok = false;
+          break;
+        }
+        const int m = it2 / p.nf2, f = it2 % p.nf2;
+        uint8_t* st = ring + stage * DK_STAGE;
+        const int nkb = min(2, p.kb2 - kb2);
+        ptx::mbar_arrive_expect_tx(&full[stage], nkb * (SW_A_TILE + kDecodeMaxTokens * ROW_BYTES));
+        for (int j = 0; j < nkb; ++j)
+          ptx::tma_load_2d(st + j * SW_A_TILE, &tmap_w2, &full[stage], (kb2 + j) * kElems,
+                           s_act[m] * p.H + f * SW_FEAT);
+        pend_stage[npend] = stage;
+        pend_kb[npend] = kb2;
+        pend_m[npend] = m;
+        ++npend;
+        advance();
+        kb2 += 2;
+        if (kb2 >= p.kb2) {
+          kb2 = 0;
+          it2 += gridDim.x;
+        }
+      }
+      // h is complete once every CTA's phase-1 stores (and, with a K split,
+      // the reduction's) are: rounds of (epilogue done -> barrier -> pass)
+      int rounds_done = 0;
+      const int rounds = p.splits1 > 1 ? 2 : 1;
+      for (; ok && rounds_done < rounds; ++rounds_done) {
+        if (!ptx::mbar_wait(epi_done, (uint32_t)rounds_done & 1, abort_flag) ||
+            !decode_grid_barrier(gridDim.x, abort_flag)) {
+          raise_device_error(7);
+          ok = false;
+          break;
+        }
+        ptx::mbar_arrive(grid_pass);
+      }
+      if (ok) {
+        fence_proxy_async_global();  // h was written through the generic proxy; TMA reads it
+        for (int i = 0; i < npend; ++i) {
+          uint8_t* st = ring + pend_stage[i] * DK_STAGE;
+          const int nkb = min(2, p.kb2 - pend_kb[i]);
+          for (int j = 0; j < nkb; ++j)
+            ptx::tma_load_2d(st + DK_STAGE_A + j * kDecodeMaxTokens * ROW_BYTES, &tmap_h, &full[pend_stage[i]],
+                             (pend_kb[i] + j) * kElems, pend_m[i] * kDecodeMaxTokens);
+        }
+      }
+      // the rest of phase 2
+      while (ok && it2 < items2) {
+        if (!ptx::mbar_wait(&empty[stage], phase ^ 1, abort_flag)) {
+          ok = false;
+          break;
+        }
+        const int m = it2 / p.nf2, f = it2 % p.nf2;
+        uint8_t* st = ring + stage * DK_STAGE;
+        const int nkb = min(2, p.kb2 - kb2);
+        ptx::mbar_arrive_expect_tx(&full[stage], nkb * (SW_A_TILE + kDecodeMaxTokens * ROW_BYTES));
+        for (int j = 0; j < nkb; ++j) {
+          ptx::tma_load_2d(st + j * SW_A_TILE, &tmap_w2, &full[stage], (kb2 + j) * kElems,
+                           s_act[m] * p.H + f * SW_FEAT);
+          ptx::tma_load_2d(st + DK_STAGE_A + j * kDecodeMaxTokens * ROW_BYTES, &tmap_h, &full[stage],
+                           (kb2 + j) * kElems, m * kDecodeMaxTokens);
+        }
+        advance();
+        kb2 += 2;
+        if (kb2 >= p.kb2) {
+          kb2 = 0;
+          it2 += gridDim.x;
+        }
+      }
+      // phase 3 starts after every CTA's adds
+      if (ok) {
+        if (!ptx::mbar_wait(epi_done, (uint32_t)rounds & 1, abort_flag) ||
+            !decode_grid_barrier(gridDim.x, abort_flag)) {
+          raise_device_error(7);
+          ok = false;
+        } else {
+          ptx::mbar_arrive(grid_pass);
+        }
+      }
+      if (!ok) {
+        raise_device_error(1);
+        *abort_flag = 1;
+        // release the epilogue warps still waiting for a pass (they see the
+        // abort flag), then let this CTA's copies in flight land
+        for (int r = rounds_done; r <= rounds; ++r) ptx::mbar_arrive(grid_pass);
+        volatile int never = 0;
+        for (int i = 0; i < DK_STAGES; ++i)
+          if (last_par[i] >= 0) ptx::mbar_wait(&full[i], (uint32_t)last_par[i], &never);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int it = 0;
+      bool ok = true;
+      for (int i1 = blockIdx.x; ok && i1 < items1; i1 += gridDim.x, ++it) {
+        const int rem = i1 % (p.nf1 * p.splits1);
+        const int s = rem % p.splits1;
+        const int kb0 = s * split_kb, kb1 = min(p.kb1, kb0 + split_kb);
+        const int buf = it & 1;
+        if (!ptx::mbar_wait(&tempty[buf], ((it >> 1) & 1) ^ 1, abort_flag)) {
+          ok = false;
+          break;
+        }
+        ptx::tc_fence_after();
+        const uint32_t d = tmem_base + (uint32_t)(buf * 32);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!ptx::mbar_wait(&full[stage], phase, abort_flag)) {
+            ok = false;
+            break;
+          }
+          ptx::tc_fence_after();
+          const uint32_t a_addr = ptx::smem_u32(ring + stage * DK_STAGE);
+          const uint32_t b_addr = a_addr + DK_STAGE_A;
+#pragma unroll
+          for (int kk = 0; kk < ROW_BYTES / 32; ++kk) {
+            const uint64_t bd = ptx::smem_desc_k128(b_addr + kk * 32);
+            const uint32_t acc = (kb > kb0 || kk > 0) ? 1u : 0u;
+            ptx::umma<KIND>(d, ptx::smem_desc_k128(a_addr + kk * 32), bd, p.idesc, acc);
+            ptx::umma<KIND>(d + 16, ptx::smem_desc_k128(a_addr + SW_A_TILE + kk * 32), bd, p.idesc, acc);
+          }
+          ptx::umma_commit(&empty[stage]);
+          if (++stage == DK_STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        ptx::umma_commit(&tfull[buf]);
+      }
+      for (int i2 = blockIdx.x; ok && i2 < items2; i2 += gridDim.x, ++it) {
+        const int buf = it & 1;
+        if (!ptx::mbar_wait(&tempty[buf], ((it >> 1) & 1) ^ 1, abort_flag)) {
+          ok = false;
+          break;
+        }
+        ptx::tc_fence_after();
+        const uint32_t d = tmem_base + (uint32_t)(buf * 32);
+        for (int st2 = 0; st2 < stages2; ++st2) {
+          if (!ptx::mbar_wait(&full[stage], phase, abort_flag)) {
+            ok = false;
+            break;
+          }
+          ptx::tc_fence_after();
+          const uint32_t a_addr = ptx::smem_u32(ring + stage * DK_STAGE);
+          const uint32_t b_addr = a_addr + DK_STAGE_A;
+          const int nkb = min(2, p.kb2 - 2 * st2);
+          for (int j = 0; j < nkb; ++j) {
+#pragma unroll
+            for (int kk = 0; kk < ROW_BYTES / 32; ++kk) {
+              const uint32_t acc = (st2 > 0 || j > 0 || kk > 0) ? 1u : 0u;
+              ptx::umma<KIND>(d, ptx::smem_desc_k128(a_addr + j * SW_A_TILE + kk * 32),
+                              ptx::smem_desc_k128(b_addr + j * kDecodeMaxTokens * ROW_BYTES + kk * 32), p.idesc, acc);
+            }
+          }
+          ptx::umma_commit(&empty[stage]);
+          if (++stage == DK_STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        ptx::umma_commit(&tfull[buf]);
+      }
+      if (!ok) {
+        raise_device_error(2);
+        *abort_flag = 1;
+      }
+      ptx::umma_commit(drain);
+      volatile int never = 0;
+      if (!ptx::mbar_wait(drain, 0, &never)) raise_device_error(4);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (128 threads)
+    const int q = warp & 3;
+    const int fit = q * 32 + lane;
+    const int et = threadIdx.x - 64;  // 0..127
+    bool ok = true;
+    int it = 0;
+    for (int i1 = blockIdx.x; i1 < items1; i1 += gridDim.x, ++it) {
+      const int m = i1 / (p.nf1 * p.splits1), rem = i1 % (p.nf1 * p.splits1);
+      const int f = rem / p.splits1, s = rem % p.splits1;
+      const int buf = it & 1;
+      const bool w_ok = ptx::mbar_wait(&tfull[buf], (it >> 1) & 1, abort_flag);
+      if (!__all_sync(0xffffffffu, w_ok)) {
+        ok = false;
+        break;
+      }
+      ptx::tc_fence_after();
+      uint32_t g[16], u[16];
+      const uint32_t tb = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * 32);
+      ptx::tmem_ld16(tb, g);
+      ptx::tmem_ld16(tb + 16, u);
+      ptx::tmem_ld_wait();
+      ptx::tc_fence_before();
+      ptx::mbar_arrive(&tempty[buf]);
+      const int feat = f * SW_FEAT + fit;
+      if (feat >= p.I) continue;
+      if (p.splits1 > 1) {
+        float* slot = p.partial + ((size_t)(m * p.nf1 + f) * p.splits1 + s) * 2 * SW_FEAT * kDecodeMaxTokens;
+        float* mine = slot + fit * kDecodeMaxTokens;
+#pragma unroll
+        for (int j = 0; j < 16; j += 4) {
+          *reinterpret_cast<float4*>(mine + j) = make_float4(acc_value<KIND>(g[j]), acc_value<KIND>(g[j + 1]),
+                                                             acc_value<KIND>(g[j + 2]), acc_value<KIND>(g[j + 3]));
+          *reinterpret_cast<float4*>(mine + SW_FEAT * kDecodeMaxTokens + j) =
+              make_float4(acc_value<KIND>(u[j]), acc_value<KIND>(u[j + 1]), acc_value<KIND>(u[j + 2]),
+                          acc_value<KIND>(u[j + 3]));
+        }
+      } else {
+#pragma unroll
+        for (int t = 0; t < kDecodeMaxTokens; ++t)
+          if (t < p.T)
+            store1_out(p.h, p.dtype, ((int64_t)m * kDecodeMaxTokens + t) * p.I + feat,
+                       silu_mul(acc_value<KIND>(g[t]), acc_value<KIND>(u[t])));
+      }
+    }
+    // phase-1 stores done: tell the producer, which arrives at the barrier;
+    // every later step waits for the producer's pass of the previous barrier,
+    // so epilogue and producer signals strictly alternate
+    volatile int never = 0;
+    uint32_t passes = 0;
+    auto wait_pass = [&]() {
+      const bool w = ptx::mbar_wait(grid_pass, passes & 1, &never);
+      ++passes;
+      return w && !*abort_flag;
+    };
+    __threadfence();
+    ptx::mbar_arrive(epi_done);
+    if (!wait_pass()) ok = false;
+    if (ok && p.splits1 > 1) {
+      if (ok) {
+        __threadfence();
+        // add the K splits' partial sums in split order and apply SwiGLU;
+        // element (m, t, i) of h over all CTAs' epilogue threads
+        const int64_t n = (int64_t)A * p.T * p.I;
+        for (int64_t idx = (int64_t)blockIdx.x * 128 + et; idx < n; idx += (int64_t)gridDim.x * 128) {
+          const int m = (int)(idx / ((int64_t)p.T * p.I));
+          const int t = (int)((idx / p.I) % p.T);
+          const int i = (int)(idx % p.I);
+          const float* base = p.partial + (size_t)(m * p.nf1 + i / SW_FEAT) * p.splits1 * 2 * SW_FEAT * kDecodeMaxTokens +
+                              (i % SW_FEAT) * kDecodeMaxTokens + t;
+          float gs = 0.f, us = 0.f;
+          for (int s = 0; s < p.splits1; ++s) {
+            gs += __ldcg(base + (size_t)s * 2 * SW_FEAT * kDecodeMaxTokens);
+            us += __ldcg(base + (size_t)s * 2 * SW_FEAT * kDecodeMaxTokens + SW_FEAT * kDecodeMaxTokens);
+          }
+          store1_out(p.h, p.dtype, ((int64_t)m * kDecodeMaxTokens + t) * p.I + i, silu_mul(gs, us));
+        }
+      }
+      __threadfence();
+      ptx::mbar_arrive(epi_done);
+      if (!wait_pass()) ok = false;
+    }
+    // phase 2: weighted adds into the fp32 accumulator
+    for (int i2 = blockIdx.x; ok && i2 < items2; i2 += gridDim.x, ++it) {
+      const int m = i2 / p.nf2, f = i2 % p.nf2;
+      const int buf = it & 1;
+      const bool w_ok = ptx::mbar_wait(&tfull[buf], (it >> 1) & 1, abort_flag);
+      if (!__all_sync(0xffffffffu, w_ok)) {
+        ok = false;
+        break;
+      }
+      ptx::tc_fence_after();
+      uint32_t v[16];
+      ptx::tmem_ld16(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * 32), v);
+      ptx::tmem_ld_wait();
+      ptx::tc_fence_before();
+      ptx::mbar_arrive(&tempty[buf]);
+      const int feat = f * SW_FEAT + fit;
+      if (feat >= p.H) continue;
+      const int e = s_act[m];
+#pragma unroll
+      for (int t = 0; t < kDecodeMaxTokens; ++t) {
+        if (t >= p.T) break;
+        float w = 0.f;  // token t's routing weight for expert e (summed if it lists e twice)
+        for (int j = 0; j < p.k; ++j)
+          if (s_ids[t * p.k + j] == e) w += s_w[t * p.k + j];
+        if (w != 0.f) red_add1(p.y32 + (int64_t)t * p.H + feat, w * acc_value<KIND>(v[t]));
+      }
+    }
+    __threadfence();
+    ptx::mbar_arrive(epi_done);
+    // phase 3: fp32 accumulator -> output dtype
+    if (ok) {
+      if (!wait_pass()) ok = false;
+      if (ok) {
+        __threadfence();
+        const int64_t n = (int64_t)p.T * p.H;
+        for (int64_t idx = (int64_t)blockIdx.x * 128 + et; idx < n; idx += (int64_t)gridDim.x * 128)
+          store1_out(p.y, p.dtype, idx, __ldcg(p.y32 + idx));
+      }
+    }
+    if (!ok) {
+      if (lane == 0) raise_device_error(3);
+      *abort_flag = 1;
+    }
+  }
+
+  __syncthreads();
+  clock_end(clk);
+  if (warp == 1) {
+    __syncwarp();
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem_base, DK_TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------- host side
+
+std::atomic<int> g_decode_fused{1};  // MOE_OPT_DECODE_FUSED
+
+constexpr size_t kDecodeSmem = 1024 + (size_t)DK_STAGES * DK_STAGE + 256 + 4 * kDecodeMaxSlots * 4;
+
+struct DecodeWs {
+  int max_tiles, nf1, nf2, kb1, kb2, splits1;
+  size_t h, partial, y32, bytes;
+};
+
+DecodeWs decode_ws(int64_t T, int k, int E, int64_t H, int64_t I, int dtype) {
+  DecodeWs w;
+  const int es = dtype_size(dtype);
+  w.max_tiles = (int)std::min<int64_t>(E, T * k);
+  w.nf1 = (int)ceil_div(I, SW_FEAT);
+  w.nf2 = (int)ceil_div(H, SW_FEAT);
+  w.kb1 = (int)ceil_div(H * es, ROW_BYTES);
+  w.kb2 = (int)ceil_div(I * es, ROW_BYTES);
+  const int64_t units1 = (int64_t)w.max_tiles * w.nf1, sms = num_sms();
+  w.splits1 = (2 * units1 <= sms) ? (int)std::max<int64_t>(1, std::min<int64_t>(sms / units1, w.kb1 / 4)) : 1;
+  size_t off = 0;
+  auto take = [&](size_t b) {
+    const size_t o = off;
+    off = align_up(off + b, 256);
+    return o;
+  };
+  w.h = take((size_t)w.max_tiles * kDecodeMaxTokens * I * es);
+  w.partial = take(w.splits1 > 1 ? (size_t)units1 * w.splits1 * 2 * SW_FEAT * kDecodeMaxTokens * 4 : 0);
+  w.y32 = take((size_t)T * H * 4);
+  w.bytes = off;
+  return w;
+}
+
+}  // namespace
+
+bool decode_fused_fits(int64_t T, int k, int E, int64_t H, int64_t I, int x_dtype, int w_dtype) {
+  return g_decode_fused.load() != 0 && T >= 1 && T <= kDecodeMaxTokens && T * k <= kDecodeMaxSlots && E >= 1 &&
+         E <= (1 << 20) && x_dtype == w_dtype && (x_dtype == MOE_BF16 || x_dtype == MOE_F16) && H % 8 == 0 &&
+         I % 8 == 0 && (int64_t)E * 2 * I < (int64_t(1) << 31) && (int64_t)E * H < (int64_t(1) << 31);
+}
+
+size_t decode_fused_workspace(int64_t T, int k, int E, int64_t H, int64_t I, int dtype) {
+  return decode_ws(T, k, E, H, I, dtype).bytes;
+}
+
+int decode_fused(const void* x, int dtype, int64_t T, int64_t H, const void* w13, const void* w2, int E, int64_t I,
+                 const float* topk_weights, const int32_t* topk_ids, int k, void* y, void* workspace,
+                 size_t workspace_bytes, cudaStream_t st) {
+  MOE_CHECK_ARG(decode_fused_fits(T, k, E, H, I, dtype, dtype), "decode_fused: batch outside the one-launch path");
+  MOE_CHECK_ARG(x && w13 && w2 && topk_weights && topk_ids && y, "decode_fused: NULL pointer");
+  MOE_CHECK_ARG((uintptr_t)x % 16 == 0 && (uintptr_t)w13 % 16 == 0 && (uintptr_t)w2 % 16 == 0,
+                "decode_fused: pointers must be 16-byte aligned");
+  const DecodeWs w = decode_ws(T, k, E, H, I, dtype);
+  if (workspace_bytes < w.bytes || !workspace)
+    return set_error(MOE_ERR_WORKSPACE, "decode_fused: workspace %zu < %zu bytes", workspace_bytes, w.bytes);
+  char* ws = static_cast<char*>(workspace);
+  CUtensorMap t13, t2, tx, th;
+  MOE_TRY(make_tmap(&t13, w13, dtype, H, (uint64_t)E * 2 * I, SW_FEAT));
+  MOE_TRY(make_tmap(&t2, w2, dtype, I, (uint64_t)E * H, SW_FEAT));
+  MOE_TRY(make_tmap(&tx, x, dtype, H, T, kDecodeMaxTokens));
+  MOE_TRY(make_tmap(&th, ws + w.h, dtype, I, (uint64_t)w.max_tiles * kDecodeMaxTokens, kDecodeMaxTokens));
+  DecodeParams p{};
+  p.T = (int)T;
+  p.k = k;
+  p.E = E;
+  p.I = (int)I;
+  p.H = (int)H;
+  p.nf1 = w.nf1;
+  p.nf2 = w.nf2;
+  p.kb1 = w.kb1;
+  p.kb2 = w.kb2;
+  p.splits1 = w.splits1;
+  p.max_tiles = w.max_tiles;
+  p.idesc = (make_idesc(dtype, SW_FEAT) & ~(0x3Fu << 17)) | ((uint32_t)(kDecodeMaxTokens >> 3) << 17);
+  p.ids = topk_ids;
+  p.wts = topk_weights;
+  p.h = ws + w.h;
+  p.partial = reinterpret_cast<float*>(ws + w.partial);
+  p.y32 = reinterpret_cast<float*>(ws + w.y32);
+  p.y = y;
+  p.dtype = dtype;
+  p.clock_slot = g_kernel_clocks_on.load() ? MOE_CLOCK_GATE_UP : -1;
+  const int64_t items1 = (int64_t)w.max_tiles * w.nf1 * w.splits1, items2 = (int64_t)w.max_tiles * w.nf2;
+  const int64_t grid = std::min<int64_t>(num_sms(), std::max(items1, items2));
+  auto kfn = moe_decode_kernel<0>;
+  MOE_CUDA_TRY(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kDecodeSmem));
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3(NUM_THREADS);
+  cfg.dynamicSmemBytes = kDecodeSmem;
+  cfg.stream = st;
+  if (pdl_enabled()) {
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+  MOE_CUDA_TRY(cudaLaunchKernelEx(&cfg, kfn, t13, t2, tx, th, p));
+  MOE_LAUNCH_CHECK("moe_decode_kernel");
+  return MOE_OK;
+}
+
+}  // namespace moe

@@ -852,6 +852,7 @@ int check_gemm_common(const char* fn, int dtype, int64_t k, int E, const int32_t
 }  // namespace moe
 
 #include "moe_gemm_swap.cuh"
+#include "moe_decode.cuh"
 
 using namespace moe;
 
@@ -862,6 +863,11 @@ extern "C" int moe_get_device_error(int* host_code, void* stream) {
   MOE_CUDA_TRY(cudaMemcpyFromSymbolAsync(host_code, g_moe_device_error, sizeof(int), 0, cudaMemcpyDeviceToHost, st));
   MOE_CUDA_TRY(cudaMemcpyToSymbolAsync(g_moe_device_error, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, st));
   MOE_CUDA_TRY(cudaStreamSynchronize(st));
+  if (*host_code == 7) {  // a barrier of the one-launch decode kernel timed out: re-arm it
+    static const unsigned int z = 0;
+    MOE_CUDA_TRY(cudaMemcpyToSymbolAsync(g_decode_bar_count, &z, sizeof(z), 0, cudaMemcpyHostToDevice, st));
+    MOE_CUDA_TRY(cudaStreamSynchronize(st));
+  }
   return MOE_OK;
 }
 
@@ -1159,6 +1165,10 @@ extern "C" int moe_set_option(int option, int value) {
     g_gemm_band.store(value);
     return MOE_OK;
   }
+  if (option == MOE_OPT_DECODE_FUSED) {
+    g_decode_fused.store(value != 0);
+    return MOE_OK;
+  }
   if (option == MOE_OPT_GEMM_BAND_DOWN) {
     MOE_CHECK_ARG(value >= 0 && value <= 1 << 20, "moe_set_option: GEMM_BAND_DOWN takes 0 .. 2^20 tiles");
     g_gemm_band_down.store(value);
@@ -1192,6 +1202,7 @@ extern "C" int moe_get_option(int option) {
   if (option == MOE_OPT_GEMM_CTA_PAIR) return g_gemm_cta_pair.load();
   if (option == MOE_OPT_GEMM_BAND) return g_gemm_band.load();
   if (option == MOE_OPT_GEMM_BAND_DOWN) return g_gemm_band_down.load();
+  if (option == MOE_OPT_DECODE_FUSED) return g_decode_fused.load();
   if (option == MOE_OPT_GEMM_STREAM_K) return g_gemm_stream_k.load();
   if (option == MOE_OPT_GEMM_HALF_UNITS) return g_gemm_half_units.load();
   if (option == MOE_OPT_PDL) return g_pdl.load();

@@ -33,7 +33,7 @@ namespace {
 constexpr int SW_FEAT = 128;            // weight rows per MMA (UMMA M)
 constexpr int SW_BOX = 16;              // token rows per TMA box
 constexpr int SW_MAX_STAGES = 12;
-constexpr int SW_SMEM_BUDGET = 220 * 1024;
+constexpr int SW_SMEM_BUDGET = 226 * 1024;  // of the 227 KB a CTA may use
 constexpr uint32_t SW_A_TILE = SW_FEAT * ROW_BYTES;  // 16 KiB
 
 struct SwapParams {
