@@ -24,6 +24,17 @@ def max_abs_rel(y, ref):
     return float(np.abs(y - ref).max() / max(np.abs(ref).max(), 1e-30))
 
 
+@pytest.fixture(autouse=True)
+def multi_launch_path():
+    """These tests cover the multi-launch path's swapped GEMMs: the one-launch
+    decode kernel (tested in test_gpu_decode.py) is switched off."""
+    lib = _lib.load()
+    old = lib.moe_get_option(_lib.OPT_DECODE_FUSED)
+    lib.moe_set_option(_lib.OPT_DECODE_FUSED, 0)
+    yield
+    lib.moe_set_option(_lib.OPT_DECODE_FUSED, old)
+
+
 @pytest.fixture(params=[2, 1], ids=["swap_auto", "swap_forced"])
 def swap(request):
     lib = _lib.load()
