@@ -23,8 +23,11 @@
 //            apply SwiGLU, then a second barrier)
 //   phase 2  down work items (tile m, 128-output-feature tile): the N operand
 //            is h[m] (16 rows), the epilogue adds weight(m, t) * acc into the
-//            fp32 accumulator row of token t
-//   barrier, phase 3  the fp32 accumulator is converted to the output dtype
+//            fp32 accumulator row of token t, then counts the add per (token,
+//            32-feature group); the warp whose add completes a group (its
+//            token's distinct experts all added) converts it to the output
+//            dtype — no barrier after phase 2. The counts and the accumulator
+//            are cleared in phase 0: nothing touches them before the barrier
 //
 // The producer starts loading its first phase-2 weight tiles as soon as ring
 // stages free up after its last phase-1 stage, before the barrier (the
@@ -43,6 +46,7 @@ namespace {
 
 constexpr int kDecodeMaxTokens = 16;
 constexpr int kDecodeMaxSlots = 128;
+constexpr int kDecodeMaxSplits = 8;  // K splits of the gate_up phase
 constexpr int DK_STAGE_A = 2 * SW_A_TILE;                  // 32 KB: gate + up tiles, or two w2 K blocks
 constexpr int DK_STAGE_B = 2 * kDecodeMaxTokens * ROW_BYTES;  // 4 KB: token boxes for the A tiles
 constexpr int DK_STAGE = DK_STAGE_A + DK_STAGE_B;
@@ -90,6 +94,7 @@ struct DecodeParams {
   void* h;               // [max_tiles][16][I], x dtype
   float* partial;        // splits1 > 1: [max_tiles * nf1][splits1][2][128][16]
   float* y32;            // [T, H]
+  int32_t* conv_cnt;     // [T][nf2 * 4] adds per (token, 32-feature group)
   void* y;               // [T, H], x dtype
   int dtype;             // MOE_BF16 or MOE_F16
   int clock_slot;
@@ -118,6 +123,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   int32_t* s_ids = s_act + kDecodeMaxSlots;                                          // [128] slot ids
   float* s_w = reinterpret_cast<float*>(s_ids + kDecodeMaxSlots);                    // [128] slot weights
   int* s_first = reinterpret_cast<int*>(s_w + kDecodeMaxSlots);                      // [128] first slot of its id
+  int* s_kd = s_first + kDecodeMaxSlots;                                             // [16] distinct experts per token
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -180,10 +186,30 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     *s_A = a;
   }
   __syncthreads();
-  // clear the fp32 accumulator (before the first barrier, so before any add)
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < (int64_t)p.T * p.H;
-       i += (int64_t)gridDim.x * blockDim.x)
+  if (threadIdx.x < p.T) {  // distinct valid experts of token t: the adds its output groups wait for
+    const int t = threadIdx.x;
+    int c = 0;
+    for (int j = 0; j < p.k; ++j) {
+      const int id = s_ids[t * p.k + j];
+      bool first = id >= 0 && id < p.E;
+      for (int q = 0; first && q < j; ++q) first = s_ids[t * p.k + q] != id;
+      c += first;
+    }
+    s_kd[t] = c;
+  }
+  // clear the fp32 accumulator and the group counts (before the first
+  // barrier, so before any add)
+  const int64_t gstride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < (int64_t)p.T * p.H; i += gstride)
     p.y32[i] = 0.f;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < (int64_t)p.T * p.nf2 * 4; i += gstride)
+    p.conv_cnt[i] = 0;
+  __syncthreads();
+  // a token whose slots were all dropped gets a zero output row here
+  for (int t = 0; t < p.T; ++t)
+    if (s_kd[t] == 0)
+      for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < p.H; i += gstride)
+        store1_out(p.y, p.dtype, (int64_t)t * p.H + i, 0.f);
   ptx::tc_fence_before();
   __syncthreads();
   ptx::tc_fence_after();
@@ -191,7 +217,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const int A = *s_A;
   const int items1 = A * p.nf1 * p.splits1;
   const int items2 = A * p.nf2;
-  const int split_kb = (p.kb1 + p.splits1 - 1) / p.splits1;  // K blocks per split (last may be shorter)
   const int stages2 = (p.kb2 + 1) / 2;                        // two w2 K blocks per stage
 
   if (warp == 0) {
@@ -214,7 +239,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const int m = it / (p.nf1 * p.splits1), rem = it % (p.nf1 * p.splits1);
         const int f = rem / p.splits1, s = rem % p.splits1;
         const int e = s_act[m];
-        const int kb0 = s * split_kb, kb1 = min(p.kb1, kb0 + split_kb);
+        const int kb0 = s * p.kb1 / p.splits1, kb1 = (s + 1) * p.kb1 / p.splits1;  // balanced, non-empty
         const int wrow = e * 2 * p.I + f * SW_FEAT;
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!ptx::mbar_wait(&empty[stage], phase ^ 1, abort_flag)) {
@@ -304,22 +329,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           it2 += gridDim.x;
         }
       }
-      // phase 3 starts after every CTA's adds
-      if (ok) {
-        if (!ptx::mbar_wait(epi_done, (uint32_t)rounds & 1, abort_flag) ||
-            !decode_grid_barrier(gridDim.x, abort_flag)) {
-          raise_device_error(7);
-          ok = false;
-        } else {
-          ptx::mbar_arrive(grid_pass);
-        }
-      }
       if (!ok) {
         raise_device_error(1);
         *abort_flag = 1;
         // release the epilogue warps still waiting for a pass (they see the
         // abort flag), then let this CTA's copies in flight land
-        for (int r = rounds_done; r <= rounds; ++r) ptx::mbar_arrive(grid_pass);
+        for (int r = rounds_done; r < rounds; ++r) ptx::mbar_arrive(grid_pass);
         volatile int never = 0;
         for (int i = 0; i < DK_STAGES; ++i)
           if (last_par[i] >= 0) ptx::mbar_wait(&full[i], (uint32_t)last_par[i], &never);
@@ -335,7 +350,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       for (int i1 = blockIdx.x; ok && i1 < items1; i1 += gridDim.x, ++it) {
         const int rem = i1 % (p.nf1 * p.splits1);
         const int s = rem % p.splits1;
-        const int kb0 = s * split_kb, kb1 = min(p.kb1, kb0 + split_kb);
+        const int kb0 = s * p.kb1 / p.splits1, kb1 = (s + 1) * p.kb1 / p.splits1;  // balanced, non-empty
         const int buf = it & 1;
         if (!ptx::mbar_wait(&tempty[buf], ((it >> 1) & 1) ^ 1, abort_flag)) {
           ok = false;
@@ -479,10 +494,21 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           const int i = (int)(idx % p.I);
           const float* base = p.partial + (size_t)(m * p.nf1 + i / SW_FEAT) * p.splits1 * 2 * SW_FEAT * kDecodeMaxTokens +
                               (i % SW_FEAT) * kDecodeMaxTokens + t;
+          float gp[kDecodeMaxSplits], up[kDecodeMaxSplits];
+#pragma unroll
+          for (int s = 0; s < kDecodeMaxSplits; ++s) {  // every split's loads in flight at once
+            gp[s] = 0.f;
+            up[s] = 0.f;
+            if (s < p.splits1) {
+              gp[s] = __ldcg(base + (size_t)s * 2 * SW_FEAT * kDecodeMaxTokens);
+              up[s] = __ldcg(base + (size_t)s * 2 * SW_FEAT * kDecodeMaxTokens + SW_FEAT * kDecodeMaxTokens);
+            }
+          }
           float gs = 0.f, us = 0.f;
-          for (int s = 0; s < p.splits1; ++s) {
-            gs += __ldcg(base + (size_t)s * 2 * SW_FEAT * kDecodeMaxTokens);
-            us += __ldcg(base + (size_t)s * 2 * SW_FEAT * kDecodeMaxTokens + SW_FEAT * kDecodeMaxTokens);
+#pragma unroll
+          for (int s = 0; s < kDecodeMaxSplits; ++s) {  // added in split order
+            gs += gp[s];
+            us += up[s];
           }
           store1_out(p.h, p.dtype, ((int64_t)m * kDecodeMaxTokens + t) * p.I + i, silu_mul(gs, us));
         }
@@ -507,27 +533,33 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       ptx::tc_fence_before();
       ptx::mbar_arrive(&tempty[buf]);
       const int feat = f * SW_FEAT + fit;
-      if (feat >= p.H) continue;
+      const bool feat_ok = feat < p.H;
       const int e = s_act[m];
+      // lane t < T: token t's routing weight for expert e (summed if it
+      // lists e twice), broadcast to the warp below
+      float my_w = 0.f;
+      if (lane < p.T)
+        for (int j = 0; j < p.k; ++j)
+          if (s_ids[lane * p.k + j] == e) my_w += s_w[lane * p.k + j];
 #pragma unroll
       for (int t = 0; t < kDecodeMaxTokens; ++t) {
         if (t >= p.T) break;
-        float w = 0.f;  // token t's routing weight for expert e (summed if it lists e twice)
-        for (int j = 0; j < p.k; ++j)
-          if (s_ids[t * p.k + j] == e) w += s_w[t * p.k + j];
-        if (w != 0.f) red_add1(p.y32 + (int64_t)t * p.H + feat, w * acc_value<KIND>(v[t]));
+        const float w = __shfl_sync(0xffffffffu, my_w, t);
+        if (w != 0.f && feat_ok) red_add1(p.y32 + (int64_t)t * p.H + feat, w * acc_value<KIND>(v[t]));
       }
-    }
-    __threadfence();
-    ptx::mbar_arrive(epi_done);
-    // phase 3: fp32 accumulator -> output dtype
-    if (ok) {
-      if (!wait_pass()) ok = false;
-      if (ok) {
-        __threadfence();
-        const int64_t n = (int64_t)p.T * p.H;
-        for (int64_t idx = (int64_t)blockIdx.x * 128 + et; idx < n; idx += (int64_t)gridDim.x * 128)
-          store1_out(p.y, p.dtype, idx, __ldcg(p.y32 + idx));
+      // count this warp's adds per token; the warp completing a (token,
+      // group) converts its 32 features
+      __threadfence();
+      __syncwarp();
+      bool done = false;
+      if (lane < p.T && my_w != 0.f)
+        done = atomicAdd(&p.conv_cnt[lane * p.nf2 * 4 + f * 4 + q], 1) == s_kd[lane] - 1;
+      unsigned todo = __ballot_sync(0xffffffffu, done);
+      if (todo) __threadfence();
+      while (todo) {
+        const int t = __ffs(todo) - 1;
+        todo &= todo - 1;
+        if (feat_ok) store1_out(p.y, p.dtype, (int64_t)t * p.H + feat, __ldcg(p.y32 + (int64_t)t * p.H + feat));
       }
     }
     if (!ok) {
@@ -549,11 +581,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
 std::atomic<int> g_decode_fused{1};  // MOE_OPT_DECODE_FUSED
 
-constexpr size_t kDecodeSmem = 1024 + (size_t)DK_STAGES * DK_STAGE + 256 + 4 * kDecodeMaxSlots * 4;
+constexpr size_t kDecodeSmem = 1024 + (size_t)DK_STAGES * DK_STAGE + 256 + 4 * kDecodeMaxSlots * 4 + 16 * 4;
 
 struct DecodeWs {
   int max_tiles, nf1, nf2, kb1, kb2, splits1;
-  size_t h, partial, y32, bytes;
+  size_t h, partial, y32, conv_cnt, bytes;
 };
 
 DecodeWs decode_ws(int64_t T, int k, int E, int64_t H, int64_t I, int dtype) {
@@ -565,7 +597,9 @@ DecodeWs decode_ws(int64_t T, int k, int E, int64_t H, int64_t I, int dtype) {
   w.kb1 = (int)ceil_div(H * es, ROW_BYTES);
   w.kb2 = (int)ceil_div(I * es, ROW_BYTES);
   const int64_t units1 = (int64_t)w.max_tiles * w.nf1, sms = num_sms();
-  w.splits1 = (2 * units1 <= sms) ? (int)std::max<int64_t>(1, std::min<int64_t>(sms / units1, w.kb1 / 4)) : 1;
+  w.splits1 = (2 * units1 <= sms)
+                  ? (int)std::max<int64_t>(1, std::min<int64_t>({sms / units1, (int64_t)w.kb1 / 4, kDecodeMaxSplits}))
+                  : 1;
   size_t off = 0;
   auto take = [&](size_t b) {
     const size_t o = off;
@@ -575,6 +609,7 @@ DecodeWs decode_ws(int64_t T, int k, int E, int64_t H, int64_t I, int dtype) {
   w.h = take((size_t)w.max_tiles * kDecodeMaxTokens * I * es);
   w.partial = take(w.splits1 > 1 ? (size_t)units1 * w.splits1 * 2 * SW_FEAT * kDecodeMaxTokens * 4 : 0);
   w.y32 = take((size_t)T * H * 4);
+  w.conv_cnt = take((size_t)T * w.nf2 * 4 * sizeof(int32_t));
   w.bytes = off;
   return w;
 }
@@ -625,6 +660,7 @@ int decode_fused(const void* x, int dtype, int64_t T, int64_t H, const void* w13
   p.h = ws + w.h;
   p.partial = reinterpret_cast<float*>(ws + w.partial);
   p.y32 = reinterpret_cast<float*>(ws + w.y32);
+  p.conv_cnt = reinterpret_cast<int32_t*>(ws + w.conv_cnt);
   p.y = y;
   p.dtype = dtype;
   p.clock_slot = g_kernel_clocks_on.load() ? MOE_CLOCK_GATE_UP : -1;
