@@ -18,9 +18,10 @@
 //            of x, rows past T zero-filled by TMA — so there is no gather.
 //            SwiGLU output h[m][t][i] for all T tokens of the tile (tokens not
 //            routed to the expert are computed and never used); with K split,
-//            each split stores fp32 partial sums instead
-//   barrier  (with K split: all CTAs add the partial sums in split order and
-//            apply SwiGLU, then a second barrier)
+//            each split stores fp32 partial sums and the last split of a unit
+//            to finish (a count per epilogue warp) adds them in split order and
+//            applies SwiGLU
+//   barrier
 //   phase 2  down work items (tile m, 128-output-feature tile): the N operand
 //            is h[m] (16 rows), the epilogue adds weight(m, t) * acc into the
 //            fp32 accumulator row of token t, then counts the add per (token,
@@ -78,6 +79,23 @@ __device__ bool decode_grid_barrier(unsigned int nblocks, volatile int* abort) {
   return true;
 }
 
+// Counts one arrival on a 64-bit counter word in caller memory that nothing
+// clears: bits [16, 64) hold the launch's tag, [0, 16) the count. A word
+// whose tag differs (left by an earlier launch, or never written) counts as
+// zero. Returns 1 for the arrival that makes the count `total`, 0 otherwise,
+// -1 if the word stayed contended past a bound.
+__device__ __forceinline__ int tagged_count_last(unsigned long long* ctr, unsigned long long tag,
+                                                 unsigned int total) {
+  unsigned long long old = atomicAdd(ctr, 0ull);
+  for (int tries = 0; tries < 256; ++tries) {
+    const unsigned int cnt = ((old >> 16) == (tag >> 16)) ? (unsigned int)(old & 0xFFFFull) : 0u;
+    const unsigned long long prev = atomicCAS(ctr, old, (tag & ~0xFFFFull) | (cnt + 1));
+    if (prev == old) return cnt + 1 == total ? 1 : 0;
+    old = prev;
+  }
+  return -1;
+}
+
 __device__ __forceinline__ void fence_proxy_async_global() {
   asm volatile("fence.proxy.async.global;" ::: "memory");
 }
@@ -93,6 +111,7 @@ struct DecodeParams {
   const float* wts;      // [T, k]
   void* h;               // [max_tiles][16][I], x dtype
   float* partial;        // splits1 > 1: [max_tiles * nf1][splits1][2][128][16]
+  unsigned long long* split_cnt;  // splits1 > 1: [max_tiles * nf1][4] tagged counts (never cleared)
   float* y32;            // [T, H]
   int32_t* conv_cnt;     // [T][nf2 * 4] adds per (token, 32-feature group)
   void* y;               // [T, H], x dtype
@@ -185,36 +204,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     for (int j = 0; j < S; ++j) a += s_first[j];
     *s_A = a;
   }
-  __syncthreads();
-  if (threadIdx.x < p.T) {  // distinct valid experts of token t: the adds its output groups wait for
-    const int t = threadIdx.x;
-    int c = 0;
-    for (int j = 0; j < p.k; ++j) {
-      const int id = s_ids[t * p.k + j];
-      bool first = id >= 0 && id < p.E;
-      for (int q = 0; first && q < j; ++q) first = s_ids[t * p.k + q] != id;
-      c += first;
-    }
-    s_kd[t] = c;
-  }
-  // clear the fp32 accumulator and the group counts (before the first
-  // barrier, so before any add)
-  const int64_t gstride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < (int64_t)p.T * p.H; i += gstride)
-    p.y32[i] = 0.f;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < (int64_t)p.T * p.nf2 * 4; i += gstride)
-    p.conv_cnt[i] = 0;
-  __syncthreads();
-  // a token whose slots were all dropped gets a zero output row here
-  for (int t = 0; t < p.T; ++t)
-    if (s_kd[t] == 0)
-      for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < p.H; i += gstride)
-        store1_out(p.y, p.dtype, (int64_t)t * p.H + i, 0.f);
   ptx::tc_fence_before();
   __syncthreads();
   ptx::tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const int A = *s_A;
+  // this launch's tag for the split counts: the barrier generation, the same
+  // for every CTA until this launch's barrier, different for every launch
+  const unsigned long long split_tag =
+      ((unsigned long long)(*(volatile unsigned int*)&g_decode_bar_gen) << 32) | 0x9e370000ull;
   const int items1 = A * p.nf1 * p.splits1;
   const int items2 = A * p.nf2;
   const int stages2 = (p.kb2 + 1) / 2;                        // two w2 K blocks per stage
@@ -283,18 +281,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           it2 += gridDim.x;
         }
       }
-      // h is complete once every CTA's phase-1 stores (and, with a K split,
-      // the reduction's) are: rounds of (epilogue done -> barrier -> pass)
-      int rounds_done = 0;
-      const int rounds = p.splits1 > 1 ? 2 : 1;
-      for (; ok && rounds_done < rounds; ++rounds_done) {
-        if (!ptx::mbar_wait(epi_done, (uint32_t)rounds_done & 1, abort_flag) ||
-            !decode_grid_barrier(gridDim.x, abort_flag)) {
+      // h is complete once every CTA's phase-1 stores (and split reductions)
+      // are: this CTA's epilogue done -> device-wide barrier -> pass
+      bool passed = false;
+      if (ok) {
+        if (!ptx::mbar_wait(epi_done, 0, abort_flag) || !decode_grid_barrier(gridDim.x, abort_flag)) {
           raise_device_error(7);
           ok = false;
-          break;
+        } else {
+          ptx::mbar_arrive(grid_pass);
+          passed = true;
         }
-        ptx::mbar_arrive(grid_pass);
       }
       if (ok) {
         fence_proxy_async_global();  // h was written through the generic proxy; TMA reads it
@@ -334,7 +331,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         *abort_flag = 1;
         // release the epilogue warps still waiting for a pass (they see the
         // abort flag), then let this CTA's copies in flight land
-        for (int r = rounds_done; r < rounds; ++r) ptx::mbar_arrive(grid_pass);
+        if (!passed) ptx::mbar_arrive(grid_pass);
         volatile int never = 0;
         for (int i = 0; i < DK_STAGES; ++i)
           if (last_par[i] >= 0) ptx::mbar_wait(&full[i], (uint32_t)last_par[i], &never);
@@ -429,6 +426,28 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const int q = warp & 3;
     const int fit = q * 32 + lane;
     const int et = threadIdx.x - 64;  // 0..127
+    // phase-0 work of the epilogue warps, done before their first arrival
+    // (so before the barrier and any phase-2 add): distinct valid experts per
+    // token (the adds its output groups wait for), the fp32 accumulator and
+    // group counts cleared, zero output rows for tokens with no valid slot
+    if (warp == 2 && lane < p.T) {
+      int c = 0;
+      for (int j = 0; j < p.k; ++j) {
+        const int id = s_ids[lane * p.k + j];
+        bool first = id >= 0 && id < p.E;
+        for (int q2 = 0; first && q2 < j; ++q2) first = s_ids[lane * p.k + q2] != id;
+        c += first;
+      }
+      s_kd[lane] = c;
+    }
+    const int64_t estride = (int64_t)gridDim.x * 128;
+    for (int64_t i = (int64_t)blockIdx.x * 128 + et; i < (int64_t)p.T * p.H; i += estride) p.y32[i] = 0.f;
+    for (int64_t i = (int64_t)blockIdx.x * 128 + et; i < (int64_t)p.T * p.nf2 * 4; i += estride) p.conv_cnt[i] = 0;
+    asm volatile("bar.sync 1, 128;" ::: "memory");  // s_kd complete (epilogue warps only)
+    for (int t = 0; t < p.T; ++t)
+      if (s_kd[t] == 0)
+        for (int64_t i = (int64_t)blockIdx.x * 128 + et; i < p.H; i += estride)
+          store1_out(p.y, p.dtype, (int64_t)t * p.H + i, 0.f);
     bool ok = true;
     int it = 0;
     for (int i1 = blockIdx.x; i1 < items1; i1 += gridDim.x, ++it) {
@@ -449,19 +468,57 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       ptx::tc_fence_before();
       ptx::mbar_arrive(&tempty[buf]);
       const int feat = f * SW_FEAT + fit;
-      if (feat >= p.I) continue;
+      const bool feat_ok = feat < p.I;
       if (p.splits1 > 1) {
-        float* slot = p.partial + ((size_t)(m * p.nf1 + f) * p.splits1 + s) * 2 * SW_FEAT * kDecodeMaxTokens;
-        float* mine = slot + fit * kDecodeMaxTokens;
+        const int unit = m * p.nf1 + f;
+        constexpr size_t kSplit = 2 * SW_FEAT * kDecodeMaxTokens;  // floats per split slot
+        const float* slot0 = p.partial + (size_t)unit * p.splits1 * kSplit;
+        float* mine = const_cast<float*>(slot0) + s * kSplit + fit * kDecodeMaxTokens;
+        if (feat_ok) {
 #pragma unroll
-        for (int j = 0; j < 16; j += 4) {
-          *reinterpret_cast<float4*>(mine + j) = make_float4(acc_value<KIND>(g[j]), acc_value<KIND>(g[j + 1]),
-                                                             acc_value<KIND>(g[j + 2]), acc_value<KIND>(g[j + 3]));
-          *reinterpret_cast<float4*>(mine + SW_FEAT * kDecodeMaxTokens + j) =
-              make_float4(acc_value<KIND>(u[j]), acc_value<KIND>(u[j + 1]), acc_value<KIND>(u[j + 2]),
-                          acc_value<KIND>(u[j + 3]));
+          for (int j = 0; j < 16; j += 4) {
+            *reinterpret_cast<float4*>(mine + j) = make_float4(acc_value<KIND>(g[j]), acc_value<KIND>(g[j + 1]),
+                                                               acc_value<KIND>(g[j + 2]), acc_value<KIND>(g[j + 3]));
+            *reinterpret_cast<float4*>(mine + SW_FEAT * kDecodeMaxTokens + j) =
+                make_float4(acc_value<KIND>(u[j]), acc_value<KIND>(u[j + 1]), acc_value<KIND>(u[j + 2]),
+                            acc_value<KIND>(u[j + 3]));
+          }
         }
-      } else {
+        // the last split of the unit (per warp: its 32 features) adds the
+        // slots in split order and applies SwiGLU
+        __threadfence();
+        __syncwarp();
+        int last = 0;
+        if (lane == 0) last = tagged_count_last(&p.split_cnt[unit * 4 + q], split_tag, (unsigned)p.splits1);
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (last < 0) {
+          ok = false;
+          break;
+        }
+        if (last && feat_ok) {
+          __threadfence();
+          for (int t = 0; t < p.T; ++t) {
+            float gp[kDecodeMaxSplits], up[kDecodeMaxSplits];
+#pragma unroll
+            for (int ss = 0; ss < kDecodeMaxSplits; ++ss) {  // every split's loads in flight at once
+              gp[ss] = 0.f;
+              up[ss] = 0.f;
+              if (ss < p.splits1) {
+                const float* src = slot0 + ss * kSplit + fit * kDecodeMaxTokens + t;
+                gp[ss] = __ldcg(src);
+                up[ss] = __ldcg(src + SW_FEAT * kDecodeMaxTokens);
+              }
+            }
+            float gs = 0.f, us = 0.f;
+#pragma unroll
+            for (int ss = 0; ss < kDecodeMaxSplits; ++ss) {  // added in split order
+              gs += gp[ss];
+              us += up[ss];
+            }
+            store1_out(p.h, p.dtype, ((int64_t)m * kDecodeMaxTokens + t) * p.I + feat, silu_mul(gs, us));
+          }
+        }
+      } else if (feat_ok) {
 #pragma unroll
         for (int t = 0; t < kDecodeMaxTokens; ++t)
           if (t < p.T)
@@ -482,41 +539,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     __threadfence();
     ptx::mbar_arrive(epi_done);
     if (!wait_pass()) ok = false;
-    if (ok && p.splits1 > 1) {
-      if (ok) {
-        __threadfence();
-        // add the K splits' partial sums in split order and apply SwiGLU;
-        // element (m, t, i) of h over all CTAs' epilogue threads
-        const int64_t n = (int64_t)A * p.T * p.I;
-        for (int64_t idx = (int64_t)blockIdx.x * 128 + et; idx < n; idx += (int64_t)gridDim.x * 128) {
-          const int m = (int)(idx / ((int64_t)p.T * p.I));
-          const int t = (int)((idx / p.I) % p.T);
-          const int i = (int)(idx % p.I);
-          const float* base = p.partial + (size_t)(m * p.nf1 + i / SW_FEAT) * p.splits1 * 2 * SW_FEAT * kDecodeMaxTokens +
-                              (i % SW_FEAT) * kDecodeMaxTokens + t;
-          float gp[kDecodeMaxSplits], up[kDecodeMaxSplits];
-#pragma unroll
-          for (int s = 0; s < kDecodeMaxSplits; ++s) {  // every split's loads in flight at once
-            gp[s] = 0.f;
-            up[s] = 0.f;
-            if (s < p.splits1) {
-              gp[s] = __ldcg(base + (size_t)s * 2 * SW_FEAT * kDecodeMaxTokens);
-              up[s] = __ldcg(base + (size_t)s * 2 * SW_FEAT * kDecodeMaxTokens + SW_FEAT * kDecodeMaxTokens);
-            }
-          }
-          float gs = 0.f, us = 0.f;
-#pragma unroll
-          for (int s = 0; s < kDecodeMaxSplits; ++s) {  // added in split order
-            gs += gp[s];
-            us += up[s];
-          }
-          store1_out(p.h, p.dtype, ((int64_t)m * kDecodeMaxTokens + t) * p.I + i, silu_mul(gs, us));
-        }
-      }
-      __threadfence();
-      ptx::mbar_arrive(epi_done);
-      if (!wait_pass()) ok = false;
-    }
     // phase 2: weighted adds into the fp32 accumulator
     for (int i2 = blockIdx.x; ok && i2 < items2; i2 += gridDim.x, ++it) {
       const int m = i2 / p.nf2, f = i2 % p.nf2;
@@ -585,7 +607,7 @@ constexpr size_t kDecodeSmem = 1024 + (size_t)DK_STAGES * DK_STAGE + 256 + 4 * k
 
 struct DecodeWs {
   int max_tiles, nf1, nf2, kb1, kb2, splits1;
-  size_t h, partial, y32, conv_cnt, bytes;
+  size_t h, partial, split_cnt, y32, conv_cnt, bytes;
 };
 
 DecodeWs decode_ws(int64_t T, int k, int E, int64_t H, int64_t I, int dtype) {
@@ -608,6 +630,7 @@ DecodeWs decode_ws(int64_t T, int k, int E, int64_t H, int64_t I, int dtype) {
   };
   w.h = take((size_t)w.max_tiles * kDecodeMaxTokens * I * es);
   w.partial = take(w.splits1 > 1 ? (size_t)units1 * w.splits1 * 2 * SW_FEAT * kDecodeMaxTokens * 4 : 0);
+  w.split_cnt = take(w.splits1 > 1 ? (size_t)units1 * 4 * sizeof(unsigned long long) : 0);
   w.y32 = take((size_t)T * H * 4);
   w.conv_cnt = take((size_t)T * w.nf2 * 4 * sizeof(int32_t));
   w.bytes = off;
@@ -659,6 +682,7 @@ int decode_fused(const void* x, int dtype, int64_t T, int64_t H, const void* w13
   p.wts = topk_weights;
   p.h = ws + w.h;
   p.partial = reinterpret_cast<float*>(ws + w.partial);
+  p.split_cnt = reinterpret_cast<unsigned long long*>(ws + w.split_cnt);
   p.y32 = reinterpret_cast<float*>(ws + w.y32);
   p.conv_cnt = reinterpret_cast<int32_t*>(ws + w.conv_cnt);
   p.y = y;
