@@ -459,11 +459,19 @@ def int8_yardstick(ctx):
         return {"tops": None, "error": str(exc)[:200]}
 
 
-def gate_up_roofline(cfg, T, world, id_sets, gemm1_ms, peaks, int8, sustained):
+def one_launch(kernel_clocks):
+    """True when the step ran as the one-launch decode kernel: its clock is
+    the gate_up class and no down GEMM launched."""
+    return kernel_clocks["down"]["launches"] == 0 and kernel_clocks["gate_up"]["launches"] > 0
+
+
+def gate_up_roofline(cfg, T, world, id_sets, gemm1_ms, peaks, int8, sustained, whole_layer=False):
     """Algorithmic work of one gate_up launch and its achieved rate: FLOPs
     2 * S * H * 2I (S routed slots), bytes = w13 of the experts with slots +
     the padded activation rows read + the h rows written; bound = the larger
-    of FLOPs / tensor peak and bytes / HBM peak (the measured peaks)."""
+    of FLOPs / tensor peak and bytes / HBM peak (the measured peaks).
+    whole_layer: the launch is the one-launch decode kernel, whose work is the
+    whole layer: w13 + w2 of the active experts, x read, y written."""
     H, I, E, k = cfg["H"], cfg["I"], cfg["E"], cfg["k"]
     wb = 1 if cfg["quant"] else (4 if cfg["dtype"] == "fp32" else 2)
     hb = 4 if cfg["dtype"] == "fp32" else 2
@@ -480,6 +488,9 @@ def gate_up_roofline(cfg, T, world, id_sets, gemm1_ms, peaks, int8, sustained):
         rows_pad = S + active * 64
     flops = 2.0 * S * H * 2 * I
     nbytes = active * 2.0 * I * H * wb + rows_pad * H * wb + rows_pad * I * hb
+    if whole_layer:
+        flops = 2.0 * S * H * 3 * I
+        nbytes = active * 3.0 * I * H * wb + 2.0 * T * H * hb
     if cfg["quant"]:
         if int8 and int8.get("tops"):
             tc_peak, tc_src = int8["tops"], "measured int8 GEMM (%s)" % int8["how"]
@@ -491,7 +502,9 @@ def gate_up_roofline(cfg, T, world, id_sets, gemm1_ms, peaks, int8, sustained):
     s = gemm1_ms / 1e3
     tensor_rate, hbm_rate = flops / s / 1e12, nbytes / s / 1e9
     tensor_bound = flops / (tc_peak * 1e12) >= nbytes / (peaks["hbm"] * 1e9)
-    r = {"kernel": "moe_gemm_kernel<SWIGLU> (gate_up GEMM + SwiGLU)", "bound": "tensor" if tensor_bound else "hbm",
+    kname = ("moe_decode_kernel (whole layer: routing, gate_up + SwiGLU, down + combine)" if whole_layer
+             else "moe_gemm_kernel<SWIGLU> (gate_up GEMM + SwiGLU)")
+    r = {"kernel": kname, "bound": "tensor" if tensor_bound else "hbm",
          "flops_per_launch": flops, "bytes_per_launch": nbytes, "active_experts": active,
          "ms_per_launch": gemm1_ms, "frac_tensor": tensor_rate / tc_peak, "frac_hbm": hbm_rate / peaks["hbm"]}
     if tensor_bound:
@@ -617,7 +630,7 @@ def run_config(ctx, name, T, args, peaks, int8, weights=None, steps=None, warmup
     r = timed_region(ctx, w, steps, kernels_per_step=w["kernels"])
     ids_sets = [v[1].cpu().numpy() for v in w["variants"]]
     roof = gate_up_roofline(cfg, T, ctx.world, ids_sets, r["kernel_clocks"]["gate_up"]["ms_per_launch"], peaks,
-                            int8, sustained=False)
+                            int8, sustained=False, whole_layer=one_launch(r["kernel_clocks"]))
     out = {"workload": cfg["desc"].split(" (")[0] + f" T={T}" + ("" if ctx.world == 1 else f" per GPU x {ctx.world}"),
            "tokens_per_gpu": T, "hidden": cfg["H"], "inter": cfg["I"], "experts": cfg["E"], "top_k": cfg["k"],
            "routing": cfg["routing"], "dtype": cfg["dtype"] + ("+w8a8" if cfg["quant"] else ""),
@@ -910,7 +923,8 @@ def main():
         n_sus = max(args.steps, int(math.ceil(args.sustain_s * 1e3 / ms)))
         sreg = timed_region(ctx, w, n_sus, kernels_per_step=w["kernels"])
         sroof = gate_up_roofline(cfg, T, world, [v[1].cpu().numpy() for v in w["variants"]],
-                                 sreg["kernel_clocks"]["gate_up"]["ms_per_launch"], peaks, None, sustained=True)
+                                 sreg["kernel_clocks"]["gate_up"]["ms_per_launch"], peaks, None, sustained=True,
+                                 whole_layer=one_launch(sreg["kernel_clocks"]))
         sustained = {"value": world * T / (sreg["ms"] / 1e3), "unit": "tokens/s", "ms_per_step": sreg["ms"],
                      "steps": n_sus, "seconds": sreg["seconds"], "clocks": sreg["clocks"],
                      "kernel_clocks": sreg["kernel_clocks"],
@@ -930,7 +944,8 @@ def main():
     int8 = int8_yardstick(ctx) if (world == 1 and (cfg["quant"] or not args.no_configs)) else None
     id_sets = [v[1].cpu().numpy() for v in w["variants"]]
     region_s = ms * args.steps / 1e3
-    roofline = gate_up_roofline(cfg, T, world, id_sets, gemm1_ms, peaks, int8, sustained=region_s >= 1.0)
+    roofline = gate_up_roofline(cfg, T, world, id_sets, gemm1_ms, peaks, int8, sustained=region_s >= 1.0,
+                                whole_layer=one_launch(reg["kernel_clocks"]))
     roofline["ms_per_launch_source"] = ("library kernel clocks (device global timer, first CTA past its wait on "
                                         "the previous kernel to last CTA end) over the timed region, "
                                         f"{reg['kernel_clocks']['gate_up']['launches']} launches")
@@ -939,7 +954,8 @@ def main():
         roofline["ms_per_launch_events"] = stage["gemm1"]
     roofline["traffic"] = load_traffic(args.config) if not args.tokens and world == 1 else None
     roofline["traffic_unit"] = "bytes"
-    if world == 1 and not cfg["quant"] and cfg["dtype"] == "bf16" and not cfg.get("prerouted"):
+    if (world == 1 and not cfg["quant"] and cfg["dtype"] == "bf16" and not cfg.get("prerouted")
+            and not one_launch(reg["kernel_clocks"])):
         roofline.update(cublas_yardsticks(ctx, cfg, T * k, gemm1_ms, args.steps))
     flops_step = 6.0 * T * k * H * I
     peak_tc = roofline["peak"] if roofline["bound"] == "tensor" else peaks["bf16"]

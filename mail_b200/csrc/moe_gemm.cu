@@ -50,6 +50,8 @@ constexpr int MAX_GEMM_EXPERTS = 1024;
 constexpr int STAGE_ROW_BYTES = 144;       // 128 B of a row + 16 B pad (conflict-free)
 constexpr int STAGE_WARP_BYTES = 32 * STAGE_ROW_BYTES;
 constexpr int EPI_STAGE_BYTES = 4 * STAGE_WARP_BYTES;  // one area per epilogue warp (down GEMM)
+constexpr int kEpiScaleCols = 256;                     // int8 column scales of one N tile
+constexpr int EPI_SCALE_BYTES = 4 * 2 * kEpiScaleCols * 4;  // int8: two tiles' scales per epilogue warp
 
 __device__ __forceinline__ void raise_device_error(int code) { atomicCAS(&g_moe_device_error, 0, code); }
 
@@ -142,7 +144,19 @@ __device__ __forceinline__ void decode_unit(int t, const int32_t* s_u, int E, in
 
 __host__ __device__ constexpr int align_up16(int v) { return (v + 15) & ~15; }
 
-__device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.0f + __expf(-g)) * u; }
+// silu(g) * u with the fast divide: for g below about -87, 1 + exp(-g)
+// overflows and the quotient is 0, the limit of silu there.
+__device__ __forceinline__ float silu_mul(float g, float u) { return __fdividef(g, 1.0f + __expf(-g)) * u; }
+
+// What the epilogue needs to drain one tile, fetched one tile ahead.
+struct EpiMeta {
+  bool live, valid, half, row_ok;
+  int e, n, m, r;  // unit's expert, N tile, this CTA's M tile; this thread's row in the tile
+  int32_t rstart, rcount, slot;
+  int64_t grow;
+  float sa, wgt;   // int8 row scale, routing weight
+  float sc[8];     // int8: this lane's 8 of the N tile's column scales
+};
 
 // Stores 8 consecutive fp32 values as the output dtype (16- or 32-byte store).
 __device__ __forceinline__ void store8_out(void* base, int dtype, int64_t idx, const float* v) {
@@ -256,6 +270,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   int32_t* s_cum = reinterpret_cast<int32_t*>(smem + S * C::kStageBytes + BAR_BYTES);
   int32_t* s_ucum = PAIR ? s_cum + (p.E + 1) : s_cum;  // scheduling-unit prefix per expert
   uint8_t* epi_stage = smem + S * C::kStageBytes + BAR_BYTES + align_up16(2 * (p.E + 1) * 4);
+  uint8_t* epi_scales = epi_stage + EPI_STAGE_BYTES;  // int8 kinds only
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -497,14 +512,74 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const int q = warp & 3;          // TMEM lane quarter this warp may access
     const uint32_t tempty_leader[2] = {PAIR ? ptx::mapa(ptx::smem_u32(&tempty[0]), 0) : ptx::smem_u32(&tempty[0]),
                                        PAIR ? ptx::mapa(ptx::smem_u32(&tempty[1]), 0) : ptx::smem_u32(&tempty[1])};
+    // The facts of the tile after the current one are fetched while the
+    // current one drains, so their global-memory latency stays off the
+    // drain: its tile row range and (int8) its 256 column scales as soon as
+    // the tile is known, this thread's row scale / routed slot after the
+    // first chunk, the slot's routing weight after the second. The column
+    // scales go to this warp's shared-memory buffer (two, alternating).
+    float* const s_scales = reinterpret_cast<float*>(epi_scales) + (warp - 2) * 2 * kEpiScaleCols;
+    EpiMeta cur, nxt;
+    auto fetch_tile = [&](EpiMeta& mt, int tt) {
+      locate(tt, mt.e, mt.n, mt.m, mt.valid, mt.half);
+      mt.r = mt.half ? (int)rank * (BM / 2) + (q & 1) * 32 + lane : q * 32 + lane;
+      mt.rstart = mt.valid ? row_start_tab[mt.m] : 0;
+      mt.rcount = mt.valid ? row_count_tab[mt.m] : 0;
+      if constexpr (KIND == 2) {
+        const int64_t wrow = (int64_t)mt.e * p.b_rows_per_expert;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int idx = lane + 32 * i;
+          int64_t src;
+          if constexpr (SWIGLU)  // [0, 128): gate scales of the tile's features, [128, 256): up scales
+            src = wrow + (idx >= 128 ? p.inter : 0) + min(mt.n * (BN / 2) + (idx & 127), p.n_valid - 1);
+          else
+            src = wrow + min(mt.n * BN + idx, p.n_valid - 1);
+          mt.sc[i] = p.b_scale[src];
+        }
+      }
+    };
+    auto fetch_rows = [&](EpiMeta& mt) {
+      mt.grow = (int64_t)mt.rstart + mt.r;
+      mt.row_ok = (mt.r < mt.rcount) && (mt.grow < p.a_rows);
+      mt.sa = 1.f;
+      if constexpr (KIND == 2) mt.sa = mt.row_ok ? p.a_scale[mt.grow] : 0.f;
+      mt.slot = (!SWIGLU && p.epi != MOE_EPI_STORE_ROWS && mt.row_ok) ? p.row_map[mt.grow] : -1;
+    };
+    auto fetch_weight = [&](EpiMeta& mt) {
+      mt.wgt = (!SWIGLU && p.epi != MOE_EPI_STORE_ROWS && p.epi != kEpiScatterPeer && mt.slot >= 0 && p.row_weight)
+                   ? p.row_weight[mt.slot]
+                   : 1.f;
+    };
+    auto stage_scales = [&](const EpiMeta& mt, int buf) {
+      if constexpr (KIND == 2) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) s_scales[buf * kEpiScaleCols + lane + 32 * i] = mt.sc[i];
+        __syncwarp();
+      }
+    };
+
     int it = 0;
     bool ok = true;
     SegIter seg(p.stream_k != 0, unit0, ustride, total, p.num_kb);
     int t, kb_begin, kb_end;
-    for (; seg.next(t, kb_begin, kb_end); ++it) {
-      int e, n, m;
-      bool valid, half;
-      locate(t, e, n, m, valid, half);
+    cur.live = seg.next(t, kb_begin, kb_end);
+    if (cur.live) {
+      fetch_tile(cur, t);
+      fetch_rows(cur);
+      fetch_weight(cur);
+      stage_scales(cur, 0);
+    }
+    for (; cur.live; ++it) {
+      nxt.live = seg.next(t, kb_begin, kb_end);
+      if (nxt.live) fetch_tile(nxt, t);
+      // after chunk c of this tile: the next tile's dependent loads
+      auto chunk_done = [&](int c) {
+        if (nxt.live) {
+          if (c == 0) fetch_rows(nxt);
+          else if (c == 1) fetch_weight(nxt);
+        }
+      };
       const int acc = it & 1;
       const uint32_t acc_par = (it >> 1) & 1;
       bool w_ok = ptx::mbar_wait(&tfull[acc], acc_par, abort_flag);
@@ -513,25 +588,24 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         break;
       }
       ptx::tc_fence_after();
-      const int32_t rstart = valid ? row_start_tab[m] : 0;
-      const int32_t rcount = valid ? row_count_tab[m] : 0;
-      // tile row of this thread, and the first accumulator column it holds
-      // (TMEM column 0 of its lane) relative to the unit's N tile
-      const int r = half ? (int)rank * (BM / 2) + (q & 1) * 32 + lane : q * 32 + lane;
-      const int64_t grow = (int64_t)rstart + r;
-      const bool row_ok = (r < rcount) && (grow < p.a_rows);
+      const int n = cur.n;
+      const bool half = cur.half;
+      const int64_t grow = cur.grow;
+      const bool row_ok = cur.row_ok;
+      const float sa = cur.sa;
+      const float* sc = s_scales + (it & 1) * kEpiScaleCols;  // this tile's column scales (int8)
+      // TMEM column 0 of this thread's lane; the row and first column it
+      // holds relative to the unit's N tile follow from the lane quarter
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
-      float sa = 1.f;
-      if constexpr (KIND == 2) sa = row_ok ? p.a_scale[grow] : 0.f;
 
       if constexpr (SWIGLU) {
-        const int64_t wrow = (int64_t)e * p.b_rows_per_expert;
         // whole unit: gate at TMEM columns [0, 128), up at [128, 256), 128
         // features; half unit: this lane's 64 features, gate at [0, 64), up
         // at [64, 128)
         const int nchunk = half ? 2 : 4;
         const int up_col = half ? BN / 4 : BN / 2;
-        const int cbase = n * (BN / 2) + (half ? (q >> 1) * (BN / 4) : 0);
+        const int lbase = half ? (q >> 1) * (BN / 4) : 0;  // first feature of this lane within the N tile
+        const int cbase = n * (BN / 2) + lbase;
 #pragma unroll 1
         for (int c = 0; c < nchunk; ++c) {
           uint32_t g[32], u[32];
@@ -544,14 +618,22 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             for (int j = 0; j < 4; ++j) {
               const int cj = col0 + 8 * j;
               if (cj < p.n_valid) {
+                float gs[8], us[8];
+                if constexpr (KIND == 2) {
+                  const int l = lbase + c * 32 + 8 * j;  // feature within the N tile
+                  *reinterpret_cast<float4*>(gs) = *reinterpret_cast<const float4*>(sc + l);
+                  *reinterpret_cast<float4*>(gs + 4) = *reinterpret_cast<const float4*>(sc + l + 4);
+                  *reinterpret_cast<float4*>(us) = *reinterpret_cast<const float4*>(sc + 128 + l);
+                  *reinterpret_cast<float4*>(us + 4) = *reinterpret_cast<const float4*>(sc + 128 + l + 4);
+                }
                 float h[8];
 #pragma unroll
                 for (int i = 0; i < 8; ++i) {
                   float gv = acc_value<KIND>(g[8 * j + i]);
                   float uv = acc_value<KIND>(u[8 * j + i]);
                   if constexpr (KIND == 2) {
-                    gv = gv * sa * p.b_scale[wrow + cj + i];
-                    uv = uv * sa * p.b_scale[wrow + p.inter + cj + i];
+                    gv = gv * sa * gs[i];
+                    uv = uv * sa * us[i];
                   }
                   h[i] = silu_mul(gv, uv);
                 }
@@ -559,14 +641,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
               }
             }
           }
+          chunk_done(c);
         }
       } else {
         int64_t dst_row = grow;
-        float wgt = 1.f;
+        const float wgt = cur.wgt;
         bool do_store = row_ok;
         void* obase = p.out;
         if (p.epi != MOE_EPI_STORE_ROWS && row_ok) {
-          const int32_t slot = p.row_map[grow];
+          const int32_t slot = cur.slot;
           do_store = slot >= 0;
           if (slot >= 0) {
             if (p.epi == kEpiScatterPeer) {
@@ -576,16 +659,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
               else do_store = false;
             } else {
               dst_row = (p.epi == MOE_EPI_COMBINE_ADD) ? (int64_t)(slot / p.top_k) : (int64_t)slot;
-              if (p.row_weight) wgt = p.row_weight[slot];
             }
           }
         }
         if (dst_row >= p.out_rows) do_store = false;
-        const int64_t wrow = (int64_t)e * p.b_rows_per_expert;
         // whole unit: N tile columns [0, 256) at TMEM columns [0, 256); half
         // unit: this lane's half of the N tile at TMEM columns [0, 128)
         const int ncols = half ? BN / 2 : BN;
-        const int cbase = n * BN + (half ? (q >> 1) * (BN / 2) : 0);
+        const int lbase = half ? (q >> 1) * (BN / 2) : 0;  // first column of this lane within the N tile
+        const int cbase = n * BN + lbase;
         if (p.out_dtype != MOE_F32 && p.epi != MOE_EPI_COMBINE_ADD) {
           uint8_t* stage = epi_stage + (warp - 2) * STAGE_WARP_BYTES;
 #pragma unroll 1
@@ -597,16 +679,22 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             const int col0 = cbase + c2 * 64;
             uint32_t packed[32];
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              const uint32_t* src = i < 16 ? v0 : v1;
-              const int li = (i & 15) * 2;
-              float a = acc_value<KIND>(src[li]), b = acc_value<KIND>(src[li + 1]);
-              if constexpr (KIND == 2) {
-                const int ca = min(col0 + 2 * i, p.n_valid - 1), cb = min(col0 + 2 * i + 1, p.n_valid - 1);
-                a = a * sa * p.b_scale[wrow + ca];
-                b = b * sa * p.b_scale[wrow + cb];
+            for (int i4 = 0; i4 < 16; ++i4) {
+              float s4[4] = {1.f, 1.f, 1.f, 1.f};
+              if constexpr (KIND == 2)
+                *reinterpret_cast<float4*>(s4) = *reinterpret_cast<const float4*>(sc + lbase + c2 * 64 + 4 * i4);
+#pragma unroll
+              for (int h2 = 0; h2 < 2; ++h2) {
+                const int i = 2 * i4 + h2;  // packed pair: columns col0 + 2i, col0 + 2i + 1
+                const uint32_t* src = i < 16 ? v0 : v1;
+                const int li = (i & 15) * 2;
+                float a = acc_value<KIND>(src[li]), b = acc_value<KIND>(src[li + 1]);
+                if constexpr (KIND == 2) {
+                  a = a * sa * s4[2 * h2];
+                  b = b * sa * s4[2 * h2 + 1];
+                }
+                packed[i] = pack2(a * wgt, b * wgt, p.out_dtype);
               }
-              packed[i] = pack2(a * wgt, b * wgt, p.out_dtype);
             }
             const int nvalid = min(64, p.n_valid - col0);
             const unsigned long long rp =
@@ -614,42 +702,54 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                                                                                (dst_row * p.ldo + col0) * 2)
                                          : 0ull;
             staged_store<8>(stage, packed, rp, nvalid > 0 ? nvalid * 2 : 0, lane);
+            chunk_done(c2);
           }
         } else {
 #pragma unroll 1
-        for (int c = 0; c < ncols / 32; ++c) {
-          uint32_t v[32];
-          ptx::tmem_ld32(tbase + c * 32, v);
-          ptx::tmem_ld_wait();
-          const int col0 = cbase + c * 32;
-          if (do_store && col0 < p.n_valid) {
+          for (int c = 0; c < ncols / 32; ++c) {
+            uint32_t v[32];
+            ptx::tmem_ld32(tbase + c * 32, v);
+            ptx::tmem_ld_wait();
+            const int col0 = cbase + c * 32;
+            if (do_store && col0 < p.n_valid) {
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const int cj = col0 + 8 * j;
-              if (cj < p.n_valid) {
-                float f[8];
+              for (int j = 0; j < 4; ++j) {
+                const int cj = col0 + 8 * j;
+                if (cj < p.n_valid) {
+                  float s8[8] = {1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f};
+                  if constexpr (KIND == 2) {
+                    const int l = lbase + c * 32 + 8 * j;
+                    *reinterpret_cast<float4*>(s8) = *reinterpret_cast<const float4*>(sc + l);
+                    *reinterpret_cast<float4*>(s8 + 4) = *reinterpret_cast<const float4*>(sc + l + 4);
+                  }
+                  float f[8];
 #pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                  float x = acc_value<KIND>(v[8 * j + i]);
-                  if constexpr (KIND == 2) x = x * sa * p.b_scale[wrow + cj + i];
-                  f[i] = x * wgt;
-                }
-                if (p.epi == MOE_EPI_COMBINE_ADD) {
-                  float* dst = static_cast<float*>(p.out) + dst_row * p.ldo + cj;
-                  red_add4(dst, f[0], f[1], f[2], f[3]);
-                  red_add4(dst + 4, f[4], f[5], f[6], f[7]);
-                } else {
-                  store8_out(obase, p.out_dtype, dst_row * p.ldo + cj, f);
+                  for (int i = 0; i < 8; ++i) {
+                    float x = acc_value<KIND>(v[8 * j + i]);
+                    if constexpr (KIND == 2) x = x * sa * s8[i];
+                    f[i] = x * wgt;
+                  }
+                  if (p.epi == MOE_EPI_COMBINE_ADD) {
+                    float* dst = static_cast<float*>(p.out) + dst_row * p.ldo + cj;
+                    red_add4(dst, f[0], f[1], f[2], f[3]);
+                    red_add4(dst + 4, f[4], f[5], f[6], f[7]);
+                  } else {
+                    store8_out(obase, p.out_dtype, dst_row * p.ldo + cj, f);
+                  }
                 }
               }
             }
+            chunk_done(c);
           }
         }
-        }
       }
+      // the next tile's column scales into the other buffer (its loads were
+      // issued before this tile drained)
+      if (nxt.live) stage_scales(nxt, (it + 1) & 1);
       ptx::tc_fence_before();
       if constexpr (PAIR) ptx::mbar_arrive_cluster(tempty_leader[acc]);
       else ptx::mbar_arrive(&tempty[acc]);
+      cur = nxt;
     }
     if (!ok) {
       if (lane == 0) raise_device_error(3);
@@ -778,15 +878,15 @@ bool use_pair(int64_t max_tiles, int E, int64_t n_tiles) {
 }
 
 template <bool PAIR>
-size_t gemm_smem_bytes(int E) {
+size_t gemm_smem_bytes(int E, bool int8_scales) {
   return 1024 + (size_t)Cfg<PAIR>::kStages * Cfg<PAIR>::kStageBytes + BAR_BYTES + align_up16(2 * (E + 1) * 4) +
-         EPI_STAGE_BYTES;
+         EPI_STAGE_BYTES + (int8_scales ? EPI_SCALE_BYTES : 0);
 }
 
 template <int KIND, bool SWIGLU, bool PAIR>
 int launch_kind(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& ta64, const CUtensorMap& tb64,
                 const Params& p, int64_t units_ub, cudaStream_t st) {
-  const size_t smem = gemm_smem_bytes<PAIR>(p.E);
+  const size_t smem = gemm_smem_bytes<PAIR>(p.E, KIND == 2);
   auto kfn = moe_gemm_kernel<KIND, SWIGLU, PAIR>;
   MOE_CUDA_TRY(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   cudaLaunchConfig_t cfg = {};
