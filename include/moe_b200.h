@@ -84,8 +84,9 @@ MOE_API int moe_version(void);
 MOE_API const char* moe_last_error(void);
 /* Copies the device error flag (0 = none, else a code identifying the stalled
  * pipeline role: 1 TMA producer, 2 MMA issuer, 3 epilogue, 4 drain,
- * 6 self-test, 7 device-wide barrier of the one-launch decode kernel) into
- * *host_code and clears it (after code 7 it also re-arms that barrier).
+ * 6 self-test, 7 cross-CTA wait of the one-launch decode kernel) into
+ * *host_code and clears it (after any error it also resets that kernel's
+ * launch counter).
  * Synchronises `stream`. */
 MOE_API int moe_get_device_error(int* host_code, void* stream);
 /* Self-test of the bounded waits: one CTA waits on an mbarrier that nothing
@@ -126,10 +127,10 @@ typedef enum {
                                band as the gate_up GEMM */
   MOE_OPT_DECODE_FUSED = 9    /* 1 (default): moe_fused_experts runs a batch of at most 16 tokens and 128 routed
                                slots (bf16/fp16, no int8) as one persistent kernel — routing, gate_up GEMM +
-                               SwiGLU, down GEMM + combine and output conversion as phases separated by
-                               device-wide barriers. Its barrier lives in the library's device memory, so
-                               two such calls must not run concurrently on one GPU (different streams);
-                               callers that overlap MoE calls on several streams set 0 */
+                               SwiGLU, down GEMM + combine and output conversion as phases whose CTAs
+                               hand results on through counters. Its launch counter lives in the library's
+                               device memory, so two such calls must not run concurrently on one GPU
+                               (different streams); callers that overlap MoE calls on several streams set 0 */
 } moe_option_t;
 MOE_API int moe_set_option(int option, int value);
 /* Current value of an option, or -1 for an unknown option. */

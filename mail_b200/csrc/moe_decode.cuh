@@ -4,14 +4,15 @@
 // clocks, tensor maps, PTX wrappers). For at most kDecodeMaxTokens tokens
 // (the MMA's N = 16) and kDecodeMaxSlots routed slots, the layer's stages —
 // routing align, gate_up GEMM + SwiGLU, down GEMM + weighted combine, output
-// conversion — run as phases of one persistent kernel, one CTA per SM,
-// separated by device-wide barriers:
+// conversion — run as phases of one persistent kernel, one CTA per SM:
 //
 //   phase 0  every CTA reads the top-k ids and weights (at most 128 slots)
 //            and derives the active experts (distinct valid ids in increasing
 //            order; expert tile m = the m-th of them) and, per (tile, token),
-//            the token's summed routing weight for that expert; the fp32
-//            output accumulator is cleared
+//            the token's summed routing weight for that expert; its share of
+//            the fp32 output accumulator, the group counts and the readiness
+//            counts is cleared, then the CTA arrives on the launch counter
+//            (nothing waits there)
 //   phase 1  gate_up work items (tile m, 128-feature tile f, K split s):
 //            weights as the MMA's 128-row operand (gate and up rows, two
 //            accumulators), the N = 16 operand is x itself — the first 16 rows
@@ -20,28 +21,38 @@
 //            routed to the expert are computed and never used); with K split,
 //            each split stores fp32 partial sums and the last split of a unit
 //            to finish (a count per epilogue warp) adds them in split order and
-//            applies SwiGLU
-//   barrier
-//   phase 2  down work items (tile m, 128-output-feature tile): the N operand
-//            is h[m] (16 rows), the epilogue adds weight(m, t) * acc into the
-//            fp32 accumulator row of token t, then counts the add per (token,
+//            applies SwiGLU. Each warp that stores its 32 features of tile m
+//            adds one to tile m's readiness count (one atomic: its waiters
+//            and adders first check that every CTA has arrived on the launch
+//            counter, long true by then, so the count was cleared)
+//   phase 2  down work items (tile m, 128-output-feature tile): the producer
+//            loads the item's weights at once and h[m] (16 rows) once tile m's
+//            readiness count is full — no device-wide barrier, so the down
+//            phase of one expert overlaps the gate_up phase of others; the
+//            epilogue, once every CTA has arrived on the launch counter (its
+//            clears are done), adds weight(m, t) * acc into the fp32
+//            accumulator row of token t, then counts the add per (token,
 //            32-feature group); the warp whose add completes a group (its
 //            token's distinct experts all added) converts it to the output
-//            dtype — no barrier after phase 2. The counts and the accumulator
-//            are cleared in phase 0: nothing touches them before the barrier
+//            dtype
 //
 // The producer starts loading its first phase-2 weight tiles as soon as ring
-// stages free up after its last phase-1 stage, before the barrier (the
-// weights do not depend on h); only the h rows wait for the barrier. At one
-// token a phase-2 item's weights (128 rows x I) fit in the ring, so the down
-// projection's weight stream overlaps the gate_up phase's tail.
+// stages free up after its last phase-1 stage (the weights do not depend on
+// h); only the h rows wait. At one token a phase-2 item's weights (128 rows x
+// I) fit in the ring, so the down projection's weight stream overlaps the
+// gate_up phase's tail.
 //
-// Device-wide barrier: a count and a generation word in static device memory,
-// self-resetting (the last CTA to arrive clears the count and advances the
-// generation). All CTAs are resident at once (grid <= SM count, one CTA per
-// SM by its shared memory). Every wait is bounded; a barrier that times out
-// latches device error 7, and moe_get_device_error() also resets the barrier.
-// Two such launches must not overlap on one GPU (different streams).
+// Cross-CTA state: a count and a generation word in static device memory
+// (the launch counter: the last CTA to arrive clears the count and advances
+// the generation, which every CTA read before arriving — the tag of this
+// launch), tagged count words in the workspace for the K splits (a word
+// left by an earlier launch carries another tag and counts as zero, so
+// nothing clears them) and the cleared readiness counts. All CTAs are resident at once (grid <= SM
+// count, one CTA per SM by its shared memory), and no CTA's phase-1 work
+// waits on another CTA. Every wait is bounded; a cross-CTA wait that times
+// out latches device error 7, and moe_get_device_error() resets the launch
+// counter after any error. Two such launches must not overlap on one GPU
+// (different streams).
 namespace moe {
 namespace {
 
@@ -57,18 +68,23 @@ constexpr int DK_TMEM_COLS = 64;                           // 2 buffers x (gate 
 __device__ unsigned int g_decode_bar_count = 0;
 __device__ unsigned int g_decode_bar_gen = 0;
 
-// Device-wide barrier (one thread per CTA). Returns false after the time
-// limit or when *abort is raised.
-__device__ bool decode_grid_barrier(unsigned int nblocks, volatile int* abort) {
-  volatile unsigned int* gen_p = &g_decode_bar_gen;
-  const unsigned int gen = *gen_p;
+// Launch counter (one thread per CTA, after the CTA's phase-0 clears):
+// the last CTA to arrive resets the count and advances the generation, so
+// the generation a CTA reads before arriving is the same for every CTA of
+// the launch and differs from launch to launch. Nothing waits here.
+__device__ void decode_launch_arrive(unsigned int nblocks) {
   __threadfence();
   if (atomicAdd(&g_decode_bar_count, 1u) == nblocks - 1u) {
     atomicExch(&g_decode_bar_count, 0u);
     __threadfence();
     atomicAdd(&g_decode_bar_gen, 1u);
-    return true;
   }
+}
+
+// Waits until every CTA of the launch has arrived (the generation moved on
+// from `gen`). Returns false after the time limit or when *abort is raised.
+__device__ bool decode_all_arrived(unsigned int gen, volatile int* abort) {
+  volatile unsigned int* gen_p = &g_decode_bar_gen;
   const uint64_t t0 = ptx::globaltimer();
   while (*gen_p == gen) {
     if (*abort) return false;
@@ -96,6 +112,20 @@ __device__ __forceinline__ int tagged_count_last(unsigned long long* ctr, unsign
   return -1;
 }
 
+// Waits until a count word holds at least `total`. Returns false after the
+// time limit or when *abort is raised.
+__device__ bool wait_count(const unsigned int* ctr, unsigned int total, volatile int* abort) {
+  const volatile unsigned int* v = ctr;
+  const uint64_t t0 = ptx::globaltimer();
+  while (*v < total) {
+    if (*abort) return false;
+    if (ptx::globaltimer() - t0 > MOE_WAIT_TIMEOUT_NS) return false;
+    __nanosleep(32);
+  }
+  __threadfence();
+  return true;
+}
+
 __device__ __forceinline__ void fence_proxy_async_global() {
   asm volatile("fence.proxy.async.global;" ::: "memory");
 }
@@ -112,6 +142,7 @@ struct DecodeParams {
   void* h;               // [max_tiles][16][I], x dtype
   float* partial;        // splits1 > 1: [max_tiles * nf1][splits1][2][128][16]
   unsigned long long* split_cnt;  // splits1 > 1: [max_tiles * nf1][4] tagged counts (never cleared)
+  unsigned int* h_ready;          // [max_tiles] finished (feature tile, warp) groups of h, cleared in phase 0
   float* y32;            // [T, H]
   int32_t* conv_cnt;     // [T][nf2 * 4] adds per (token, 32-feature group)
   void* y;               // [T, H], x dtype
@@ -132,11 +163,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   uint64_t* tfull = empty + DK_STAGES;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
-  uint64_t* epi_done = drain + 1;   // epilogue warps: a phase's global stores are done
-  uint64_t* grid_pass = epi_done + 1;  // producer: the device-wide barrier was passed
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(grid_pass + 1);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  int* s_A = reinterpret_cast<int*>(tmem_slot + 2);  // number of active experts
+  int* s_A = reinterpret_cast<int*>(tmem_slot + 2);                // number of active experts
+  unsigned int* s_gen = reinterpret_cast<unsigned int*>(tmem_slot + 3);  // launch generation
   // routing tables (phase 0)
   int32_t* s_act = reinterpret_cast<int32_t*>(smem + DK_STAGES * DK_STAGE + 256);  // [128] expert of tile m
   int32_t* s_ids = s_act + kDecodeMaxSlots;                                          // [128] slot ids
@@ -159,8 +189,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       ptx::mbar_init(&tempty[a], 4 * 32);
     }
     ptx::mbar_init(drain, 1);
-    ptx::mbar_init(epi_done, 4 * 32);
-    ptx::mbar_init(grid_pass, 1);
     *abort_flag = 0;
     ptx::fence_mbar_init();
   }
@@ -203,16 +231,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     int a = 0;
     for (int j = 0; j < S; ++j) a += s_first[j];
     *s_A = a;
+    // read once per CTA, before any of its threads arrives on the counter
+    *s_gen = *(volatile unsigned int*)&g_decode_bar_gen;
   }
   ptx::tc_fence_before();
   __syncthreads();
   ptx::tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const int A = *s_A;
-  // this launch's tag for the split counts: the barrier generation, the same
-  // for every CTA until this launch's barrier, different for every launch
-  const unsigned long long split_tag =
-      ((unsigned long long)(*(volatile unsigned int*)&g_decode_bar_gen) << 32) | 0x9e370000ull;
+  // this launch's tag for the tagged counts: the launch generation, the same
+  // for every CTA of the launch, different for every launch
+  const unsigned int gen = *s_gen;
+  const unsigned long long tag = ((unsigned long long)gen << 32) | 0x9e370000ull;
+  const unsigned int h_total = (unsigned int)p.nf1 * 4;  // (feature tile, warp) groups of one tile's h
   const int items1 = A * p.nf1 * p.splits1;
   const int items2 = A * p.nf2;
   const int stages2 = (p.kb2 + 1) / 2;                        // two w2 K blocks per stage
@@ -253,9 +284,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           advance();
         }
       }
-      // the first phase-2 stages' weights ahead of the barrier (they do not
-      // depend on h); a slot is free once its phase-1 MMAs are done, so these
-      // waits never depend on the barrier. At most one ring's worth.
+      // the first phase-2 stages' weights ahead of h (they do not depend on
+      // it); a slot is free once its phase-1 MMAs are done, so these waits
+      // never depend on other CTAs. At most one ring's worth.
       int pend_stage[DK_STAGES], pend_kb[DK_STAGES], pend_m[DK_STAGES], npend = 0;
       int it2 = blockIdx.x, kb2 = 0;  // next phase-2 stage: item it2, K blocks kb2, kb2 + 1
       while (ok && it2 < items2 && npend < DK_STAGES) {
@@ -281,27 +312,36 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           it2 += gridDim.x;
         }
       }
-      // h is complete once every CTA's phase-1 stores (and split reductions)
-      // are: this CTA's epilogue done -> device-wide barrier -> pass
-      bool passed = false;
-      if (ok) {
-        if (!ptx::mbar_wait(epi_done, 0, abort_flag) || !decode_grid_barrier(gridDim.x, abort_flag)) {
+      // tile m's h is complete once all its (feature tile, warp) groups are
+      // stored, whichever CTAs computed them: a tagged count per tile. A
+      // phase-2 stage's h rows are loaded once that count is full.
+      int ready_m = -1;
+      bool cleared = false;  // every CTA's phase-0 clears (of the counts too) are done
+      auto wait_h = [&](int m) {
+        if (m == ready_m) return true;
+        if (!cleared && !decode_all_arrived(gen, abort_flag)) {
           raise_device_error(7);
-          ok = false;
-        } else {
-          ptx::mbar_arrive(grid_pass);
-          passed = true;
+          return false;
         }
-      }
-      if (ok) {
+        cleared = true;
+        if (!wait_count(&p.h_ready[m], h_total, abort_flag)) {
+          raise_device_error(7);
+          return false;
+        }
         fence_proxy_async_global();  // h was written through the generic proxy; TMA reads it
-        for (int i = 0; i < npend; ++i) {
-          uint8_t* st = ring + pend_stage[i] * DK_STAGE;
-          const int nkb = min(2, p.kb2 - pend_kb[i]);
-          for (int j = 0; j < nkb; ++j)
-            ptx::tma_load_2d(st + DK_STAGE_A + j * kDecodeMaxTokens * ROW_BYTES, &tmap_h, &full[pend_stage[i]],
-                             (pend_kb[i] + j) * kElems, pend_m[i] * kDecodeMaxTokens);
-        }
+        ready_m = m;
+        return true;
+      };
+      // every stage given an expected byte count gets its h loads, also after
+      // a failed wait (then from h as it is: the kernel has failed, but the
+      // stage's barrier completes, so the drain below never waits it out)
+      for (int i = 0; i < npend; ++i) {
+        if (ok && !wait_h(pend_m[i])) ok = false;
+        uint8_t* st = ring + pend_stage[i] * DK_STAGE;
+        const int nkb = min(2, p.kb2 - pend_kb[i]);
+        for (int j = 0; j < nkb; ++j)
+          ptx::tma_load_2d(st + DK_STAGE_A + j * kDecodeMaxTokens * ROW_BYTES, &tmap_h, &full[pend_stage[i]],
+                           (pend_kb[i] + j) * kElems, pend_m[i] * kDecodeMaxTokens);
       }
       // the rest of phase 2
       while (ok && it2 < items2) {
@@ -313,13 +353,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         uint8_t* st = ring + stage * DK_STAGE;
         const int nkb = min(2, p.kb2 - kb2);
         ptx::mbar_arrive_expect_tx(&full[stage], nkb * (SW_A_TILE + kDecodeMaxTokens * ROW_BYTES));
-        for (int j = 0; j < nkb; ++j) {
+        for (int j = 0; j < nkb; ++j)
           ptx::tma_load_2d(st + j * SW_A_TILE, &tmap_w2, &full[stage], (kb2 + j) * kElems,
                            s_act[m] * p.H + f * SW_FEAT);
+        if (!wait_h(m)) ok = false;  // the h loads are issued regardless (see above)
+        for (int j = 0; j < nkb; ++j)
           ptx::tma_load_2d(st + DK_STAGE_A + j * kDecodeMaxTokens * ROW_BYTES, &tmap_h, &full[stage],
                            (kb2 + j) * kElems, m * kDecodeMaxTokens);
-        }
         advance();
+        if (!ok) break;
         kb2 += 2;
         if (kb2 >= p.kb2) {
           kb2 = 0;
@@ -329,9 +371,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       if (!ok) {
         raise_device_error(1);
         *abort_flag = 1;
-        // release the epilogue warps still waiting for a pass (they see the
-        // abort flag), then let this CTA's copies in flight land
-        if (!passed) ptx::mbar_arrive(grid_pass);
+        // let this CTA's copies in flight land
         volatile int never = 0;
         for (int i = 0; i < DK_STAGES; ++i)
           if (last_par[i] >= 0) ptx::mbar_wait(&full[i], (uint32_t)last_par[i], &never);
@@ -426,10 +466,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const int q = warp & 3;
     const int fit = q * 32 + lane;
     const int et = threadIdx.x - 64;  // 0..127
-    // phase-0 work of the epilogue warps, done before their first arrival
-    // (so before the barrier and any phase-2 add): distinct valid experts per
-    // token (the adds its output groups wait for), the fp32 accumulator and
-    // group counts cleared, zero output rows for tokens with no valid slot
+    // phase-0 work of the epilogue warps, done before the CTA arrives on the
+    // launch counter (so before any CTA's phase-2 add): distinct valid experts
+    // per token (the adds its output groups wait for), the fp32 accumulator
+    // and group counts cleared, zero output rows for tokens with no valid slot
     if (warp == 2 && lane < p.T) {
       int c = 0;
       for (int j = 0; j < p.k; ++j) {
@@ -443,12 +483,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const int64_t estride = (int64_t)gridDim.x * 128;
     for (int64_t i = (int64_t)blockIdx.x * 128 + et; i < (int64_t)p.T * p.H; i += estride) p.y32[i] = 0.f;
     for (int64_t i = (int64_t)blockIdx.x * 128 + et; i < (int64_t)p.T * p.nf2 * 4; i += estride) p.conv_cnt[i] = 0;
-    asm volatile("bar.sync 1, 128;" ::: "memory");  // s_kd complete (epilogue warps only)
+    for (int64_t i = (int64_t)blockIdx.x * 128 + et; i < A; i += estride) p.h_ready[i] = 0;
+    __threadfence();
+    asm volatile("bar.sync 1, 128;" ::: "memory");  // s_kd complete, clears fenced (epilogue warps only)
+    if (et == 0) decode_launch_arrive(gridDim.x);
     for (int t = 0; t < p.T; ++t)
       if (s_kd[t] == 0)
         for (int64_t i = (int64_t)blockIdx.x * 128 + et; i < p.H; i += estride)
           store1_out(p.y, p.dtype, (int64_t)t * p.H + i, 0.f);
     bool ok = true;
+    bool cleared = false;  // (lane 0) every CTA's phase-0 clears are done
     int it = 0;
     for (int i1 = blockIdx.x; i1 < items1; i1 += gridDim.x, ++it) {
       const int m = i1 / (p.nf1 * p.splits1), rem = i1 % (p.nf1 * p.splits1);
@@ -489,7 +533,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         __threadfence();
         __syncwarp();
         int last = 0;
-        if (lane == 0) last = tagged_count_last(&p.split_cnt[unit * 4 + q], split_tag, (unsigned)p.splits1);
+        if (lane == 0) last = tagged_count_last(&p.split_cnt[unit * 4 + q], tag, (unsigned)p.splits1);
         last = __shfl_sync(0xffffffffu, last, 0);
         if (last < 0) {
           ok = false;
@@ -518,6 +562,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             store1_out(p.h, p.dtype, ((int64_t)m * kDecodeMaxTokens + t) * p.I + feat, silu_mul(gs, us));
           }
         }
+        if (!last) continue;  // the unit's last split stores and counts this warp's features
       } else if (feat_ok) {
 #pragma unroll
         for (int t = 0; t < kDecodeMaxTokens; ++t)
@@ -525,21 +570,35 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             store1_out(p.h, p.dtype, ((int64_t)m * kDecodeMaxTokens + t) * p.I + feat,
                        silu_mul(acc_value<KIND>(g[t]), acc_value<KIND>(u[t])));
       }
+      // this warp's 32 features of tile m are stored: count them (once every
+      // CTA has cleared its part of the counts)
+      __threadfence();
+      __syncwarp();
+      int cnt_ok = 1;
+      if (lane == 0) {
+        if (!cleared && !decode_all_arrived(gen, abort_flag)) {
+          raise_device_error(7);
+          cnt_ok = 0;
+        } else {
+          cleared = true;
+          atomicAdd(&p.h_ready[m], 1u);
+        }
+      }
+      if (!__shfl_sync(0xffffffffu, cnt_ok, 0)) {
+        ok = false;
+        break;
+      }
     }
-    // phase-1 stores done: tell the producer, which arrives at the barrier;
-    // every later step waits for the producer's pass of the previous barrier,
-    // so epilogue and producer signals strictly alternate
-    volatile int never = 0;
-    uint32_t passes = 0;
-    auto wait_pass = [&]() {
-      const bool w = ptx::mbar_wait(grid_pass, passes & 1, &never);
-      ++passes;
-      return w && !*abort_flag;
-    };
-    __threadfence();
-    ptx::mbar_arrive(epi_done);
-    if (!wait_pass()) ok = false;
-    // phase 2: weighted adds into the fp32 accumulator
+    // phase 2: weighted adds into the fp32 accumulator, once every CTA has
+    // cleared its part of it (all arrived on the launch counter)
+    if (ok && blockIdx.x < items2) {
+      int arrived = 1;
+      if (lane == 0 && !cleared) arrived = decode_all_arrived(gen, abort_flag);
+      if (!__shfl_sync(0xffffffffu, arrived, 0)) {
+        if (lane == 0) raise_device_error(7);
+        ok = false;
+      }
+    }
     for (int i2 = blockIdx.x; ok && i2 < items2; i2 += gridDim.x, ++it) {
       const int m = i2 / p.nf2, f = i2 % p.nf2;
       const int buf = it & 1;
@@ -607,7 +666,7 @@ constexpr size_t kDecodeSmem = 1024 + (size_t)DK_STAGES * DK_STAGE + 256 + 4 * k
 
 struct DecodeWs {
   int max_tiles, nf1, nf2, kb1, kb2, splits1;
-  size_t h, partial, split_cnt, y32, conv_cnt, bytes;
+  size_t h, partial, split_cnt, h_ready, y32, conv_cnt, bytes;
 };
 
 DecodeWs decode_ws(int64_t T, int k, int E, int64_t H, int64_t I, int dtype) {
@@ -631,6 +690,7 @@ DecodeWs decode_ws(int64_t T, int k, int E, int64_t H, int64_t I, int dtype) {
   w.h = take((size_t)w.max_tiles * kDecodeMaxTokens * I * es);
   w.partial = take(w.splits1 > 1 ? (size_t)units1 * w.splits1 * 2 * SW_FEAT * kDecodeMaxTokens * 4 : 0);
   w.split_cnt = take(w.splits1 > 1 ? (size_t)units1 * 4 * sizeof(unsigned long long) : 0);
+  w.h_ready = take((size_t)w.max_tiles * sizeof(unsigned int));
   w.y32 = take((size_t)T * H * 4);
   w.conv_cnt = take((size_t)T * w.nf2 * 4 * sizeof(int32_t));
   w.bytes = off;
@@ -683,6 +743,7 @@ int decode_fused(const void* x, int dtype, int64_t T, int64_t H, const void* w13
   p.h = ws + w.h;
   p.partial = reinterpret_cast<float*>(ws + w.partial);
   p.split_cnt = reinterpret_cast<unsigned long long*>(ws + w.split_cnt);
+  p.h_ready = reinterpret_cast<unsigned int*>(ws + w.h_ready);
   p.y32 = reinterpret_cast<float*>(ws + w.y32);
   p.conv_cnt = reinterpret_cast<int32_t*>(ws + w.conv_cnt);
   p.y = y;

@@ -963,8 +963,16 @@ extern "C" int moe_get_device_error(int* host_code, void* stream) {
   MOE_CUDA_TRY(cudaMemcpyFromSymbolAsync(host_code, g_moe_device_error, sizeof(int), 0, cudaMemcpyDeviceToHost, st));
   MOE_CUDA_TRY(cudaMemcpyToSymbolAsync(g_moe_device_error, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, st));
   MOE_CUDA_TRY(cudaStreamSynchronize(st));
-  if (*host_code == 7) {  // a barrier of the one-launch decode kernel timed out: re-arm it
+  if (*host_code != 0) {
+    // a failed launch of the one-launch decode kernel may leave its launch
+    // counter partial: clear it and move to a fresh generation, so the next
+    // launch's tag differs from every count word the failed one left
+    unsigned int gen = 0;
     static const unsigned int z = 0;
+    MOE_CUDA_TRY(cudaMemcpyFromSymbolAsync(&gen, g_decode_bar_gen, sizeof(gen), 0, cudaMemcpyDeviceToHost, st));
+    MOE_CUDA_TRY(cudaStreamSynchronize(st));
+    gen += 1;
+    MOE_CUDA_TRY(cudaMemcpyToSymbolAsync(g_decode_bar_gen, &gen, sizeof(gen), 0, cudaMemcpyHostToDevice, st));
     MOE_CUDA_TRY(cudaMemcpyToSymbolAsync(g_decode_bar_count, &z, sizeof(z), 0, cudaMemcpyHostToDevice, st));
     MOE_CUDA_TRY(cudaStreamSynchronize(st));
   }

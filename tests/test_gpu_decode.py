@@ -1,7 +1,8 @@
 """The one-launch decode kernel (MOE_OPT_DECODE_FUSED): at most 16 tokens and
 128 routed slots run as one persistent kernel — routing, gate_up GEMM +
 SwiGLU, down GEMM + weighted combine and the output conversion as phases
-separated by device-wide barriers. Checked against the oracle (max-abs-rel
+whose CTAs hand results on through counters (a launch counter in the
+library's memory, counts in the workspace). Checked against the oracle (max-abs-rel
 error 1e-2, the bar of every bf16 output here) and against the multi-launch
 path on the same inputs."""
 import numpy as np
@@ -93,9 +94,10 @@ def test_dropped_and_repeated_ids():
     assert mb.device_error(dev()) == 0
 
 
-def test_barrier_rearms_over_many_launches_of_different_grids():
-    """Consecutive launches with different grid sizes (the barrier counts the
-    CTAs of each launch) stay correct and raise no device error."""
+def test_launch_counter_over_many_launches_of_different_grids():
+    """Consecutive launches with different grid sizes (the launch counter
+    counts the CTAs of each launch and tags its counts) stay correct and
+    raise no device error."""
     H, I, E = 2048, 768, 128
     w13 = (torch.randn(E, 2 * I, H, device=dev()) * 0.02).to(torch.bfloat16).transpose(1, 2)
     w2 = (torch.randn(E, H, I, device=dev()) * 0.02).to(torch.bfloat16).transpose(1, 2)
