@@ -584,8 +584,11 @@ def build_single(ctx, cfg, T, n_var, graph, weights=None):
     return out
 
 
-def build_ep(ctx, cfg, T, ep_kind):
-    """Expert-parallel workload on this rank: its E / N experts, T tokens."""
+def build_ep(ctx, cfg, T, ep_kind, replicate=False):
+    """Expert-parallel workload on this rank: its E / N experts, T tokens.
+    replicate: also hold the replicas mail_b200.ep.plan_replicas picks from
+    every rank's slot counts of this routing (at most E / N of them)."""
+    import mail_b200 as mb
     from mail_b200 import ep as mep
 
     E, world, rank = cfg["E"], ctx.world, ctx.rank
@@ -593,16 +596,25 @@ def build_ep(ctx, cfg, T, ep_kind):
     x, ids, wts, dt = make_inputs(cfg, rank, ctx.device)
     local = list(range(rank * E // world, (rank + 1) * E // world))
     w13, w2, scales = make_weights(cfg, local, ctx.device, dt)
+    replicas, rep = None, []
+    if replicate:
+        counts = ctx.torch.empty((world, E), dtype=ctx.torch.int32, device=ctx.device)
+        ctx.dist.all_gather_into_tensor(counts, mb.moe_align(ids, E, block_m=1)["group_sizes"])
+        rep = mep.plan_replicas(counts, E // world)
+        if rep:
+            r13, r2, rsc = make_weights(cfg, rep, ctx.device, dt)
+            replicas = (rep, r13, r2, rsc)
     if ep_kind == "peer":
-        layer = mep.PeerExpertParallelMoE(w13, w2, E, max_tokens=T, top_k=cfg["k"], dtype=dt, scales=scales)
+        layer = mep.PeerExpertParallelMoE(w13, w2, E, max_tokens=T, top_k=cfg["k"], dtype=dt, scales=scales,
+                                          replicas=replicas)
     else:
-        layer = mep.ExpertParallelMoE(w13, w2, E, scales=scales)
+        layer = mep.ExpertParallelMoE(w13, w2, E, scales=scales, replicas=replicas)
 
     def step(xx, ii, ww):
         return layer(xx, ww, ii)
     variants = [(x, ids, wts)]
     return dict(step=step, variants=variants, weights=(w13, w2, scales), layer=layer, kernels=None, dt=dt,
-                captured=None, inp=lambda i: variants[0])
+                captured=None, inp=lambda i: variants[0], replicas=rep)
 
 
 def close_workload(ctx, w):
@@ -614,13 +626,14 @@ def close_workload(ctx, w):
     ctx.torch.cuda.empty_cache()
 
 
-def run_config(ctx, name, T, args, peaks, int8, weights=None, steps=None, warmup=3, ep_kind="peer"):
+def run_config(ctx, name, T, args, peaks, int8, weights=None, steps=None, warmup=3, ep_kind="peer",
+               replicate=False):
     """A sub-configuration of the line: build, warm up, time, roofline."""
     cfg = dict(CONFIGS[name])
     cfg["T"] = T
     steps = steps or args.steps
     if ctx.world > 1:
-        w = build_ep(ctx, cfg, T, ep_kind)
+        w = build_ep(ctx, cfg, T, ep_kind, replicate=replicate)
         n_var, l2 = 1, "expert-parallel, weights streamed every step"
     else:
         n_var, l2 = n_variants(cfg, T, 1, ctx.rank)
@@ -637,6 +650,8 @@ def run_config(ctx, name, T, args, peaks, int8, weights=None, steps=None, warmup
            "value": ctx.world * T / (r["ms"] / 1e3), "unit": "tokens/s", "ms_per_step": r["ms"], "steps": steps,
            "kernel_clocks": r["kernel_clocks"], "roofline": roof, "clocks": r["clocks"], "l2": l2,
            "graph_steps": w.get("chain_steps", 1)}
+    if ctx.world > 1:
+        out["replicated_experts"] = w.get("replicas", [])
     if ctx.world == 1:
         # the step's own weight-streaming bound: every active expert's three
         # matrices once at the measured copy rate
@@ -672,6 +687,15 @@ def sub_configs(ctx, args, peaks, int8):
         Ts = 8192 // ctx.world
         res["dsv3-w8a8-strong"], _ = run_config(ctx, "dsv3-w8a8", Ts, args, peaks, int8, ep_kind=args.ep)
         res["dsv3-w8a8-strong"].update(scaling="strong", tokens_total=8192)
+        # load-imbalance stress: expert-parallel as is, then with the replicas
+        # plan_replicas picks from the all-gathered slot counts
+        st_steps = max(5, args.steps // 2)
+        res["stress-w8a8"], _ = run_config(ctx, "stress-w8a8", 65536, args, peaks, int8, steps=st_steps,
+                                           ep_kind=args.ep)
+        res["stress-w8a8"]["scaling"] = "weak"
+        res["stress-w8a8-replicated"], _ = run_config(ctx, "stress-w8a8", 65536, args, peaks, int8, steps=st_steps,
+                                                      ep_kind=args.ep, replicate=True)
+        res["stress-w8a8-replicated"]["scaling"] = "weak"
     return res
 
 

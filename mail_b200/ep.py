@@ -14,6 +14,11 @@ Rank r owns experts [r * E / W, (r + 1) * E / W). One forward:
   6. combine: y[t] = sum_j topk_weights[t, j] * out[slot_pos[t * k + j]]
      (deterministic fp32 sum, moe_combine_rows)
 
+Hot experts can be replicated (`replicas=`): every rank then also holds
+their weights and serves the slots its own tokens route to them, so a
+popular expert's load spreads over all ranks instead of landing on its
+owner (ExpertPlacement).
+
 The reference has no distributed code; this layer is what the multi-GPU
 workloads need around the single-GPU hot path. The device work of steps 1, 3,
 4 and 6 goes through `ops` (CudaOps = libmoe_b200 kernels); the collectives
@@ -29,6 +34,119 @@ import torch.distributed as dist
 
 from . import _lib
 from . import moe as _moe
+
+
+class ExpertPlacement:
+    """Which rank runs each routed slot.
+
+    E experts over W ranks: rank r owns experts [r * E / W, (r + 1) * E / W).
+    `replicated` experts (the same list on every rank) are also held by every
+    rank, and a slot routed to one of them runs on the rank whose token it
+    is. The exchange then works in a virtual expert space of W * EL' ids,
+    EL' = E / W + len(replicated): rank r's virtual experts
+    [r * EL', (r + 1) * EL') are its owned experts in order, then its copies
+    of the replicated ones in list order. `remap` turns this rank's global
+    ids into virtual ids (invalid ids, < 0 or >= E, become -1: dropped), so
+    the plan, dispatch and expert pass run unchanged over EL' local experts.
+    Replicas hold the same weights, so each row's result is the same
+    wherever it runs.
+    """
+
+    def __init__(self, num_experts: int, world: int, rank: int, replicated=()):
+        if num_experts % world:
+            raise ValueError("num_experts must be divisible by the world size")
+        rep_list = [int(e) for e in replicated]
+        if len(set(rep_list)) != len(rep_list) or any(e < 0 or e >= num_experts for e in rep_list):
+            raise ValueError("replicated experts must be distinct ids in [0, num_experts)")
+        self.E, self.world, self.rank = num_experts, world, rank
+        self.replicated = rep_list
+        self.EL = num_experts // world
+        self.EL_virtual = self.EL + len(rep_list)
+        self.E_virtual = world * self.EL_virtual
+        lut = torch.empty(num_experts, dtype=torch.int32)
+        for e in range(num_experts):
+            owner = e // self.EL
+            lut[e] = owner * self.EL_virtual + (e - owner * self.EL)
+        for j, e in enumerate(rep_list):
+            lut[e] = rank * self.EL_virtual + self.EL + j
+        self._lut_cpu = lut
+        self._lut = {}
+
+    def lut(self, device) -> torch.Tensor:
+        """Global id -> virtual id for this rank, on `device`."""
+        key = str(device)
+        if key not in self._lut:
+            self._lut[key] = self._lut_cpu.to(device)
+        return self._lut[key]
+
+    def remap(self, topk_ids: torch.Tensor) -> torch.Tensor:
+        if not self.replicated:
+            return topk_ids
+        ids = topk_ids.to(torch.int64)
+        valid = (ids >= 0) & (ids < self.E)
+        v = self.lut(topk_ids.device)[ids.clamp(0, self.E - 1)]
+        return torch.where(valid, v, torch.full_like(v, -1)).to(torch.int32)
+
+    def local_weights(self, w13, w2, scales=None, replicas=None):
+        """This rank's owned experts followed by its replica copies, as one
+        [EL', ...] set: logical (E, K, N) views over K-major storage (int8
+        scales concatenated the same way)."""
+        if not self.replicated:
+            return w13, w2, scales
+        if replicas is None:
+            raise ValueError("replicated experts need their weights (replicas=)")
+        ids, r13, r2 = replicas[0], replicas[1], replicas[2]
+        rsc = replicas[3] if len(replicas) > 3 else None
+        if [int(e) for e in ids] != self.replicated:
+            raise ValueError("replica weights must be given in the order of the replicated ids")
+        if r13.shape[0] != len(self.replicated) or r2.shape[0] != len(self.replicated):
+            raise ValueError("one replica weight per replicated expert")
+        w13v = torch.cat([_moe.kmajor(w13), _moe.kmajor(r13)]).transpose(1, 2)
+        w2v = torch.cat([_moe.kmajor(w2), _moe.kmajor(r2)]).transpose(1, 2)
+        sc = None
+        if scales is not None:
+            if rsc is None:
+                raise ValueError("int8 replicas need their scales")
+            sc = tuple(torch.cat([a.to(torch.float32), b.to(torch.float32)]) for a, b in zip(scales, rsc))
+        return w13v, w2v, sc
+
+
+def plan_replicas(counts: torch.Tensor, n: int):
+    """Replicas that even out the expert-parallel load.
+
+    counts [W, E]: slots rank r routes to expert e (the all-gathered
+    per-rank counts, so every rank computes the same list). A rank's load is
+    the slots of its owned experts from every rank plus its own slots to the
+    replicated experts. Greedy: add, one at a time, the expert whose
+    replication lowers the largest rank load the most (ties to the lower
+    id); stop after n or when no single replica lowers it."""
+    C = counts.to(torch.int64).cpu()
+    W, E = C.shape
+    EL = E // W
+    tot = C.sum(0)
+    owner = torch.arange(E) // EL
+    load = torch.zeros(W, dtype=torch.int64).index_add_(0, owner, tot)
+    chosen = []
+    for _ in range(n):
+        # max over ranks of the load if expert e were replicated, for every e
+        cand = load.view(W, 1) + C - torch.nn.functional.one_hot(owner, W).T * tot.view(1, E)
+        best = cand.max(0).values
+        if chosen:
+            best[torch.tensor(chosen)] = torch.iinfo(torch.int64).max
+        e = int(torch.argmin(best))  # first minimum: the lower id on ties
+        if int(best[e]) >= int(load.max()):
+            break
+        chosen.append(e)
+        load = cand[:, e].clone()
+    return chosen
+
+
+def hot_experts(group_sizes: torch.Tensor, n: int):
+    """The n experts with the most routed slots (ties to the lower id), from
+    per-expert counts summed over the ranks — the replicas to place."""
+    c = group_sizes.to(torch.int64).cpu()
+    order = sorted(range(c.numel()), key=lambda e: (-int(c[e]), e))
+    return order[:n]
 
 
 class CudaOps:
@@ -73,7 +191,7 @@ class ExpertParallelMoE:
     """
 
     def __init__(self, w13, w2, num_experts: int, scales=None, group=None, ops=None, chunks: int = 1,
-                 min_chunk_tokens: int = 1024):
+                 min_chunk_tokens: int = 1024, replicas=None):
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
@@ -83,7 +201,8 @@ class ExpertParallelMoE:
         self.E_local = num_experts // self.world
         if w13.shape[0] != self.E_local or w2.shape[0] != self.E_local:
             raise ValueError(f"expected {self.E_local} local experts, got {w13.shape[0]}/{w2.shape[0]}")
-        self.w13, self.w2, self.scales = w13, w2, scales
+        self.placement = ExpertPlacement(num_experts, self.world, self.rank, replicas[0] if replicas else ())
+        self.w13, self.w2, self.scales = self.placement.local_weights(w13, w2, scales, replicas)
         self.ops = ops or CudaOps()
         self.chunks = max(1, int(chunks))
         self.min_chunk_tokens = min_chunk_tokens
@@ -96,12 +215,13 @@ class ExpertParallelMoE:
     def __call__(self, x: torch.Tensor, topk_weights: torch.Tensor, topk_ids: torch.Tensor) -> torch.Tensor:
         T, H = x.shape
         k = topk_ids.shape[1]
-        W, EL = self.world, self.E_local
+        W, EL = self.world, self.placement.EL_virtual
         topk_weights = topk_weights.to(torch.float32).contiguous()
+        topk_ids = self.placement.remap(topk_ids)  # virtual ids: replicated experts stay on this rank
         bounds = self._bounds(T)
         C = len(bounds)
         # 1. per-chunk dispatch plan (stable sort by expert = by owning rank)
-        plans = [self.ops.sort_slots(topk_ids[a:b], self.E) for a, b in bounds]
+        plans = [self.ops.sort_slots(topk_ids[a:b], self.placement.E_virtual) for a, b in bounds]
         per_dest = torch.stack([gs.to(torch.int64).view(W, EL) for _, _, gs, _ in plans], dim=1)  # [W, C, EL]
         recv_expert = torch.empty_like(per_dest)
         dist.all_to_all_single(recv_expert, per_dest.contiguous(), group=self.group)     # [W(src), C, EL]
@@ -158,7 +278,7 @@ class PeerExpertParallelMoE:
     """
 
     def __init__(self, w13, w2, num_experts: int, max_tokens: int, top_k: int, dtype=torch.bfloat16,
-                 scales=None, group=None):
+                 scales=None, group=None, replicas=None):
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
@@ -167,6 +287,10 @@ class PeerExpertParallelMoE:
         self.E, self.EL = num_experts, num_experts // self.world
         if w13.shape[0] != self.EL or w2.shape[0] != self.EL:
             raise ValueError(f"expected {self.EL} local experts, got {w13.shape[0]}/{w2.shape[0]}")
+        # from here on E / EL count virtual experts (owned + replicas per rank)
+        self.placement = ExpertPlacement(num_experts, self.world, self.rank, replicas[0] if replicas else ())
+        w13, w2, scales = self.placement.local_weights(w13, w2, scales, replicas)
+        self.E, self.EL = self.placement.E_virtual, self.placement.EL_virtual
         self.H = w13.shape[1]
         self.I = w13.shape[2] // 2
         self.k = top_k
@@ -231,7 +355,7 @@ class PeerExpertParallelMoE:
             raise ValueError("PeerExpertParallelMoE: input does not match the buffers it was built for")
         st = _moe._stream(x.device)
         x = x.contiguous()
-        ids = topk_ids.to(torch.int32).contiguous()
+        ids = self.placement.remap(topk_ids.to(torch.int32)).contiguous()
         w = topk_weights.to(torch.float32).contiguous()
         S = T * self.k
         a = _moe.moe_align(ids, self.E, block_m=1)

@@ -58,7 +58,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, E, T, H, I, k, drop, chunks, result_q):
+def _worker(rank, world, port, E, T, H, I, k, drop, chunks, result_q, replicated=()):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
@@ -72,9 +72,11 @@ def _worker(rank, world, port, E, T, H, I, k, drop, chunks, result_q):
         if drop:
             ids[::4, 0] = -1
         el = E // world
+        rep = list(replicated)
+        replicas = (rep, torch.from_numpy(w13[rep]), torch.from_numpy(w2[rep])) if rep else None
         layer = ExpertParallelMoE(torch.from_numpy(w13[rank * el:(rank + 1) * el]),
                                   torch.from_numpy(w2[rank * el:(rank + 1) * el]), E, ops=OracleOps(),
-                                  chunks=chunks, min_chunk_tokens=8)
+                                  chunks=chunks, min_chunk_tokens=8, replicas=replicas)
         y = layer(torch.from_numpy(x), torch.from_numpy(wts), torch.from_numpy(ids))
         ref = O.moe_mlp_topk(x, w13, w2, wts, ids)
         result_q.put((rank, float(np.abs(y.numpy() - ref).max()), float(np.abs(ref).max())))
@@ -82,14 +84,19 @@ def _worker(rank, world, port, E, T, H, I, k, drop, chunks, result_q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("E,T,k,drop,chunks", [(8, 40, 2, False, 1), (4, 33, 3, True, 3), (6, 1, 2, False, 2),
-                                                (8, 64, 2, True, 2)])
-def test_expert_parallel_two_ranks_matches_oracle(E, T, k, drop, chunks):
+@pytest.mark.parametrize("E,T,k,drop,chunks,replicated", [(8, 40, 2, False, 1, ()), (4, 33, 3, True, 3, ()),
+                                                           (6, 1, 2, False, 2, ()), (8, 64, 2, True, 2, ()),
+                                                           (8, 40, 2, False, 1, (5,)), (4, 33, 3, True, 3, (0, 3)),
+                                                           (8, 64, 2, True, 2, (6, 1, 2))])
+def test_expert_parallel_two_ranks_matches_oracle(E, T, k, drop, chunks, replicated):
+    """Replicated experts (one owned by each rank, in the last cases) run on
+    the rank whose token routes to them; results stay those of the oracle."""
     world = 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, E, T, 32, 24, k, drop, chunks, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, E, T, 32, 24, k, drop, chunks, q, replicated))
+             for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:

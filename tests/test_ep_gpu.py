@@ -1,5 +1,6 @@
 """Expert-parallel layer on 2 GPUs (NCCL): matches the single-GPU fused op on
-the same weights and tokens. Skipped when fewer than 2 GPUs are visible."""
+the same weights and tokens, also with replicated experts. Skipped when fewer
+than 2 GPUs are visible."""
 import os
 import socket
 
@@ -31,7 +32,7 @@ def _worker(rank, world, port, cfg, transport, q):
     dev = torch.device("cuda", rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60), device_id=dev)
     try:
-        T, H, I, E, k, quant = cfg
+        T, H, I, E, k, quant, repl = cfg
         g = torch.Generator(device=dev).manual_seed(7)  # identical global weights on every rank
         w13 = (torch.randn(E, 2 * I, H, device=dev, generator=g) * 0.02).to(torch.bfloat16).transpose(1, 2)
         w2 = (torch.randn(E, H, I, device=dev, generator=g) * 0.02).to(torch.bfloat16).transpose(1, 2)
@@ -45,13 +46,17 @@ def _worker(rank, world, port, cfg, transport, q):
         ids_t, wts_t = torch.from_numpy(ids).to(dev), torch.from_numpy(wts).to(dev)
         el = E // world
         lsc = None if scales is None else tuple(s[rank * el:(rank + 1) * el] for s in scales)
+        rl = list(repl)
+        replicas = None
+        if rl:  # every rank also holds these experts and serves its own slots to them
+            replicas = (rl, w13[rl], w2[rl], None if scales is None else tuple(s[rl] for s in scales))
         if transport == "peer":
             from mail_b200.ep import PeerExpertParallelMoE
             layer = PeerExpertParallelMoE(w13[rank * el:(rank + 1) * el], w2[rank * el:(rank + 1) * el], E,
-                                          max_tokens=T, top_k=k, scales=lsc)
+                                          max_tokens=T, top_k=k, scales=lsc, replicas=replicas)
         else:
             layer = ExpertParallelMoE(w13[rank * el:(rank + 1) * el], w2[rank * el:(rank + 1) * el], E,
-                                      scales=lsc, chunks=2, min_chunk_tokens=128)
+                                      scales=lsc, chunks=2, min_chunk_tokens=128, replicas=replicas)
         y = layer(x, wts_t, ids_t)
         y_again = layer(x, wts_t, ids_t)  # the second call reuses the buffers
         torch.cuda.synchronize()
@@ -70,7 +75,8 @@ def _worker(rank, world, port, cfg, transport, q):
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 @pytest.mark.parametrize("transport", ["peer", "nccl"])
-@pytest.mark.parametrize("cfg", [(512, 1024, 512, 8, 2, False), (300, 1024, 256, 16, 4, True)])
+@pytest.mark.parametrize("cfg", [(512, 1024, 512, 8, 2, False, ()), (300, 1024, 256, 16, 4, True, ()),
+                                 (512, 1024, 512, 8, 2, False, (5,)), (300, 1024, 256, 16, 4, True, (0, 9))])
 def test_expert_parallel_matches_single_gpu(cfg, transport):
     world = 2
     ctx = mp.get_context("spawn")

@@ -58,13 +58,23 @@ def _ptrs(ts):
     return torch.tensor([t.data_ptr() for t in ts], dtype=torch.int64, device=DEV)
 
 
-@pytest.mark.parametrize("W,E,k,T,quant", [(2, 8, 2, 300, False), (4, 8, 2, 256, False), (2, 16, 4, 200, True)])
-def test_ep_emulated_ranks_match_single_gpu(W, E, k, T, quant):
+@pytest.mark.parametrize("W,E,k,T,quant,rep", [(2, 8, 2, 300, False, ()), (4, 8, 2, 256, False, ()),
+                                                (2, 16, 4, 200, True, ()), (4, 8, 2, 256, False, (6, 1)),
+                                                (2, 16, 4, 200, True, (3,))])
+def test_ep_emulated_ranks_match_single_gpu(W, E, k, T, quant, rep):
+    """rep: experts replicated on every rank (mail_b200.ep.ExpertPlacement):
+    the exchange then runs over virtual expert ids, owned experts first, then
+    the replicas, and a replicated expert's slots stay on their own rank."""
+    from mail_b200.ep import ExpertPlacement
     H, I = 512, 256
-    EL = E // W
+    E_glob = E
+    places = [ExpertPlacement(E, W, r, rep) for r in range(W)]
+    EL_own = E // W
+    EL = places[0].EL_virtual
+    E = places[0].E_virtual
     g = torch.Generator(device=DEV).manual_seed(11)
-    w13 = (torch.randn(E, 2 * I, H, device=DEV, generator=g) * 0.03).to(torch.bfloat16).transpose(1, 2)
-    w2 = (torch.randn(E, H, I, device=DEV, generator=g) * 0.03).to(torch.bfloat16).transpose(1, 2)
+    w13 = (torch.randn(E_glob, 2 * I, H, device=DEV, generator=g) * 0.03).to(torch.bfloat16).transpose(1, 2)
+    w2 = (torch.randn(E_glob, H, I, device=DEV, generator=g) * 0.03).to(torch.bfloat16).transpose(1, 2)
     scales = None
     if quant:
         w13, w2, scales = mb.quantize_weights_int8(w13, w2)
@@ -72,8 +82,10 @@ def test_ep_emulated_ranks_match_single_gpu(W, E, k, T, quant):
     for r in range(W):
         rng = np.random.default_rng(100 + r)
         xs.append(torch.from_numpy(rng.standard_normal((T, H), dtype=np.float32)).to(DEV, torch.bfloat16))
-        ids, wts = O.synthetic_routing("uniform-softmax", T, E, k, seed=r)
+        ids, wts = O.synthetic_routing("uniform-softmax", T, E_glob, k, seed=r)
         ids[::6, 0] = -1
+        if rep:
+            ids[1::3, 1] = rep[0]  # make the first replicated expert hot
         idss.append(torch.from_numpy(ids).to(DEV))
         wtss.append(torch.from_numpy(wts).to(DEV))
     S = T * k
@@ -84,7 +96,8 @@ def test_ep_emulated_ranks_match_single_gpu(W, E, k, T, quant):
     recv_s = [torch.empty(recv_cap, dtype=torch.float32, device=DEV) for _ in range(W)]
     meta = [torch.full((recv_cap,), -5, dtype=torch.int32, device=DEV) for _ in range(W)]
     ret = [torch.empty((S, H), dtype=torch.bfloat16, device=DEV) for _ in range(W)]
-    aligns = [mb.moe_align(idss[r], E, 1) for r in range(W)]
+    vids = [places[r].remap(idss[r]).contiguous() for r in range(W)]
+    aligns = [mb.moe_align(vids[r], E, 1) for r in range(W)]
     counts = torch.stack([a["group_sizes"] for a in aligns])
     tables, dests, rets = [], [], []
     for r in range(W):
@@ -98,7 +111,7 @@ def test_ep_emulated_ranks_match_single_gpu(W, E, k, T, quant):
     px, ps, pm, pr = _ptrs(recv_x), _ptrs(recv_s), _ptrs(meta), _ptrs(ret)
     for r in range(W):
         a = aligns[r]
-        _lib.call("moe_ep_dispatch", xs[r].data_ptr(), _lib.BF16, H, k, idss[r].data_ptr(), a["sorted_slots"].data_ptr(),
+        _lib.call("moe_ep_dispatch", xs[r].data_ptr(), _lib.BF16, H, k, vids[r].data_ptr(), a["sorted_slots"].data_ptr(),
                   a["padded_offsets"].data_ptr(), dests[r].data_ptr(), a["tile_table"][1:2].data_ptr(), S, W, r, EL,
                   recv_cap, px.data_ptr(), recv_code, ps.data_ptr() if quant else None, pm.data_ptr(), err.data_ptr(),
                   st())
@@ -106,11 +119,13 @@ def test_ep_emulated_ranks_match_single_gpu(W, E, k, T, quant):
     ws = torch.empty(_lib.query("moe_ep_expert_pass_workspace_size", recv_cap, I, recv_code), dtype=torch.uint8,
                      device=DEV)
     for r in range(W):
-        sl = slice(r * EL, (r + 1) * EL)
-        s13 = scales[0][sl].contiguous() if quant else None
-        s2 = scales[1][sl].contiguous() if quant else None
+        # this rank's owned experts, then its replica copies
+        own = list(range(r * EL_own, (r + 1) * EL_own)) + list(rep)
+        w13r, w2r = w13k[own].contiguous(), w2k[own].contiguous()
+        s13 = scales[0][own].contiguous() if quant else None
+        s2 = scales[1][own].contiguous() if quant else None
         _lib.call("moe_ep_expert_pass", recv_x[r].data_ptr(), recv_code, recv_s[r].data_ptr() if quant else None,
-                  recv_cap, H, w13k[sl].data_ptr(), w2k[sl].data_ptr(), EL, I,
+                  recv_cap, H, w13r.data_ptr(), w2r.data_ptr(), EL, I,
                   s13.data_ptr() if quant else None, s2.data_ptr() if quant else None, tables[r].data_ptr(),
                   meta[r].data_ptr(), pr.data_ptr(), W, S, _lib.BF16, ws.data_ptr(), ws.numel(), st())
     assert int(err.item()) == 0
