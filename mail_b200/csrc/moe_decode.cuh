@@ -130,18 +130,72 @@ __device__ __forceinline__ void fence_proxy_async_global() {
   asm volatile("fence.proxy.async.global;" ::: "memory");
 }
 
+// The gate_up phase's work: units u = m * nf1 + f (expert tile m, feature
+// tile f) of kb1 K blocks each, spread over the G CTAs in one of two ways:
+//   split  (sp >= 1, while units * sp <= G): CTA b < units * sp takes K split
+//          b % sp of unit b / sp (balanced, non-empty ranges); sp = 1 is one
+//          unit per CTA
+//   waves  (sp = 0, more units than CTAs): whole units, CTA b taking units b,
+//          b + G, ..., so each wave's expert tiles finish together and their
+//          down phase starts while the next wave runs. (Splitting the
+//          partial last wave along K over all CTAs measured slower: the
+//          reduction of its partials costs more than the imbalance it
+//          removes, which the down phase mostly overlaps anyway.)
+// A unit split over several CTAs is a sum of fp32 partials, one slot per
+// CTA.
+struct P1Plan {
+  int sp, kb1, units, G;
+  __device__ P1Plan(int units_, int kb1_, int G_) : kb1(kb1_), units(units_), G(G_) {
+    if (2 * units <= G && units > 0) sp = max(1, min(min(G / units, kDecodeMaxSplits), kb1 / 4));
+    else sp = units <= G ? 1 : 0;
+  }
+  // segments (unit, K blocks [k0, k1)) of CTA b, in order
+  struct Iter {
+    const P1Plan& pl;
+    int b, next_u;
+    __device__ Iter(const P1Plan& p, int b_) : pl(p), b(b_), next_u(b_) {}
+    __device__ bool next(int& u, int& k0, int& k1) {
+      if (pl.sp) {
+        if (next_u != b || b >= pl.units * pl.sp) return false;
+        u = b / pl.sp;
+        const int s = b % pl.sp;
+        k0 = s * pl.kb1 / pl.sp;
+        k1 = (s + 1) * pl.kb1 / pl.sp;
+        next_u = -1;
+        return true;
+      }
+      if (next_u >= pl.units) return false;
+      u = next_u;
+      k0 = 0;
+      k1 = pl.kb1;
+      next_u += pl.G;
+      return true;
+    }
+  };
+  // CTAs that compute unit u: [first, last], in K order
+  __device__ void ctas(int u, int& first, int& last) const {
+    if (sp) {
+      first = u * sp;
+      last = first + sp - 1;
+    } else {
+      first = last = u % G;
+    }
+  }
+  // partial-sum slot of unit u's segment on CTA b (units split over CTAs only)
+  __device__ int slot(int u, int b) const { return b; }
+};
+
 struct DecodeParams {
   int T, k, E, I, H;
   int nf1, nf2;          // feature tiles of 128: ceil(I / 128), ceil(H / 128)
   int kb1, kb2;          // K blocks of 128 bytes: gate_up (H), down (I)
-  int splits1;           // K splits of the gate_up phase
   int max_tiles;         // tiles reserved in h: min(E, T * k)
   uint32_t idesc;        // M = 128, N = 16
   const int32_t* ids;    // [T, k]
   const float* wts;      // [T, k]
   void* h;               // [max_tiles][16][I], x dtype
-  float* partial;        // splits1 > 1: [max_tiles * nf1][splits1][2][128][16]
-  unsigned long long* split_cnt;  // splits1 > 1: [max_tiles * nf1][4] tagged counts (never cleared)
+  float* partial;        // [grid][2][128][16] partial sums of units split over several CTAs
+  unsigned long long* split_cnt;  // [max_tiles * nf1][4] tagged counts (never cleared)
   unsigned int* h_ready;          // [max_tiles] finished (feature tile, warp) groups of h, cleared in phase 0
   float* y32;            // [T, H]
   int32_t* conv_cnt;     // [T][nf2 * 4] adds per (token, 32-feature group)
@@ -165,14 +219,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   uint64_t* drain = tempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  int* s_A = reinterpret_cast<int*>(tmem_slot + 2);                // number of active experts
   unsigned int* s_gen = reinterpret_cast<unsigned int*>(tmem_slot + 3);  // launch generation
   // routing tables (phase 0)
   int32_t* s_act = reinterpret_cast<int32_t*>(smem + DK_STAGES * DK_STAGE + 256);  // [128] expert of tile m
   int32_t* s_ids = s_act + kDecodeMaxSlots;                                          // [128] slot ids
   float* s_w = reinterpret_cast<float*>(s_ids + kDecodeMaxSlots);                    // [128] slot weights
-  int* s_first = reinterpret_cast<int*>(s_w + kDecodeMaxSlots);                      // [128] first slot of its id
-  int* s_kd = s_first + kDecodeMaxSlots;                                             // [16] distinct experts per token
+  int* s_key = reinterpret_cast<int*>(s_w + kDecodeMaxSlots);                        // [128] expert id of a first slot
+  int* s_kd = s_key + kDecodeMaxSlots;                                             // [16] distinct experts per token
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -213,38 +266,44 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   }
   __syncthreads();
   // slot s is the first of its expert if no earlier slot has the same valid
-  // id; its tile = number of distinct valid ids smaller than its id
+  // id (its key: the id; other slots: a key above every id); its tile = the
+  // number of keys below its id. Slot tables are read four at a time.
   if (threadIdx.x < kDecodeMaxSlots) {
     const int s = threadIdx.x, id = s_ids[s];
     bool first = id >= 0 && id < p.E;
-    for (int j = 0; first && j < s; ++j) first = s_ids[j] != id;
-    s_first[s] = first;
+    const int4* v = reinterpret_cast<const int4*>(s_ids);
+    for (int j4 = 0; first && 4 * j4 < s; ++j4) {  // the earlier slots
+      const int4 q = v[j4];
+      const int j = 4 * j4;
+      first = !((q.x == id) | ((q.y == id) & (j + 1 < s)) | ((q.z == id) & (j + 2 < s)) | ((q.w == id) & (j + 3 < s)));
+    }
+    s_key[s] = first ? id : 0x7FFFFFFF;
   }
-  __syncthreads();
-  if (threadIdx.x < S && s_first[threadIdx.x]) {
-    const int id = s_ids[threadIdx.x];
-    int rank = 0;
-    for (int j = 0; j < S; ++j) rank += s_first[j] && s_ids[j] < id;
-    s_act[rank] = id;
-  }
-  if (threadIdx.x == 0) {
-    int a = 0;
-    for (int j = 0; j < S; ++j) a += s_first[j];
-    *s_A = a;
-    // read once per CTA, before any of its threads arrives on the counter
+  if (threadIdx.x == 0)  // read once per CTA, before any of its threads arrives on the counter
     *s_gen = *(volatile unsigned int*)&g_decode_bar_gen;
+  __syncthreads();
+  int is_first = 0;
+  if (threadIdx.x < S && s_key[threadIdx.x] != 0x7FFFFFFF) {
+    const int key = s_key[threadIdx.x];
+    const int4* f = reinterpret_cast<const int4*>(s_key);
+    int rank = 0;
+    for (int j4 = 0; 4 * j4 < S; ++j4) {
+      const int4 q = f[j4];
+      rank += (q.x < key) + (q.y < key) + (q.z < key) + (q.w < key);
+    }
+    s_act[rank] = key;
+    is_first = 1;
   }
   ptx::tc_fence_before();
-  __syncthreads();
+  const int A = __syncthreads_count(is_first);  // active experts (also the barrier for s_act)
   ptx::tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  const int A = *s_A;
   // this launch's tag for the tagged counts: the launch generation, the same
   // for every CTA of the launch, different for every launch
   const unsigned int gen = *s_gen;
   const unsigned long long tag = ((unsigned long long)gen << 32) | 0x9e370000ull;
   const unsigned int h_total = (unsigned int)p.nf1 * 4;  // (feature tile, warp) groups of one tile's h
-  const int items1 = A * p.nf1 * p.splits1;
+  const P1Plan plan1(A * p.nf1, p.kb1, (int)gridDim.x);
   const int items2 = A * p.nf2;
   const int stages2 = (p.kb2 + 1) / 2;                        // two w2 K blocks per stage
 
@@ -264,11 +323,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
       };
       // phase 1: gate + up weight tiles and the x box of each K block
-      for (int it = blockIdx.x; ok && it < items1; it += gridDim.x) {
-        const int m = it / (p.nf1 * p.splits1), rem = it % (p.nf1 * p.splits1);
-        const int f = rem / p.splits1, s = rem % p.splits1;
+      P1Plan::Iter seg1(plan1, blockIdx.x);
+      int u1, kb0, kb1;
+      while (ok && seg1.next(u1, kb0, kb1)) {
+        const int m = u1 / p.nf1, f = u1 % p.nf1;
         const int e = s_act[m];
-        const int kb0 = s * p.kb1 / p.splits1, kb1 = (s + 1) * p.kb1 / p.splits1;  // balanced, non-empty
         const int wrow = e * 2 * p.I + f * SW_FEAT;
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!ptx::mbar_wait(&empty[stage], phase ^ 1, abort_flag)) {
@@ -384,10 +443,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       uint32_t phase = 0;
       int it = 0;
       bool ok = true;
-      for (int i1 = blockIdx.x; ok && i1 < items1; i1 += gridDim.x, ++it) {
-        const int rem = i1 % (p.nf1 * p.splits1);
-        const int s = rem % p.splits1;
-        const int kb0 = s * p.kb1 / p.splits1, kb1 = (s + 1) * p.kb1 / p.splits1;  // balanced, non-empty
+      P1Plan::Iter seg1(plan1, blockIdx.x);
+      int u1, kb0, kb1;
+      for (; ok && seg1.next(u1, kb0, kb1); ++it) {
         const int buf = it & 1;
         if (!ptx::mbar_wait(&tempty[buf], ((it >> 1) & 1) ^ 1, abort_flag)) {
           ok = false;
@@ -494,9 +552,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     bool ok = true;
     bool cleared = false;  // (lane 0) every CTA's phase-0 clears are done
     int it = 0;
-    for (int i1 = blockIdx.x; i1 < items1; i1 += gridDim.x, ++it) {
-      const int m = i1 / (p.nf1 * p.splits1), rem = i1 % (p.nf1 * p.splits1);
-      const int f = rem / p.splits1, s = rem % p.splits1;
+    P1Plan::Iter seg1(plan1, blockIdx.x);
+    int u1, kb0, kb1;
+    for (; seg1.next(u1, kb0, kb1); ++it) {
+      const int m = u1 / p.nf1, f = u1 % p.nf1;
+      int b_first, b_last;
+      plan1.ctas(u1, b_first, b_last);
       const int buf = it & 1;
       const bool w_ok = ptx::mbar_wait(&tfull[buf], (it >> 1) & 1, abort_flag);
       if (!__all_sync(0xffffffffu, w_ok)) {
@@ -513,11 +574,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       ptx::mbar_arrive(&tempty[buf]);
       const int feat = f * SW_FEAT + fit;
       const bool feat_ok = feat < p.I;
-      if (p.splits1 > 1) {
-        const int unit = m * p.nf1 + f;
-        constexpr size_t kSplit = 2 * SW_FEAT * kDecodeMaxTokens;  // floats per split slot
-        const float* slot0 = p.partial + (size_t)unit * p.splits1 * kSplit;
-        float* mine = const_cast<float*>(slot0) + s * kSplit + fit * kDecodeMaxTokens;
+      if (b_last > b_first) {
+        const int unit = u1;
+        constexpr size_t kSplit = 2 * SW_FEAT * kDecodeMaxTokens;  // floats per partial slot
+        float* mine = p.partial + (size_t)plan1.slot(unit, blockIdx.x) * kSplit + fit * kDecodeMaxTokens;
         if (feat_ok) {
 #pragma unroll
           for (int j = 0; j < 16; j += 4) {
@@ -528,12 +588,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                             acc_value<KIND>(u[j + 3]));
           }
         }
-        // the last split of the unit (per warp: its 32 features) adds the
-        // slots in split order and applies SwiGLU
+        // the last segment of the unit to finish (per warp: its 32 features)
+        // adds the partials in K order and applies SwiGLU
         __threadfence();
         __syncwarp();
         int last = 0;
-        if (lane == 0) last = tagged_count_last(&p.split_cnt[unit * 4 + q], tag, (unsigned)p.splits1);
+        if (lane == 0) last = tagged_count_last(&p.split_cnt[unit * 4 + q], tag, (unsigned)(b_last - b_first + 1));
         last = __shfl_sync(0xffffffffu, last, 0);
         if (last < 0) {
           ok = false;
@@ -541,28 +601,32 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
         if (last && feat_ok) {
           __threadfence();
+          const int nseg = b_last - b_first + 1;
           for (int t = 0; t < p.T; ++t) {
-            float gp[kDecodeMaxSplits], up[kDecodeMaxSplits];
-#pragma unroll
-            for (int ss = 0; ss < kDecodeMaxSplits; ++ss) {  // every split's loads in flight at once
-              gp[ss] = 0.f;
-              up[ss] = 0.f;
-              if (ss < p.splits1) {
-                const float* src = slot0 + ss * kSplit + fit * kDecodeMaxTokens + t;
-                gp[ss] = __ldcg(src);
-                up[ss] = __ldcg(src + SW_FEAT * kDecodeMaxTokens);
-              }
-            }
             float gs = 0.f, us = 0.f;
+            for (int j0 = 0; j0 < nseg; j0 += 4) {  // four segments' loads in flight, added in K order
+              float gp[4], up[4];
 #pragma unroll
-            for (int ss = 0; ss < kDecodeMaxSplits; ++ss) {  // added in split order
-              gs += gp[ss];
-              us += up[ss];
+              for (int jj = 0; jj < 4; ++jj) {
+                gp[jj] = 0.f;
+                up[jj] = 0.f;
+                if (j0 + jj < nseg) {
+                  const float* src = p.partial + (size_t)plan1.slot(unit, b_first + j0 + jj) * kSplit +
+                                     fit * kDecodeMaxTokens + t;
+                  gp[jj] = __ldcg(src);
+                  up[jj] = __ldcg(src + SW_FEAT * kDecodeMaxTokens);
+                }
+              }
+#pragma unroll
+              for (int jj = 0; jj < 4; ++jj) {
+                gs += gp[jj];
+                us += up[jj];
+              }
             }
             store1_out(p.h, p.dtype, ((int64_t)m * kDecodeMaxTokens + t) * p.I + feat, silu_mul(gs, us));
           }
         }
-        if (!last) continue;  // the unit's last split stores and counts this warp's features
+        if (!last) continue;  // the unit's last segment stores and counts this warp's features
       } else if (feat_ok) {
 #pragma unroll
         for (int t = 0; t < kDecodeMaxTokens; ++t)
@@ -665,7 +729,7 @@ std::atomic<int> g_decode_fused{1};  // MOE_OPT_DECODE_FUSED
 constexpr size_t kDecodeSmem = 1024 + (size_t)DK_STAGES * DK_STAGE + 256 + 4 * kDecodeMaxSlots * 4 + 16 * 4;
 
 struct DecodeWs {
-  int max_tiles, nf1, nf2, kb1, kb2, splits1;
+  int max_tiles, nf1, nf2, kb1, kb2, grid;  // grid: CTAs of the launch
   size_t h, partial, split_cnt, h_ready, y32, conv_cnt, bytes;
 };
 
@@ -678,9 +742,13 @@ DecodeWs decode_ws(int64_t T, int k, int E, int64_t H, int64_t I, int dtype) {
   w.kb1 = (int)ceil_div(H * es, ROW_BYTES);
   w.kb2 = (int)ceil_div(I * es, ROW_BYTES);
   const int64_t units1 = (int64_t)w.max_tiles * w.nf1, sms = num_sms();
-  w.splits1 = (2 * units1 <= sms)
-                  ? (int)std::max<int64_t>(1, std::min<int64_t>({sms / units1, (int64_t)w.kb1 / 4, kDecodeMaxSplits}))
-                  : 1;
+  // enough CTAs for the gate_up units (K-split while they fill at most half
+  // the SMs, with at most as many splits as the kernel will choose) and the
+  // down items, at most one per SM (all resident)
+  const int64_t sp = (2 * units1 <= sms)
+                         ? std::max<int64_t>(1, std::min<int64_t>({sms / units1, (int64_t)w.kb1 / 4, kDecodeMaxSplits}))
+                         : 1;
+  w.grid = (int)std::min<int64_t>(sms, std::max<int64_t>(units1 * sp, (int64_t)w.max_tiles * w.nf2));
   size_t off = 0;
   auto take = [&](size_t b) {
     const size_t o = off;
@@ -688,8 +756,8 @@ DecodeWs decode_ws(int64_t T, int k, int E, int64_t H, int64_t I, int dtype) {
     return o;
   };
   w.h = take((size_t)w.max_tiles * kDecodeMaxTokens * I * es);
-  w.partial = take(w.splits1 > 1 ? (size_t)units1 * w.splits1 * 2 * SW_FEAT * kDecodeMaxTokens * 4 : 0);
-  w.split_cnt = take(w.splits1 > 1 ? (size_t)units1 * 4 * sizeof(unsigned long long) : 0);
+  w.partial = take((size_t)w.grid * 2 * SW_FEAT * kDecodeMaxTokens * 4);  // one slot per CTA
+  w.split_cnt = take((size_t)units1 * 4 * sizeof(unsigned long long));
   w.h_ready = take((size_t)w.max_tiles * sizeof(unsigned int));
   w.y32 = take((size_t)T * H * 4);
   w.conv_cnt = take((size_t)T * w.nf2 * 4 * sizeof(int32_t));
@@ -735,7 +803,6 @@ int decode_fused(const void* x, int dtype, int64_t T, int64_t H, const void* w13
   p.nf2 = w.nf2;
   p.kb1 = w.kb1;
   p.kb2 = w.kb2;
-  p.splits1 = w.splits1;
   p.max_tiles = w.max_tiles;
   p.idesc = (make_idesc(dtype, SW_FEAT) & ~(0x3Fu << 17)) | ((uint32_t)(kDecodeMaxTokens >> 3) << 17);
   p.ids = topk_ids;
@@ -749,8 +816,7 @@ int decode_fused(const void* x, int dtype, int64_t T, int64_t H, const void* w13
   p.y = y;
   p.dtype = dtype;
   p.clock_slot = g_kernel_clocks_on.load() ? MOE_CLOCK_GATE_UP : -1;
-  const int64_t items1 = (int64_t)w.max_tiles * w.nf1 * w.splits1, items2 = (int64_t)w.max_tiles * w.nf2;
-  const int64_t grid = std::min<int64_t>(num_sms(), std::max(items1, items2));
+  const int64_t grid = w.grid;
   auto kfn = moe_decode_kernel<0>;
   MOE_CUDA_TRY(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kDecodeSmem));
   cudaLaunchConfig_t cfg = {};
