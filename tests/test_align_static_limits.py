@@ -1,7 +1,7 @@
 """Host-side checks of moe_align_static's documented size limit (no GPU: the
 size check rejects a request before any CUDA call, and the workspace query
-is host arithmetic). They keep the limit stated in include/moe_b200.h,
-DESIGN.md and INTEGRATION.md tied to moe_align_workspace_size."""
+is host arithmetic). They keep the limit stated in include/moe_b200.h (and
+the integration notes) tied to moe_align_workspace_size."""
 from mail_b200 import _lib
 
 STATIC_BYTES = 1 << 20  # MOE_ALIGN_STATIC_SCRATCH_BYTES
