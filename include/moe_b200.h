@@ -130,7 +130,11 @@ typedef enum {
                                SwiGLU, down GEMM + combine and output conversion as phases whose CTAs
                                hand results on through counters. Its launch counter lives in the library's
                                device memory, so two such calls must not run concurrently on one GPU
-                               (different streams); callers that overlap MoE calls on several streams set 0 */
+                               (different streams); callers that overlap MoE calls on several streams set 0.
+                               With 1 a batch whose gate_up work is split along K runs as clusters of the
+                               split CTAs, which add their partial sums through distributed shared memory
+                               (when every cluster of the grid can be resident at once); 2: the same kernel
+                               without clusters, partial sums through global memory */
 } moe_option_t;
 MOE_API int moe_set_option(int option, int value);
 /* Current value of an option, or -1 for an unknown option. */

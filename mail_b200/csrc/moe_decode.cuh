@@ -64,6 +64,9 @@ constexpr int DK_STAGE_B = 2 * kDecodeMaxTokens * ROW_BYTES;  // 4 KB: token box
 constexpr int DK_STAGE = DK_STAGE_A + DK_STAGE_B;
 constexpr int DK_STAGES = 6;
 constexpr int DK_TMEM_COLS = 64;                           // 2 buffers x (gate 16 + up 16) columns
+// cluster K-split reduction: the leader CTA's buffer for the other splits'
+// gate and up sums, [split - 1][128 features][2][T] floats
+constexpr int kDecodeRedBytes = 6144;
 
 __device__ unsigned int g_decode_bar_count = 0;
 __device__ unsigned int g_decode_bar_gen = 0;
@@ -145,8 +148,11 @@ __device__ __forceinline__ void fence_proxy_async_global() {
 // CTA.
 struct P1Plan {
   int sp, kb1, units, G;
-  __device__ P1Plan(int units_, int kb1_, int G_) : kb1(kb1_), units(units_), G(G_) {
-    if (2 * units <= G && units > 0) sp = max(1, min(min(G / units, kDecodeMaxSplits), kb1 / 4));
+  // sp_fixed > 0: that split count (the cluster size of a cluster launch,
+  // where each cluster holds one unit's splits)
+  __device__ P1Plan(int units_, int kb1_, int G_, int sp_fixed) : kb1(kb1_), units(units_), G(G_) {
+    if (sp_fixed > 0) sp = sp_fixed;
+    else if (2 * units <= G && units > 0) sp = max(1, min(min(G / units, kDecodeMaxSplits), kb1 / 4));
     else sp = units <= G ? 1 : 0;
   }
   // segments (unit, K blocks [k0, k1)) of CTA b, in order
@@ -202,6 +208,8 @@ struct DecodeParams {
   void* y;               // [T, H], x dtype
   int dtype;             // MOE_BF16 or MOE_F16
   int clock_slot;
+  int cluster_sp;        // > 0: launched as clusters of this many CTAs, each one gate_up unit's K splits,
+                         // reduced through the leader's shared memory
 };
 
 template <int KIND>
@@ -226,6 +234,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   float* s_w = reinterpret_cast<float*>(s_ids + kDecodeMaxSlots);                    // [128] slot weights
   int* s_key = reinterpret_cast<int*>(s_w + kDecodeMaxSlots);                        // [128] expert id of a first slot
   int* s_kd = s_key + kDecodeMaxSlots;                                             // [16] distinct experts per token
+  float* s_red = reinterpret_cast<float*>(s_kd + 16);                                // cluster reduction buffer
+  uint64_t* red_bar = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(s_red) + kDecodeRedBytes);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -242,6 +252,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       ptx::mbar_init(&tempty[a], 4 * 32);
     }
     ptx::mbar_init(drain, 1);
+    // cluster launch: one arrival per epilogue warp of every other split
+    if (p.cluster_sp > 0) ptx::mbar_init(red_bar, 4 * (p.cluster_sp - 1));
     *abort_flag = 0;
     ptx::fence_mbar_init();
   }
@@ -296,6 +308,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   }
   ptx::tc_fence_before();
   const int A = __syncthreads_count(is_first);  // active experts (also the barrier for s_act)
+  // cluster launch: every CTA's reduction barrier is initialised before any
+  // peer arrives on it (the epilogue warps wait before phase 1, the others
+  // at the end)
+  if (p.cluster_sp > 0) ptx::cluster_arrive();
   ptx::tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   // this launch's tag for the tagged counts: the launch generation, the same
@@ -303,7 +319,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const unsigned int gen = *s_gen;
   const unsigned long long tag = ((unsigned long long)gen << 32) | 0x9e370000ull;
   const unsigned int h_total = (unsigned int)p.nf1 * 4;  // (feature tile, warp) groups of one tile's h
-  const P1Plan plan1(A * p.nf1, p.kb1, (int)gridDim.x);
+  const P1Plan plan1(A * p.nf1, p.kb1, (int)gridDim.x, p.cluster_sp);
   const int items2 = A * p.nf2;
   const int stages2 = (p.kb2 + 1) / 2;                        // two w2 K blocks per stage
 
@@ -551,6 +567,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           store1_out(p.y, p.dtype, (int64_t)t * p.H + i, 0.f);
     bool ok = true;
     bool cleared = false;  // (lane 0) every CTA's phase-0 clears are done
+    if (p.cluster_sp > 0) ptx::cluster_wait();  // the cluster's reduction barriers exist
     int it = 0;
     P1Plan::Iter seg1(plan1, blockIdx.x);
     int u1, kb0, kb1;
@@ -574,7 +591,46 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       ptx::mbar_arrive(&tempty[buf]);
       const int feat = f * SW_FEAT + fit;
       const bool feat_ok = feat < p.I;
-      if (b_last > b_first) {
+      if (b_last > b_first && p.cluster_sp > 0) {
+        // the unit's K splits are the CTAs of this cluster: the others send
+        // their sums to the leader's shared memory, the leader adds them in
+        // split order, applies SwiGLU and stores and counts the features
+        const uint32_t crank = ptx::cluster_ctarank();
+        if (crank > 0) {
+          const uint32_t base = ptx::mapa(ptx::smem_u32(s_red), 0);
+          const int slot = ((int)(crank - 1) * 128 + fit) * 2 * p.T;
+#pragma unroll
+          for (int t = 0; t < kDecodeMaxTokens; ++t) {
+            if (t < p.T) {
+              ptx::st_cluster_f32(base + 4u * (uint32_t)(slot + t), acc_value<KIND>(g[t]));
+              ptx::st_cluster_f32(base + 4u * (uint32_t)(slot + p.T + t), acc_value<KIND>(u[t]));
+            }
+          }
+          __syncwarp();
+          if (lane == 0) ptx::mbar_arrive_cluster(ptx::mapa(ptx::smem_u32(red_bar), 0));
+          continue;
+        }
+        const bool r_ok = ptx::mbar_wait_cluster(red_bar, 0, abort_flag);
+        if (!__all_sync(0xffffffffu, r_ok)) {
+          if (lane == 0) raise_device_error(7);
+          ok = false;
+          break;
+        }
+        if (feat_ok) {
+#pragma unroll
+          for (int t = 0; t < kDecodeMaxTokens; ++t) {
+            if (t < p.T) {
+              float gs = acc_value<KIND>(g[t]), us = acc_value<KIND>(u[t]);
+              for (int s2 = 1; s2 < p.cluster_sp; ++s2) {
+                const int slot = ((s2 - 1) * 128 + fit) * 2 * p.T;
+                gs += s_red[slot + t];
+                us += s_red[slot + p.T + t];
+              }
+              store1_out(p.h, p.dtype, ((int64_t)m * kDecodeMaxTokens + t) * p.I + feat, silu_mul(gs, us));
+            }
+          }
+        }
+      } else if (b_last > b_first) {
         const int unit = u1;
         constexpr size_t kSplit = 2 * SW_FEAT * kDecodeMaxTokens;  // floats per partial slot
         float* mine = p.partial + (size_t)plan1.slot(unit, blockIdx.x) * kSplit + fit * kDecodeMaxTokens;
@@ -715,6 +771,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
   __syncthreads();
   clock_end(clk);
+  if (p.cluster_sp > 0) {
+    if (warp < 2) ptx::cluster_wait();  // the producer and MMA warps' wait on the barrier after phase 0
+    ptx::cluster_sync();                // no CTA leaves while a peer may still write its shared memory
+  }
   if (warp == 1) {
     __syncwarp();
     ptx::tc_fence_after();
@@ -726,10 +786,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
 std::atomic<int> g_decode_fused{1};  // MOE_OPT_DECODE_FUSED
 
-constexpr size_t kDecodeSmem = 1024 + (size_t)DK_STAGES * DK_STAGE + 256 + 4 * kDecodeMaxSlots * 4 + 16 * 4;
+constexpr size_t kDecodeSmem =
+    1024 + (size_t)DK_STAGES * DK_STAGE + 256 + 4 * kDecodeMaxSlots * 4 + 16 * 4 + kDecodeRedBytes + 16;
 
 struct DecodeWs {
   int max_tiles, nf1, nf2, kb1, kb2, grid;  // grid: CTAs of the launch
+  int sp1;  // gate_up K splits when every routed expert is distinct
   size_t h, partial, split_cnt, h_ready, y32, conv_cnt, bytes;
 };
 
@@ -749,6 +811,7 @@ DecodeWs decode_ws(int64_t T, int k, int E, int64_t H, int64_t I, int dtype) {
                          ? std::max<int64_t>(1, std::min<int64_t>({sms / units1, (int64_t)w.kb1 / 4, kDecodeMaxSplits}))
                          : 1;
   w.grid = (int)std::min<int64_t>(sms, std::max<int64_t>(units1 * sp, (int64_t)w.max_tiles * w.nf2));
+  w.sp1 = (int)sp;
   size_t off = 0;
   auto take = [&](size_t b) {
     const size_t o = off;
@@ -816,21 +879,66 @@ int decode_fused(const void* x, int dtype, int64_t T, int64_t H, const void* w13
   p.y = y;
   p.dtype = dtype;
   p.clock_slot = g_kernel_clocks_on.load() ? MOE_CLOCK_GATE_UP : -1;
-  const int64_t grid = w.grid;
+  int64_t grid = w.grid;
   auto kfn = moe_decode_kernel<0>;
   MOE_CUDA_TRY(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kDecodeSmem));
+  // K-split gate_up units reduce through distributed shared memory when each
+  // unit's splits can form one cluster, the other splits' sums fit the
+  // leader's buffer and every cluster of the grid can be resident at once
+  // (the kernel's CTAs wait on one another). The split count is the largest,
+  // up to the one without clusters, whose clusters all fit: at one token of
+  // the Qwen3 layer 48 units need 48 clusters, three-CTA clusters fit 45 at
+  // once and two-CTA clusters 74, so it runs two splits per unit (measured
+  // 27.6 vs 28.5 µs for three splits reduced through global memory).
+  int cluster = 0;
+  const int64_t sms = num_sms(), units_ub = (int64_t)w.max_tiles * w.nf1, items2_ub = (int64_t)w.max_tiles * w.nf2;
+  for (int spc = (g_decode_fused.load() == 1) ? w.sp1 : 0; spc >= 2 && !cluster; --spc) {
+    if ((int64_t)(spc - 1) * T * 128 * 2 * 4 > kDecodeRedBytes) continue;
+    const int64_t gc = ceil_div(std::min<int64_t>(sms, std::max<int64_t>(units_ub * spc, items2_ub)), (int64_t)spc) * spc;
+    if (gc > sms) continue;
+    cudaLaunchConfig_t occ = {};
+    cudaLaunchAttribute ca[1];
+    occ.gridDim = dim3((unsigned)gc);
+    occ.blockDim = dim3(NUM_THREADS);
+    occ.dynamicSmemBytes = kDecodeSmem;
+    ca[0].id = cudaLaunchAttributeClusterDimension;
+    ca[0].val.clusterDim.x = (unsigned)spc;
+    ca[0].val.clusterDim.y = 1;
+    ca[0].val.clusterDim.z = 1;
+    occ.attrs = ca;
+    occ.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kfn, &occ) != cudaSuccess) {
+      (void)cudaGetLastError();  // not fatal: the launch runs without clusters
+      break;
+    }
+    if ((int64_t)n * spc >= gc) {
+      cluster = spc;
+      grid = gc;
+    }
+  }
+  p.cluster_sp = cluster;
   cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
+  int na = 0;
   cfg.gridDim = dim3((unsigned)grid);
   cfg.blockDim = dim3(NUM_THREADS);
   cfg.dynamicSmemBytes = kDecodeSmem;
   cfg.stream = st;
   if (pdl_enabled()) {
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
   }
+  if (cluster) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = (unsigned)cluster;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = 1;
+    ++na;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
   MOE_CUDA_TRY(cudaLaunchKernelEx(&cfg, kfn, t13, t2, tx, th, p));
   MOE_LAUNCH_CHECK("moe_decode_kernel");
   return MOE_OK;

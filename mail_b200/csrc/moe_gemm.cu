@@ -1274,7 +1274,8 @@ extern "C" int moe_set_option(int option, int value) {
     return MOE_OK;
   }
   if (option == MOE_OPT_DECODE_FUSED) {
-    g_decode_fused.store(value != 0);
+    MOE_CHECK_ARG(value >= 0 && value <= 2, "moe_set_option: DECODE_FUSED takes 0, 1 or 2");
+    g_decode_fused.store(value);
     return MOE_OK;
   }
   if (option == MOE_OPT_GEMM_BAND_DOWN) {

@@ -37,7 +37,7 @@ def layer(T, H, I, E, dtype, seed):
 def run(x, w13, w2, ids, wts, fused=True):
     lib = _lib.load()
     old = lib.moe_get_option(_lib.OPT_DECODE_FUSED)
-    lib.moe_set_option(_lib.OPT_DECODE_FUSED, int(fused))
+    assert lib.moe_set_option(_lib.OPT_DECODE_FUSED, int(fused)) == 0
     try:
         before = lib.moe_launch_count()
         y = mb.fused_moe_mlp(x, w13, w2, torch.from_numpy(wts).to(dev()), torch.from_numpy(ids).to(dev()))
@@ -91,6 +91,34 @@ def test_dropped_and_repeated_ids():
     yf = y.float().cpu().numpy()
     assert (yf[[0, 9]] == 0).all()
     assert max_abs_rel(yf, oracle(x, w13, w2, ids, wts, torch.bfloat16)) < TOL
+    assert mb.device_error(dev()) == 0
+
+
+@pytest.mark.parametrize("mode", [1, 2])
+@pytest.mark.parametrize("distinct", [0, 1, 2, 3, 5, 8])
+def test_one_token_few_experts(distinct, mode):
+    """One token whose eight slots name only a few distinct experts (repeated
+    ids; none valid for distinct = 0). Mode 1: the gate_up K splits of a
+    feature tile run as one cluster and add their sums through the leader's
+    shared memory; mode 2: no clusters, the split count follows the experts
+    actually routed (up to 8 CTAs per feature tile), sums through global
+    memory. Both add the splits in K order."""
+    T, H, I, E, k = 1, 2048, 768, 128, 8
+    x, w13, w2 = layer(T, H, I, E, torch.bfloat16, 40 + distinct)
+    rng = np.random.default_rng(distinct)
+    experts = rng.choice(E, size=max(distinct, 1), replace=False)
+    ids = np.array([[experts[j % len(experts)] for j in range(k)]], dtype=np.int32)
+    if distinct == 0:
+        ids[:] = -1
+    wts = rng.random((1, k)).astype(np.float32)
+    wts /= wts.sum()
+    y, launches = run(x, w13, w2, ids, wts, fused=mode)
+    assert launches == 1
+    yf = y.float().cpu().numpy()
+    if distinct == 0:
+        assert (yf == 0).all()
+    else:
+        assert max_abs_rel(yf, oracle(x, w13, w2, ids, wts, torch.bfloat16)) < TOL
     assert mb.device_error(dev()) == 0
 
 
