@@ -341,6 +341,22 @@ MOE_API int moe_fused_experts(const void* x, int x_dtype, int64_t num_tokens, in
                       const int32_t* topk_ids, int top_k, const float* w13_scale, const float* w2_scale,
                       void* y, void* workspace, size_t workspace_bytes, void* stream);
 
+/* moe_fused_experts_from_logits — routing and the layer in one call (no
+ * reference counterpart: the reference's callers route with an external op).
+ * The router of moe_route_topk (same selection, tie rule and weights) turns
+ * router_logits [T, E] (fp32/bf16/fp16) into topk_ids [T, k] and topk_weights
+ * [T, k], both written as outputs, and moe_fused_experts runs on them. A batch
+ * that takes the one-launch decode kernel (MOE_OPT_DECODE_FUSED) with
+ * E <= 256 routes inside that kernel's first phase, so the whole layer,
+ * routing included, is one launch; other batches launch the router first.
+ * Workspace: moe_fused_experts_workspace_size with the same sizes. */
+MOE_API int moe_fused_experts_from_logits(const void* x, int x_dtype, int64_t num_tokens, int64_t hidden,
+                                          const void* w13, const void* w2, int w_dtype, int num_experts,
+                                          int64_t inter, const void* router_logits, int logits_dtype, int top_k,
+                                          int scoring, int renormalize, int32_t* topk_ids, float* topk_weights,
+                                          const float* w13_scale, const float* w2_scale, void* y, void* workspace,
+                                          size_t workspace_bytes, void* stream);
+
 /* moe_fused_expert_rows — the expert MLP applied row by row, with no routing
  * weights and no combine: out[r] = MLP_{expert_ids[r]}(x[r]) for r < rows,
  * in x_dtype (rows whose id is outside [0, E) are left unwritten). This is

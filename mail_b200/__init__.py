@@ -9,6 +9,7 @@ from .moe import (
     device_error,
     fused_expert_rows,
     fused_moe_mlp,
+    fused_moe_mlp_from_logits,
     gather_rows,
     kmajor,
     moe_align,
@@ -21,7 +22,8 @@ from .moe import (
 )
 
 __all__ = [
-    "BLOCK_M", "CapturedMoeMLP", "MoeError", "build_tile_schedule", "device_error", "fused_expert_rows", "fused_moe_mlp", "gather_rows", "kmajor",
+    "BLOCK_M", "CapturedMoeMLP", "MoeError", "build_tile_schedule", "device_error", "fused_expert_rows", "fused_moe_mlp",
+    "fused_moe_mlp_from_logits", "gather_rows", "kmajor",
     "load_library", "moe_align", "prepack_weights", "quant_int8_rows", "quantize_weights_int8", "route_topk",
     "weights_from_checkpoint", "weights_from_linear",
 ]

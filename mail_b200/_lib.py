@@ -55,6 +55,8 @@ SIGNATURES = {
     "moe_fused_mlp": (_i, [_p, _i, _i64, _i64, _p, _p, _i, _i64, _p, _i, _i, _p, _p, _sz, _p]),
     "moe_fused_experts_workspace_size": (_sz, [_i64, _i64, _i64, _i, _i, _i, _i]),
     "moe_fused_experts": (_i, [_p, _i, _i64, _i64, _p, _p, _i, _i, _i64, _p, _p, _i, _p, _p, _p, _p, _sz, _p]),
+    "moe_fused_experts_from_logits": (_i, [_p, _i, _i64, _i64, _p, _p, _i, _i, _i64, _p, _i, _i, _i, _i, _p, _p, _p,
+                                           _p, _p, _p, _sz, _p]),
     "moe_ipc_malloc": (_i, [_sz, _p, _p]),
     "moe_ipc_open": (_i, [_p, _p]),
     "moe_ipc_close": (_i, [_p]),

@@ -239,9 +239,20 @@ int prep_small(const int32_t* topk_ids, int64_t num_tokens, int top_k, int num_e
 // conversion, separated by device-wide barriers (MOE_OPT_DECODE_FUSED).
 bool decode_fused_fits(int64_t T, int k, int E, int64_t H, int64_t I, int x_dtype, int w_dtype);
 size_t decode_fused_workspace(int64_t T, int k, int E, int64_t H, int64_t I, int dtype);
+// Routing inside the one-launch kernel: the router logits [T, E] in, the
+// top-k ids and weights [T, k] out (decode_fused's topk_weights / topk_ids
+// are then not read).
+struct DecodeRouting {
+  const void* logits;
+  int dtype;  // MOE_F32, MOE_BF16 or MOE_F16
+  int sigmoid, renormalize;
+  int32_t* ids_out;
+  float* wts_out;
+};
+bool decode_route_fits(int E, int k, int logits_dtype);
 int decode_fused(const void* x, int dtype, int64_t T, int64_t H, const void* w13, const void* w2, int E, int64_t I,
                  const float* topk_weights, const int32_t* topk_ids, int k, void* y, void* workspace,
-                 size_t workspace_bytes, cudaStream_t st);
+                 size_t workspace_bytes, cudaStream_t st, const DecodeRouting* route = nullptr);
 
 // Token-order scatter of the routed rows (+ per-token int8 quantisation):
 // dst[slot_pos[t * k + j]] = row t of src, each row read once (moe_rows.cu).

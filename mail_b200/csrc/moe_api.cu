@@ -357,6 +357,41 @@ extern "C" int moe_fused_experts(const void* x, int x_dtype, int64_t num_tokens,
   return run_experts(a);
 }
 
+extern "C" int moe_fused_experts_from_logits(const void* x, int x_dtype, int64_t num_tokens, int64_t hidden,
+                                             const void* w13, const void* w2, int w_dtype, int num_experts,
+                                             int64_t inter, const void* router_logits, int logits_dtype, int top_k,
+                                             int scoring, int renormalize, int32_t* topk_ids, float* topk_weights,
+                                             const float* w13_scale, const float* w2_scale, void* y,
+                                             void* workspace, size_t workspace_bytes, void* stream) {
+  ExpertsArgs a{x, x_dtype, num_tokens, hidden, w13, w2, w_dtype, num_experts, inter, topk_weights, topk_ids,
+                top_k, w13_scale, w2_scale, y, workspace, workspace_bytes, stream,
+                combine_mode(num_tokens, hidden), "moe_fused_experts_from_logits"};
+  MOE_TRY(check_experts(a));
+  MOE_CHECK_ARG(logits_dtype == MOE_F32 || logits_dtype == MOE_BF16 || logits_dtype == MOE_F16,
+                "moe_fused_experts_from_logits: logits dtype must be fp32, bf16 or fp16");
+  MOE_CHECK_ARG(scoring == MOE_SCORE_SOFTMAX || scoring == MOE_SCORE_SIGMOID,
+                "moe_fused_experts_from_logits: bad scoring %d", scoring);
+  MOE_CHECK_ARG(top_k <= 32 && top_k <= num_experts, "moe_fused_experts_from_logits: top_k %d outside [1, min(E, 32)]",
+                top_k);
+  if (num_tokens == 0) return MOE_OK;
+  MOE_CHECK_ARG(router_logits && topk_ids && topk_weights, "moe_fused_experts_from_logits: NULL pointer");
+  if (one_launch(a) && decode_route_fits(num_experts, top_k, logits_dtype)) {
+    // routing is phase 0 of the one-launch kernel
+    cudaStream_t st = as_stream(stream);
+    const DecodeRouting route{router_logits, logits_dtype, scoring == MOE_SCORE_SIGMOID, renormalize != 0,
+                              topk_ids, topk_weights};
+    MOE_CHECK_ARG(a.x && a.w13 && a.w2, "moe_fused_experts_from_logits: NULL input");
+    MOE_TRY(record_stage(MOE_STAGE_ENTRY, st));
+    MOE_TRY(decode_fused(x, x_dtype, num_tokens, hidden, w13, w2, num_experts, inter, nullptr, nullptr, top_k, y,
+                         workspace, workspace_bytes, st, &route));
+    for (int s = MOE_STAGE_ROUTED; s <= MOE_STAGE_DONE; ++s) MOE_TRY(record_stage(s, st));
+    return MOE_OK;
+  }
+  MOE_TRY(moe_route_topk(router_logits, logits_dtype, num_tokens, num_experts, top_k, scoring, renormalize, topk_ids,
+                         topk_weights, stream));
+  return run_experts(a);
+}
+
 extern "C" size_t moe_fused_expert_rows_workspace_size(int64_t rows, int64_t hidden, int64_t inter, int num_experts,
                                                        int x_dtype, int w_dtype) {
   if (rows < 0 || hidden <= 0 || inter <= 0 || num_experts <= 0) return 0;

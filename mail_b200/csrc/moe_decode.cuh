@@ -7,7 +7,9 @@
 // conversion — run as phases of one persistent kernel, one CTA per SM:
 //
 //   phase 0  every CTA reads the top-k ids and weights (at most 128 slots)
-//            and derives the active experts (distinct valid ids in increasing
+//            — or, given the router logits, routes the tokens itself, one
+//            warp per token (route.cuh; CTA 0 writes the ids and weights
+//            out) — and derives the active experts (distinct valid ids in increasing
 //            order; expert tile m = the m-th of them) and, per (tile, token),
 //            the token's summed routing weight for that expert; its share of
 //            the fp32 output accumulator, the group counts and the readiness
@@ -53,11 +55,14 @@
 // out latches device error 7, and moe_get_device_error() resets the launch
 // counter after any error. Two such launches must not overlap on one GPU
 // (different streams).
+#include "route.cuh"
+
 namespace moe {
 namespace {
 
 constexpr int kDecodeMaxTokens = 16;
 constexpr int kDecodeMaxSlots = 128;
+constexpr int kDecodeRouteMaxExperts = 256;  // routing in phase 0: 8 logits per lane
 constexpr int kDecodeMaxSplits = 8;  // K splits of the gate_up phase
 constexpr int DK_STAGE_A = 2 * SW_A_TILE;                  // 32 KB: gate + up tiles, or two w2 K blocks
 constexpr int DK_STAGE_B = 2 * kDecodeMaxTokens * ROW_BYTES;  // 4 KB: token boxes for the A tiles
@@ -210,6 +215,13 @@ struct DecodeParams {
   int clock_slot;
   int cluster_sp;        // > 0: launched as clusters of this many CTAs, each one gate_up unit's K splits,
                          // reduced through the leader's shared memory
+  // routing in phase 0 (logits != nullptr; ids / wts unused): CTA 0
+  // writes the routing to ids_out / wts_out
+  const void* logits;    // [T, E] router logits
+  int logits_dtype;      // MOE_F32, MOE_BF16 or MOE_F16
+  int sigmoid, renormalize;
+  int32_t* ids_out;      // [T, k]
+  float* wts_out;        // [T, k]
 };
 
 template <int KIND>
@@ -272,9 +284,38 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   }
 
   // ---------------------------------------------------------------- phase 0: routing
-  for (int s = threadIdx.x; s < kDecodeMaxSlots; s += blockDim.x) {
-    s_ids[s] = s < S ? p.ids[s] : -1;
-    s_w[s] = s < S ? p.wts[s] : 0.f;
+  if (p.logits == nullptr) {
+    for (int s = threadIdx.x; s < kDecodeMaxSlots; s += blockDim.x) {
+      s_ids[s] = s < S ? p.ids[s] : -1;
+      s_w[s] = s < S ? p.wts[s] : 0.f;
+    }
+  } else {
+    for (int s = S + threadIdx.x; s < kDecodeMaxSlots; s += blockDim.x) {
+      s_ids[s] = -1;
+      s_w[s] = 0.f;
+    }
+    for (int t = warp; t < p.T; t += NUM_THREADS / 32) {
+      int id;
+      float wt;
+      const size_t off = (size_t)t * p.E;
+      if (p.logits_dtype == MOE_F32)
+        route_token<float, 8>(static_cast<const float*>(p.logits) + off, p.E, p.k, p.sigmoid, p.renormalize, lane,
+                              id, wt);
+      else if (p.logits_dtype == MOE_BF16)
+        route_token<__nv_bfloat16, 8>(static_cast<const __nv_bfloat16*>(p.logits) + off, p.E, p.k, p.sigmoid,
+                                      p.renormalize, lane, id, wt);
+      else
+        route_token<__half, 8>(static_cast<const __half*>(p.logits) + off, p.E, p.k, p.sigmoid, p.renormalize, lane,
+                               id, wt);
+      if (lane < p.k) {
+        s_ids[t * p.k + lane] = id;
+        s_w[t * p.k + lane] = wt;
+        if (blockIdx.x == 0) {
+          p.ids_out[t * p.k + lane] = id;
+          p.wts_out[t * p.k + lane] = wt;
+        }
+      }
+    }
   }
   __syncthreads();
   // slot s is the first of its expert if no earlier slot has the same valid
@@ -840,11 +881,19 @@ size_t decode_fused_workspace(int64_t T, int k, int E, int64_t H, int64_t I, int
   return decode_ws(T, k, E, H, I, dtype).bytes;
 }
 
+bool decode_route_fits(int E, int k, int logits_dtype) {
+  return E <= kDecodeRouteMaxExperts && k <= 32 &&
+         (logits_dtype == MOE_F32 || logits_dtype == MOE_BF16 || logits_dtype == MOE_F16);
+}
+
 int decode_fused(const void* x, int dtype, int64_t T, int64_t H, const void* w13, const void* w2, int E, int64_t I,
                  const float* topk_weights, const int32_t* topk_ids, int k, void* y, void* workspace,
-                 size_t workspace_bytes, cudaStream_t st) {
+                 size_t workspace_bytes, cudaStream_t st, const DecodeRouting* route) {
   MOE_CHECK_ARG(decode_fused_fits(T, k, E, H, I, dtype, dtype), "decode_fused: batch outside the one-launch path");
-  MOE_CHECK_ARG(x && w13 && w2 && topk_weights && topk_ids && y, "decode_fused: NULL pointer");
+  MOE_CHECK_ARG(x && w13 && w2 && y && (route ? route->logits && route->ids_out && route->wts_out
+                                                : topk_weights && topk_ids),
+                "decode_fused: NULL pointer");
+  MOE_CHECK_ARG(!route || decode_route_fits(E, k, route->dtype), "decode_fused: routing outside the one-launch path");
   MOE_CHECK_ARG((uintptr_t)x % 16 == 0 && (uintptr_t)w13 % 16 == 0 && (uintptr_t)w2 % 16 == 0,
                 "decode_fused: pointers must be 16-byte aligned");
   const DecodeWs w = decode_ws(T, k, E, H, I, dtype);
@@ -879,6 +928,14 @@ int decode_fused(const void* x, int dtype, int64_t T, int64_t H, const void* w13
   p.y = y;
   p.dtype = dtype;
   p.clock_slot = g_kernel_clocks_on.load() ? MOE_CLOCK_GATE_UP : -1;
+  if (route) {
+    p.logits = route->logits;
+    p.logits_dtype = route->dtype;
+    p.sigmoid = route->sigmoid;
+    p.renormalize = route->renormalize;
+    p.ids_out = route->ids_out;
+    p.wts_out = route->wts_out;
+  }
   int64_t grid = w.grid;
   auto kfn = moe_decode_kernel<0>;
   MOE_CUDA_TRY(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kDecodeSmem));

@@ -14,6 +14,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "route.cuh"
 #include "scan.cuh"
 
 namespace moe {
@@ -328,17 +329,9 @@ __global__ void __launch_bounds__(kScanThreads) align_small_kernel(
 }
 
 // ---------------------------------------------------------------------------
-// Router: logits [T, E] -> top-k ids and weights, one warp per token. The k
-// largest logits are selected (softmax and sigmoid are monotonic, so this is
-// the top-k of the scores), ties going to the lower expert id; lane l holds
-// experts l, l+32, ... in registers.
+// Router: logits [T, E] -> top-k ids and weights, one warp per token
+// (route_token in route.cuh: ties to the lower expert id).
 constexpr int kRouteMaxPerLane = 32;  // E <= 1024
-
-template <typename T>
-__device__ __forceinline__ float to_f32(T v) {
-  if constexpr (sizeof(T) == 4) return v;
-  else return static_cast<float>(v);
-}
 
 template <typename T, int PER>
 __global__ void __launch_bounds__(256) route_topk_kernel(const T* __restrict__ logits, int64_t num_tokens, int E,
@@ -349,63 +342,11 @@ __global__ void __launch_bounds__(256) route_topk_kernel(const T* __restrict__ l
   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
   for (int64_t t = warp; t < num_tokens; t += nwarps) {
-    float v[PER];
-    const T* row = logits + t * E;
-#pragma unroll
-    for (int i = 0; i < PER; ++i) {
-      const int e = lane + 32 * i;
-      v[i] = e < E ? to_f32(row[e]) : -INFINITY;
-    }
-    // softmax over all experts needs the maximum and the partition function
-    float m = -INFINITY;
-#pragma unroll
-    for (int i = 0; i < PER; ++i) m = fmaxf(m, v[i]);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    float z = 0.f;
-    if (!sigmoid && !renormalize) {
-#pragma unroll
-      for (int i = 0; i < PER; ++i)
-        if (lane + 32 * i < E) z += expf(v[i] - m);
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) z += __shfl_xor_sync(0xffffffffu, z, o);
-    }
-    unsigned taken = 0u;  // bit i: this lane's expert lane + 32 i already chosen
-    float sel_sum = 0.f, my_score = 0.f;
-    int my_j = -1;
-    for (int j = 0; j < k; ++j) {
-      float best = -INFINITY;
-      int bidx = 0x7fffffff;
-#pragma unroll
-      for (int i = 0; i < PER; ++i) {
-        const int e = lane + 32 * i;
-        if (e < E && !(taken >> i & 1u) && (v[i] > best || (v[i] == best && e < bidx))) {
-          best = v[i];
-          bidx = e;
-        }
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        const float ob = __shfl_xor_sync(0xffffffffu, best, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, bidx, o);
-        if (ob > best || (ob == best && oi < bidx)) {
-          best = ob;
-          bidx = oi;
-        }
-      }
-      if ((bidx & 31) == lane) taken |= 1u << (bidx >> 5);
-      const float score = sigmoid ? 1.0f / (1.0f + expf(-best)) : expf(best - m);
-      sel_sum += score;
-      if (lane == j) {
-        my_j = bidx;
-        my_score = score;
-      }
-    }
+    int id;
+    float w;
+    route_token<T, PER>(logits + t * E, E, k, sigmoid, renormalize, lane, id, w);
     if (lane < k) {
-      float w = my_score;
-      if (renormalize) w = w / sel_sum;
-      else if (!sigmoid) w = w / z;
-      ids[t * k + lane] = my_j;
+      ids[t * k + lane] = id;
       wts[t * k + lane] = w;
     }
   }

@@ -274,6 +274,21 @@ def _prerouted_impl(x, w13, w2, group_sizes):
     return out
 
 
+def _weight_scales(x, w13, w2, w13_scale, w2_scale, E, H, inter):
+    """(w_code, w13_scale, w2_scale) of a top-k call, checked: int8 weights
+    need fp32 scales [E, 2I] and [E, H]; other weights share x's dtype."""
+    s13 = s2 = None
+    if w13.dtype == torch.int8:
+        if w13_scale is None or w2_scale is None:
+            raise ValueError("fused_moe_mlp: int8 weights need scales=(w13_scale, w2_scale)")
+        s13, s2 = w13_scale.to(torch.float32).contiguous(), w2_scale.to(torch.float32).contiguous()
+        if tuple(s13.shape) != (E, 2 * inter) or tuple(s2.shape) != (E, H):
+            raise ValueError("fused_moe_mlp: scales must be w13_scale [E, 2I] and w2_scale [E, H]")
+    elif w13.dtype != x.dtype or w2.dtype != x.dtype:
+        raise TypeError("fused_moe_mlp: weights must share x's dtype or be int8")
+    return _code(w13), s13, s2
+
+
 def _topk_impl(x, w13, w2, topk_weights, topk_ids, w13_scale, w2_scale):
     """moe_fused_experts: align -> GEMMs -> weighted combine."""
     _require_cuda(x, w13, w2, topk_weights, topk_ids)
@@ -286,16 +301,7 @@ def _topk_impl(x, w13, w2, topk_weights, topk_ids, w13_scale, w2_scale):
     if topk_weights.shape != ids.shape or ids.dim() != 2 or ids.shape[0] != T:
         raise ValueError("fused_moe_mlp: topk_weights/topk_ids must both be [T, k]")
     k = ids.shape[1]
-    w_code = _code(w13)
-    s13 = s2 = None
-    if w13.dtype == torch.int8:
-        if w13_scale is None or w2_scale is None:
-            raise ValueError("fused_moe_mlp: int8 weights need scales=(w13_scale, w2_scale)")
-        s13, s2 = w13_scale.to(torch.float32).contiguous(), w2_scale.to(torch.float32).contiguous()
-        if tuple(s13.shape) != (E, 2 * inter) or tuple(s2.shape) != (E, H):
-            raise ValueError("fused_moe_mlp: scales must be w13_scale [E, 2I] and w2_scale [E, H]")
-    elif w13.dtype != x.dtype or w2.dtype != x.dtype:
-        raise TypeError("fused_moe_mlp: weights must share x's dtype or be int8")
+    w_code, s13, s2 = _weight_scales(x, w13, w2, w13_scale, w2_scale, E, H, inter)
     y = torch.empty((T, H), dtype=x.dtype, device=dev)
     ws = _workspace(_lib.query("moe_fused_experts_workspace_size", T, H, inter, E, k, _code(x), w_code), dev)
     _lib.call("moe_fused_experts", x.data_ptr(), _code(x), T, H, w13k.data_ptr(), w2k.data_ptr(), w_code, E, inter,
@@ -369,6 +375,37 @@ def fused_moe_mlp(x: torch.Tensor, w13: torch.Tensor, w2: torch.Tensor, group_si
     if compiling:
         return torch.ops.mail_b200.fused_experts(x, w13, w2, group_sizes_or_topk_weights, topk_ids, s13, s2)
     return _topk_impl(x, w13, w2, group_sizes_or_topk_weights, topk_ids, s13, s2)
+
+
+def fused_moe_mlp_from_logits(x: torch.Tensor, w13: torch.Tensor, w2: torch.Tensor, router_logits: torch.Tensor,
+                              top_k: int, scoring: str = "softmax", renormalize: bool = True, scales=None):
+    """Routing and the top-k form of fused_moe_mlp in one call: router_logits
+    [T, E] (fp32/bf16/fp16) are routed as route_topk routes them (the k
+    largest logits, ties to the lower expert id, softmax or sigmoid weights,
+    optionally renormalised over the k), then the layer runs on that routing.
+    Returns (y [T, H] in x.dtype, topk_weights fp32 [T, k], topk_ids int32
+    [T, k]). A decode-sized batch (at most 16 tokens, E <= 256, bf16/fp16)
+    routes inside the one-launch decode kernel: the whole layer is one launch.
+    """
+    _require_cuda(x, w13, w2, router_logits)
+    T, H, E, inter = _check_shapes(x, w13, w2)
+    lg = router_logits.contiguous()
+    if lg.dim() != 2 or tuple(lg.shape) != (T, E):
+        raise ValueError(f"fused_moe_mlp_from_logits: router_logits must be [T, E] = [{T}, {E}]")
+    x = x.contiguous()
+    w13k, w2k = kmajor(w13), kmajor(w2)
+    dev = x.device
+    s13, s2 = scales if scales is not None else (None, None)
+    w_code, s13, s2 = _weight_scales(x, w13, w2, s13, s2, E, H, inter)
+    y = torch.empty((T, H), dtype=x.dtype, device=dev)
+    ids = torch.empty((T, top_k), dtype=torch.int32, device=dev)
+    wts = torch.empty((T, top_k), dtype=torch.float32, device=dev)
+    sc = {"softmax": 0, "sigmoid": 1}[scoring]
+    ws = _workspace(_lib.query("moe_fused_experts_workspace_size", T, H, inter, E, top_k, _code(x), w_code), dev)
+    _lib.call("moe_fused_experts_from_logits", x.data_ptr(), _code(x), T, H, w13k.data_ptr(), w2k.data_ptr(), w_code,
+              E, inter, lg.data_ptr(), _code(lg), top_k, sc, int(renormalize), ids.data_ptr(), wts.data_ptr(),
+              _ptr(s13), _ptr(s2), y.data_ptr(), ws.data_ptr(), ws.numel(), _stream(dev))
+    return y, wts, ids
 
 
 def fused_expert_rows(x: torch.Tensor, w13: torch.Tensor, w2: torch.Tensor, expert_ids: torch.Tensor,

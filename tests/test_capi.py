@@ -55,6 +55,15 @@ def test_version_and_pure_host_queries():
      "dtype"),
     (lambda L: L.moe_fused_experts(None, _lib.BF16, 4, 64, None, None, _lib.F16, 2, 64, None, None, 2, None, None,
                                    None, None, 0, None), "int8"),
+    (lambda L: L.moe_fused_experts_from_logits(None, _lib.BF16, 4, 64, None, None, _lib.BF16, 8, 64, None, _lib.I8, 2,
+                                               0, 1, None, None, None, None, ctypes.c_void_p(16), None, 0, None),
+     "logits dtype"),
+    (lambda L: L.moe_fused_experts_from_logits(None, _lib.BF16, 4, 64, None, None, _lib.BF16, 8, 64, None, _lib.F32,
+                                               2, 5, 1, None, None, None, None, ctypes.c_void_p(16), None, 0, None),
+     "bad scoring"),
+    (lambda L: L.moe_fused_experts_from_logits(None, _lib.BF16, 4, 64, None, None, _lib.BF16, 8, 64, None, _lib.F32,
+                                               2, 0, 1, None, None, None, None, ctypes.c_void_p(16), None, 0, None),
+     "NULL pointer"),
 ])
 def test_invalid_arguments_are_rejected_on_host(call, needle):
     lib = _lib.load()
