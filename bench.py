@@ -663,6 +663,60 @@ def run_config(ctx, name, T, args, peaks, int8, weights=None, steps=None, warmup
     return out, keep
 
 
+def decode_from_logits(ctx, weights, T, ids_ms):
+    """The Qwen3 decode step called with the router logits
+    (fused_moe_mlp_from_logits: routing is phase 0 of the one-launch kernel).
+    Each step's logits rank its seeded routing's k experts first, so the
+    experts, rows and weight bytes equal the ids-given step's (ids_ms), and
+    steps chain in one graph the same way."""
+    import mail_b200 as mb
+
+    torch = ctx.torch
+    cfg = dict(CONFIGS["qwen3-decode"])
+    cfg["T"] = T
+    E, k = cfg["E"], cfg["k"]
+    w13, w2, _ = weights
+    n_var, _ = n_variants(cfg, T, 1, ctx.rank)
+    variants = []
+    for v in range(n_var):
+        x, ids, _, _ = make_inputs(cfg, ctx.rank, ctx.device, v)
+        lg = torch.randn(T, E, device=ctx.device) - 20.0
+        lg.scatter_(1, ids.long(), (10.0 - torch.arange(k, device=ctx.device, dtype=torch.float32)).expand(T, k))
+        variants.append((x, lg, ids))
+    for x, lg, ids in variants:  # warm-up, and the routing is the seeded one
+        _, _, got = mb.fused_moe_mlp_from_logits(x, w13, w2, lg, k)
+        assert torch.equal(got, ids), "decode_from_logits: logits do not reproduce the routing"
+    G = n_var * -(-8 // n_var)
+    steps = G * -(-200 // G)
+
+    def chained(fused):
+        chain = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(chain):
+            for j in range(G):
+                x, lg, _ = variants[j % n_var]
+                if fused:
+                    mb.fused_moe_mlp_from_logits(x, w13, w2, lg, k)
+                else:  # the router's own launch, then the layer
+                    ids, wts = mb.route_topk(lg, k)
+                    mb.fused_moe_mlp(x, w13, w2, wts, ids)
+        w = dict(chain=chain, chain_steps=G)
+        run_steps(w, 3 * G)
+        torch.cuda.synchronize()
+        r = timed_region(ctx, w, steps, kernels_per_step=1 if fused else 2)
+        del w, chain
+        return r
+
+    r = chained(True)
+    r2 = chained(False)
+    out = {"workload": f"Qwen3-30B-A3B decode T={T}, router logits in (routing fused into the one-launch kernel)",
+           "value": T / (r["ms"] / 1e3), "unit": "tokens/s", "ms_per_step": r["ms"], "steps": steps,
+           "launches_per_step": 1, "router_then_layer_ms_per_step": r2["ms"], "ids_given_ms_per_step": ids_ms,
+           "clocks": r["clocks"], "graph_steps": G}
+    del variants
+    torch.cuda.synchronize()
+    return out
+
+
 def sub_configs(ctx, args, peaks, int8):
     """The workloads beside the headline, at their own shapes."""
     res = {}
@@ -677,6 +731,9 @@ def sub_configs(ctx, args, peaks, int8):
                 weights = make_weights(cfg, list(range(cfg["E"])), ctx.device, dt)
             res[f"qwen3-decode-T{T}"], _ = run_config(ctx, "qwen3-decode", T, args, peaks, int8, weights=weights,
                                                       steps=steps)
+        for T in (1, 8):
+            res[f"qwen3-decode-T{T}-from-logits"] = decode_from_logits(ctx, weights, T,
+                                                                       res[f"qwen3-decode-T{T}"]["ms_per_step"])
         del weights
         ctx.torch.cuda.empty_cache()
         res["dsv3-w8a8"], _ = run_config(ctx, "dsv3-w8a8", 8192, args, peaks, int8)

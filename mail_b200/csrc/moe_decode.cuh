@@ -55,6 +55,8 @@
 // out latches device error 7, and moe_get_device_error() resets the launch
 // counter after any error. Two such launches must not overlap on one GPU
 // (different streams).
+#include <type_traits>
+
 #include "route.cuh"
 
 namespace moe {
@@ -294,25 +296,55 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       s_ids[s] = -1;
       s_w[s] = 0.f;
     }
-    for (int t = warp; t < p.T; t += NUM_THREADS / 32) {
-      int id;
-      float wt;
-      const size_t off = (size_t)t * p.E;
+    // warp w routes tokens w, w + 6, w + 12 (those below T): all its logit
+    // rows are loaded before the selection, so their loads overlap, and its
+    // tokens are selected together (interleaved reduction chains)
+    constexpr int kWarps = NUM_THREADS / 32;
+    constexpr int kRounds = (kDecodeMaxTokens + kWarps - 1) / kWarps;
+    const int nt = warp < p.T ? (p.T - 1 - warp) / kWarps + 1 : 0;
+    float lv[kRounds][8];
+#pragma unroll
+    for (int r = 0; r < kRounds; ++r) {
+      if (r >= nt) break;
+      const size_t off = (size_t)(warp + kWarps * r) * p.E;
       if (p.logits_dtype == MOE_F32)
-        route_token<float, 8>(static_cast<const float*>(p.logits) + off, p.E, p.k, p.sigmoid, p.renormalize, lane,
-                              id, wt);
+        route_load<float, 8>(static_cast<const float*>(p.logits) + off, p.E, lane, lv[r]);
       else if (p.logits_dtype == MOE_BF16)
-        route_token<__nv_bfloat16, 8>(static_cast<const __nv_bfloat16*>(p.logits) + off, p.E, p.k, p.sigmoid,
-                                      p.renormalize, lane, id, wt);
+        route_load<__nv_bfloat16, 8>(static_cast<const __nv_bfloat16*>(p.logits) + off, p.E, lane, lv[r]);
       else
-        route_token<__half, 8>(static_cast<const __half*>(p.logits) + off, p.E, p.k, p.sigmoid, p.renormalize, lane,
-                               id, wt);
-      if (lane < p.k) {
-        s_ids[t * p.k + lane] = id;
-        s_w[t * p.k + lane] = wt;
+        route_load<__half, 8>(static_cast<const __half*>(p.logits) + off, p.E, lane, lv[r]);
+    }
+    int rid[kRounds];
+    float rw[kRounds];
+    auto select = [&](auto n_tag) {
+      constexpr int N = decltype(n_tag)::value;
+      float v[N][8];
+      int id[N];
+      float wt[N];
+#pragma unroll
+      for (int r = 0; r < N; ++r)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[r][i] = lv[r][i];
+      route_select<N, 8>(v, p.E, p.k, p.sigmoid, p.renormalize, lane, id, wt);
+#pragma unroll
+      for (int r = 0; r < N; ++r) {
+        rid[r] = id[r];
+        rw[r] = wt[r];
+      }
+    };
+    static_assert(kRounds == 3, "phase-0 routing selects 1 to 3 tokens per warp");
+    if (nt == 1) select(std::integral_constant<int, 1>{});
+    else if (nt == 2) select(std::integral_constant<int, 2>{});
+    else if (nt == 3) select(std::integral_constant<int, 3>{});
+#pragma unroll
+    for (int r = 0; r < kRounds; ++r) {
+      const int t = warp + kWarps * r;
+      if (r < nt && lane < p.k) {
+        s_ids[t * p.k + lane] = rid[r];
+        s_w[t * p.k + lane] = rw[r];
         if (blockIdx.x == 0) {
-          p.ids_out[t * p.k + lane] = id;
-          p.wts_out[t * p.k + lane] = wt;
+          p.ids_out[t * p.k + lane] = rid[r];
+          p.wts_out[t * p.k + lane] = rw[r];
         }
       }
     }
