@@ -310,7 +310,7 @@ def _topk_impl(x, w13, w2, topk_weights, topk_ids, w13_scale, w2_scale):
     return y
 
 
-# The two forms as PyTorch operators (torch.ops.mail_b200.*), so a
+# The two forms (and the logits-in call below) as PyTorch operators (torch.ops.mail_b200.*), so a
 # torch.compile'd MoE layer sees one opaque op per call instead of a graph
 # break; the fake (meta) kernels give the output shape and dtype for tracing.
 @torch.library.custom_op("mail_b200::fused_moe_mlp", mutates_args=())
@@ -377,26 +377,26 @@ def fused_moe_mlp(x: torch.Tensor, w13: torch.Tensor, w2: torch.Tensor, group_si
     return _topk_impl(x, w13, w2, group_sizes_or_topk_weights, topk_ids, s13, s2)
 
 
-def fused_moe_mlp_from_logits(x: torch.Tensor, w13: torch.Tensor, w2: torch.Tensor, router_logits: torch.Tensor,
-                              top_k: int, scoring: str = "softmax", renormalize: bool = True, scales=None):
-    """Routing and the top-k form of fused_moe_mlp in one call: router_logits
-    [T, E] (fp32/bf16/fp16) are routed as route_topk routes them (the k
-    largest logits, ties to the lower expert id, softmax or sigmoid weights,
-    optionally renormalised over the k), then the layer runs on that routing.
-    Returns (y [T, H] in x.dtype, topk_weights fp32 [T, k], topk_ids int32
-    [T, k]). A decode-sized batch (at most 16 tokens, E <= 256, bf16/fp16)
-    routes inside the one-launch decode kernel: the whole layer is one launch.
-    """
-    _require_cuda(x, w13, w2, router_logits)
+def _check_logits(x, w13, w2, router_logits, top_k, scoring):
     T, H, E, inter = _check_shapes(x, w13, w2)
-    lg = router_logits.contiguous()
-    if lg.dim() != 2 or tuple(lg.shape) != (T, E):
+    if router_logits.dim() != 2 or tuple(router_logits.shape) != (T, E):
         raise ValueError(f"fused_moe_mlp_from_logits: router_logits must be [T, E] = [{T}, {E}]")
+    if not 1 <= top_k <= min(E, 32):
+        raise ValueError(f"fused_moe_mlp_from_logits: top_k {top_k} outside [1, min(E, 32)]")
+    if scoring not in ("softmax", "sigmoid"):
+        raise ValueError(f"fused_moe_mlp_from_logits: scoring must be softmax or sigmoid, not {scoring!r}")
+    return T, H, E, inter
+
+
+def _from_logits_impl(x, w13, w2, router_logits, top_k, scoring, renormalize, w13_scale, w2_scale):
+    """moe_fused_experts_from_logits: router -> align -> GEMMs -> combine."""
+    _require_cuda(x, w13, w2, router_logits)
+    T, H, E, inter = _check_logits(x, w13, w2, router_logits, top_k, scoring)
+    lg = router_logits.contiguous()
     x = x.contiguous()
     w13k, w2k = kmajor(w13), kmajor(w2)
     dev = x.device
-    s13, s2 = scales if scales is not None else (None, None)
-    w_code, s13, s2 = _weight_scales(x, w13, w2, s13, s2, E, H, inter)
+    w_code, s13, s2 = _weight_scales(x, w13, w2, w13_scale, w2_scale, E, H, inter)
     y = torch.empty((T, H), dtype=x.dtype, device=dev)
     ids = torch.empty((T, top_k), dtype=torch.int32, device=dev)
     wts = torch.empty((T, top_k), dtype=torch.float32, device=dev)
@@ -406,6 +406,39 @@ def fused_moe_mlp_from_logits(x: torch.Tensor, w13: torch.Tensor, w2: torch.Tens
               E, inter, lg.data_ptr(), _code(lg), top_k, sc, int(renormalize), ids.data_ptr(), wts.data_ptr(),
               _ptr(s13), _ptr(s2), y.data_ptr(), ws.data_ptr(), ws.numel(), _stream(dev))
     return y, wts, ids
+
+
+@torch.library.custom_op("mail_b200::fused_experts_from_logits", mutates_args=())
+def _op_from_logits(x: torch.Tensor, w13: torch.Tensor, w2: torch.Tensor, router_logits: torch.Tensor, top_k: int,
+                    scoring: str, renormalize: bool, w13_scale: torch.Tensor | None,
+                    w2_scale: torch.Tensor | None) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    return _from_logits_impl(x, w13, w2, router_logits, top_k, scoring, renormalize, w13_scale, w2_scale)
+
+
+@_op_from_logits.register_fake
+def _(x, w13, w2, router_logits, top_k, scoring, renormalize, w13_scale, w2_scale):
+    T, H, _, _ = _check_logits(x, w13, w2, router_logits, top_k, scoring)
+    return (x.new_empty((T, H)), x.new_empty((T, top_k), dtype=torch.float32),
+            x.new_empty((T, top_k), dtype=torch.int32))
+
+
+def fused_moe_mlp_from_logits(x: torch.Tensor, w13: torch.Tensor, w2: torch.Tensor, router_logits: torch.Tensor,
+                              top_k: int, scoring: str = "softmax", renormalize: bool = True, scales=None):
+    """Routing and the top-k form of fused_moe_mlp in one call: router_logits
+    [T, E] (fp32/bf16/fp16) are routed as route_topk routes them (the k
+    largest logits, ties to the lower expert id, softmax or sigmoid weights,
+    optionally renormalised over the k), then the layer runs on that routing.
+    Returns (y [T, H] in x.dtype, topk_weights fp32 [T, k], topk_ids int32
+    [T, k]). A decode-sized batch (at most 16 tokens, E <= 256, bf16/fp16)
+    routes inside the one-launch decode kernel: the whole layer is one launch.
+    Under torch.compile the call is one operator
+    (torch.ops.mail_b200.fused_experts_from_logits).
+    """
+    s13, s2 = scales if scales is not None else (None, None)
+    if torch.compiler.is_compiling():
+        return torch.ops.mail_b200.fused_experts_from_logits(x, w13, w2, router_logits, top_k, scoring, renormalize,
+                                                             s13, s2)
+    return _from_logits_impl(x, w13, w2, router_logits, top_k, scoring, renormalize, s13, s2)
 
 
 def fused_expert_rows(x: torch.Tensor, w13: torch.Tensor, w2: torch.Tensor, expert_ids: torch.Tensor,

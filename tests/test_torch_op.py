@@ -30,6 +30,27 @@ def test_schemas():
         "Tensor? w13_scale, Tensor? w2_scale) -> Tensor")
 
 
+def test_from_logits_schema_and_fake_kernel():
+    """The logits-in call: routing outputs beside y, shapes from the fake
+    kernel; a bad top_k or scoring fails while tracing."""
+    assert str(torch.ops.mail_b200.fused_experts_from_logits.default._schema) == (
+        "mail_b200::fused_experts_from_logits(Tensor x, Tensor w13, Tensor w2, Tensor router_logits, SymInt top_k, "
+        "str scoring, bool renormalize, Tensor? w13_scale, Tensor? w2_scale) -> (Tensor, Tensor, Tensor)")
+    with FakeTensorMode():
+        x, w13, w2, _, _, _, _ = fake_inputs(T=5, E=16)
+        lg = torch.empty(5, 16, device="cuda")
+        y, w, ids = torch.ops.mail_b200.fused_experts_from_logits(x, w13, w2, lg, 8, "sigmoid", True, None, None)
+        assert y.shape == (5, 128) and y.dtype == torch.bfloat16
+        assert w.shape == (5, 8) and w.dtype == torch.float32
+        assert ids.shape == (5, 8) and ids.dtype == torch.int32
+        with pytest.raises(ValueError):
+            torch.ops.mail_b200.fused_experts_from_logits(x, w13, w2, lg, 17, "softmax", True, None, None)
+        with pytest.raises(ValueError):
+            torch.ops.mail_b200.fused_experts_from_logits(x, w13, w2, lg, 2, "relu", True, None, None)
+        with pytest.raises(ValueError):
+            torch.ops.mail_b200.fused_experts_from_logits(x, w13, w2, lg[:, :8], 2, "softmax", True, None, None)
+
+
 @pytest.mark.parametrize("quant", [False, True])
 def test_fake_kernels_give_output_shape_and_dtype(quant):
     with FakeTensorMode():
@@ -101,3 +122,28 @@ def test_torch_compile_prerouted_form():
     torch._dynamo.reset()
     got = torch.compile(lambda a: mb.fused_moe_mlp(a, w13, w2, gs), fullgraph=True)(x)
     assert torch.equal(got, ref)  # the pre-routed form has no atomics: bit-identical
+
+
+@pytest.mark.gpu
+def test_torch_compile_from_logits():
+    """The logits-in call under torch.compile(fullgraph=True): one operator,
+    the same routing and output as the eager call (decode-sized: the routing
+    runs inside the one-launch kernel)."""
+    torch.manual_seed(2)
+    T, H, I, E, k = 4, 256, 128, 16, 4
+    x = torch.randn(T, H, device="cuda").to(torch.bfloat16)
+    w13 = (torch.randn(E, 2 * I, H, device="cuda") * 0.02).to(torch.bfloat16).transpose(1, 2)
+    w2 = (torch.randn(E, H, I, device="cuda") * 0.02).to(torch.bfloat16).transpose(1, 2)
+    lg = torch.randn(T, E, device="cuda")
+
+    def layer(x, lg):
+        y, _, ids = mb.fused_moe_mlp_from_logits(x, w13, w2, lg, k)
+        return y + x, ids
+
+    ref_y, ref_ids = layer(x, lg)
+    torch._dynamo.reset()
+    got_y, got_ids = torch.compile(layer, fullgraph=True)(x, lg)
+    assert torch.equal(got_ids, ref_ids)
+    ref = ref_y.float()
+    assert float((got_y.float() - ref).abs().max() / ref.abs().max()) < 1e-2
+    assert mb.device_error() == 0
