@@ -719,6 +719,47 @@ def decode_from_logits(ctx, weights, T, ids_ms):
     return out
 
 
+def router_timing(ctx, peaks):
+    """The GPU router (route_topk) on the routing inputs of the DeepSeek-V3
+    (8192 x 256 fp32 logits, sigmoid top-8) and stress (65536 x 64, softmax
+    top-6) workloads: CUDA events around one replay of a graph of 20
+    launches; algorithmic bytes = logits read + ids and weights written."""
+    import mail_b200 as mb
+
+    torch = ctx.torch
+    out = {}
+    for name, T, E, k, scoring in (("dsv3", 8192, 256, 8, "sigmoid"), ("stress", 65536, 64, 6, "softmax")):
+        # enough logits buffers, cycled, to exceed twice the L2: every launch
+        # reads its logits from HBM
+        nb = int(math.ceil(2 * L2_BYTES / (T * E * 4)))
+        lgs = [torch.randn(T, E, device=ctx.device) for _ in range(nb)]
+        for i in range(3):
+            mb.route_topk(lgs[i % nb], k, scoring=scoring)
+        torch.cuda.synchronize()
+        # one graph of 20 launches (one per buffer in turn), so the host's
+        # per-call cost is not what is timed
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for i in range(20):
+                mb.route_topk(lgs[(3 + i) % nb], k, scoring=scoring)
+        g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(ctx.stream)
+        g.replay()
+        e1.record(ctx.stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / 20
+        del g
+        nbytes = T * E * 4 + T * k * 8
+        gbs = nbytes / (ms / 1e3) / 1e9
+        out[name] = {"tokens": T, "experts": E, "top_k": k, "scoring": scoring, "us_per_launch": ms * 1e3,
+                     "bytes": nbytes, "achieved_gbs": gbs, "frac_hbm": gbs / peaks["hbm"],
+                     "l2": f"{nb} logits buffers cycled ({nb * T * E * 4 / 1e6:.0f} MB, over twice the L2)"}
+        del lgs
+    return out
+
+
 def sub_configs(ctx, args, peaks, int8):
     """The workloads beside the headline, at their own shapes."""
     res = {}
@@ -740,6 +781,7 @@ def sub_configs(ctx, args, peaks, int8):
         ctx.torch.cuda.empty_cache()
         res["dsv3-w8a8"], _ = run_config(ctx, "dsv3-w8a8", 8192, args, peaks, int8)
         res["stress-w8a8"], _ = run_config(ctx, "stress-w8a8", 65536, args, peaks, int8, steps=max(5, args.steps // 2))
+        res["router"] = router_timing(ctx, peaks)
     else:
         res["dsv3-w8a8"], _ = run_config(ctx, "dsv3-w8a8", 8192, args, peaks, int8, ep_kind=args.ep)
         res["dsv3-w8a8"]["scaling"] = "weak"

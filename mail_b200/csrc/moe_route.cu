@@ -330,10 +330,12 @@ __global__ void __launch_bounds__(kScanThreads) align_small_kernel(
 
 // ---------------------------------------------------------------------------
 // Router: logits [T, E] -> top-k ids and weights, one warp per token
-// (route_token in route.cuh: ties to the lower expert id).
+// (route.cuh: ties to the lower expert id). When the tokens outnumber the
+// warps that fit on the GPU at once, each warp takes R consecutive tokens
+// at a time: their rows are loaded together and their selections interleave.
 constexpr int kRouteMaxPerLane = 32;  // E <= 1024
 
-template <typename T, int PER>
+template <typename T, int PER, int R>
 __global__ void __launch_bounds__(256) route_topk_kernel(const T* __restrict__ logits, int64_t num_tokens, int E,
                                                          int k, int sigmoid, int renormalize,
                                                          int32_t* __restrict__ ids, float* __restrict__ wts) {
@@ -341,13 +343,23 @@ __global__ void __launch_bounds__(256) route_topk_kernel(const T* __restrict__ l
   const int lane = threadIdx.x & 31;
   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
-  for (int64_t t = warp; t < num_tokens; t += nwarps) {
-    int id;
-    float w;
-    route_token<T, PER>(logits + t * E, E, k, sigmoid, renormalize, lane, id, w);
-    if (lane < k) {
-      ids[t * k + lane] = id;
-      wts[t * k + lane] = w;
+  for (int64_t t0 = warp * R; t0 < num_tokens; t0 += nwarps * R) {
+    float v[R][PER];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const int64_t t = min(t0 + r, num_tokens - 1);  // a row past the end repeats the last one, not stored
+      route_load<T, PER>(logits + t * E, E, lane, v[r]);
+    }
+    int id[R];
+    float w[R];
+    route_select<R, PER>(v, E, k, sigmoid, renormalize, lane, id, w);
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const int64_t t = t0 + r;
+      if (t < num_tokens && lane < k) {
+        ids[t * k + lane] = id[r];
+        wts[t * k + lane] = w[r];
+      }
     }
   }
 }
@@ -367,20 +379,36 @@ extern "C" int moe_route_topk(const void* logits, int dtype, int64_t num_tokens,
                 scoring);
   if (num_tokens == 0) return MOE_OK;
   MOE_CHECK_ARG(logits && topk_ids && topk_weights, "moe_route_topk: NULL pointer");
-  int64_t blocks = ceil_div(num_tokens, 8);
-  const int64_t cap = (int64_t)num_sms() * 16;
+  // one token per warp while every warp fits on the GPU at once (eight
+  // 256-thread blocks per SM); above that four tokens per warp at a time
+  // (E <= 256: their logits stay in registers)
+  const int64_t resident_warps = (int64_t)num_sms() * 64;
+  const int R = (num_tokens > resident_warps && num_experts <= 256) ? 4 : 1;
+  int64_t blocks = ceil_div(ceil_div(num_tokens, (int64_t)R), (int64_t)8);
+  const int64_t cap = (int64_t)num_sms() * 8;
   if (blocks > cap) blocks = cap;
   cudaStream_t st = as_stream(stream);
   const int sig = scoring == MOE_SCORE_SIGMOID;
-#define ROUTE(TT, PER)                                                                             \
-  MOE_CUDA_TRY(launch_kernel(route_topk_kernel<TT, PER>, dim3((unsigned)blocks), dim3(256), 0, st, \
-                             static_cast<const TT*>(logits), num_tokens, num_experts, top_k, sig,  \
+#define ROUTE(TT, PER, RR)                                                                              \
+  MOE_CUDA_TRY(launch_kernel(route_topk_kernel<TT, PER, RR>, dim3((unsigned)blocks), dim3(256), 0, st, \
+                             static_cast<const TT*>(logits), num_tokens, num_experts, top_k, sig,       \
                              renormalize != 0, topk_ids, topk_weights))
-#define ROUTE_T(TT)                          \
-  if (num_experts <= 32) ROUTE(TT, 1);       \
-  else if (num_experts <= 128) ROUTE(TT, 4); \
-  else if (num_experts <= 256) ROUTE(TT, 8); \
-  else ROUTE(TT, kRouteMaxPerLane);
+#define ROUTE_T(TT)                                  \
+  if (num_experts <= 32) {                           \
+    if (R == 4) ROUTE(TT, 1, 4);                     \
+    else ROUTE(TT, 1, 1);                            \
+  } else if (num_experts <= 64) {                    \
+    if (R == 4) ROUTE(TT, 2, 4);                     \
+    else ROUTE(TT, 2, 1);                            \
+  } else if (num_experts <= 128) {                   \
+    if (R == 4) ROUTE(TT, 4, 4);                     \
+    else ROUTE(TT, 4, 1);                            \
+  } else if (num_experts <= 256) {                   \
+    if (R == 4) ROUTE(TT, 8, 4);                     \
+    else ROUTE(TT, 8, 1);                            \
+  } else {                                           \
+    ROUTE(TT, kRouteMaxPerLane, 1);                  \
+  }
   if (dtype == MOE_F32) {
     ROUTE_T(float)
   } else if (dtype == MOE_BF16) {

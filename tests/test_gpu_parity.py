@@ -129,12 +129,18 @@ def test_align_bit_exact(kind, T, k, E):
     (64, 8, 2, "softmax", True, torch.float32), (4096, 8, 2, "softmax", True, torch.bfloat16),
     (777, 128, 8, "softmax", False, torch.float32), (300, 256, 8, "sigmoid", True, torch.float32),
     (5, 64, 6, "sigmoid", False, torch.float16), (33, 1000, 4, "softmax", True, torch.float32),
+    # more tokens than warps resident at once: four tokens per warp (E <= 256), odd T; one per warp above
+    (20000, 64, 6, "softmax", True, torch.float32), (30001, 256, 8, "sigmoid", True, torch.bfloat16),
+    (12000, 1000, 4, "softmax", False, torch.float32),
 ])
 def test_route_topk_matches_oracle(T, E, k, scoring, renorm, dtype):
     rng = np.random.default_rng(E + k)
     lg = rng.standard_normal((T, E), dtype=np.float32)
     lg[0, :] = 0.25          # all tied: lowest ids win
     lg[1, 3] = lg[1, 5] = 9  # a tie at the top
+    if T > 2 and E > 6:      # -0 and +0 compare equal: a tie, the lower id first
+        lg[2, :] = -1.0
+        lg[2, 6], lg[2, 2] = -0.0, 0.0
     lt = torch.from_numpy(lg).to(dev(), dtype)
     ids, w = mb.route_topk(lt, k, scoring, renorm)
     ids_ref, w_ref = O.route_topk(npf(lt), k, scoring, renorm)
