@@ -125,7 +125,8 @@ typedef enum {
                                GEMMs included, without K splits). 0: never */,
   MOE_OPT_GEMM_BAND_DOWN = 8, /* the down GEMM's band of M tiles (MOE_OPT_GEMM_BAND); 0 (default): the same
                                band as the gate_up GEMM */
-  MOE_OPT_DECODE_FUSED = 9    /* 1 (default): moe_fused_experts runs a batch of at most 16 tokens and 128 routed
+  MOE_OPT_DECODE_FUSED = 9    /* 1 (default): moe_fused_experts (and moe_fused_experts_from_logits, with its
+                               router, up to 256 experts) runs a batch of at most 16 tokens and 128 routed
                                slots (bf16/fp16, no int8) as one persistent kernel — routing, gate_up GEMM +
                                SwiGLU, down GEMM + combine and output conversion as phases whose CTAs
                                hand results on through counters. Its launch counter lives in the library's
